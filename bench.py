@@ -1,0 +1,334 @@
+"""Benchmark of the B200 beam-search decode path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload decode-attention|rollout]
+
+Workloads (seeded synthetic inputs; the reference's hwb6 circuit, rule set
+and checkpoint are not available):
+
+* ``decode-attention``: the shared-prefix paged decode microbenchmark -
+  512 beams, one query token each, 8 heads x 32, bf16, 381 shared s0 node
+  keys, 64 action K/V entries per beam in pages of 16, block tables from a
+  random prefix tree.  A step is one decode-attention launch over all beams.
+
+Timing: W untimed warm-up steps, then K timed steps; before every timed step
+a 256 MiB buffer is written to flush L2; each step is bracketed by CUDA events
+on the launching stream, with barrier + synchronize around the timed region
+and the max over ranks.  ``e2e`` repeats the step through the public Python
+API with the per-step inputs copied from pinned host memory and the result
+copied back, inside the timed region.  Clocks are sampled with nvidia-smi
+during the timed region.  ``--impl reference`` times the CPU oracle (the
+reference's algorithm restated on the host) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from pathlib import Path
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "beam-state decode steps/s at B=1000,T=64; paged-attn HBM GB/s vs peak"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "bf16_tflops": data["bf16_tflops"],
+                "bf16_tflops_sustained": data.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def profiled_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    return json.loads(path.read_text()).get(kernel)
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, flag in zip(names, r[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": num(rows[0][2]), "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world: int, device):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# decode-attention workload
+# ---------------------------------------------------------------------------
+def run_decode_attention(args, world, rank, device):
+    from graph_rewrite_system_b200.paged_attention import paged_attention
+    from graph_rewrite_system_b200.workloads import decode_attention_workload
+
+    w = decode_attention_workload(device, seed=rank)
+    out = torch.empty_like(w.query)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        paged_attention(w.query, w.key_cache, w.value_cache, w.block_table, w.lengths,
+                        shared_key=w.shared_key, shared_value=w.shared_value, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world, device)
+    torch.cuda.synchronize(device)
+    with ClockSampler(device.index) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world, device)
+    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    kernel_ms = max_over_ranks(kernel_ms, world, device)
+
+    # end to end through the public API with host buffers
+    q_host = w.query.cpu().pin_memory()
+    bt_host = w.block_table.cpu().pin_memory()
+    len_host = w.lengths.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    q_dev, bt_dev, len_dev = torch.empty_like(w.query), torch.empty_like(w.block_table), \
+        torch.empty_like(w.lengths)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        bt_dev.copy_(bt_host, non_blocking=True)
+        len_dev.copy_(len_host, non_blocking=True)
+        paged_attention(q_dev, w.key_cache, w.value_cache, bt_dev, len_dev,
+                        shared_key=w.shared_key, shared_value=w.shared_value, out=out)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e2e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e2e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world, device)
+    for i in range(args.steps):
+        flush.zero_()
+        e2e_starts[i].record(stream)
+        e2e_step()
+        e2e_ends[i].record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e2e_starts, e2e_ends)) / args.steps
+    e2e_ms = max_over_ranks(e2e_ms, world, device)
+    h2d = q_host.numel() * q_host.element_size() + bt_host.numel() * 4 + len_host.numel() * 4
+    d2h = out_host.numel() * out_host.element_size()
+
+    peaks = measured_peaks()
+    achieved = w.unique_bytes / (kernel_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": world * 1e3 / kernel_ms, "unit": "steps/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": kernel_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "decode-attention: B=512 beams x 1 query, 8 heads x 32, "
+                               "381 shared s0 keys + 64 paged action K/V (page 16), "
+                               "prefix-tree block tables (branching 4)",
+                   "beams": 512, "tokens": 64, "page_size": 16, "shared_keys": 381,
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "parallelism": f"replicas x{world}"},
+        "e2e": {"value": world * 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "traffic": profiled_traffic("decode_attention"),
+                     "algorithmic_bytes": w.unique_bytes,
+                     "peak_source": f"{peaks['source']} hbm_gbs",
+                     "kernel": "paged_attention_rows_kernel"},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_attention(w, device)
+    return line
+
+
+def cpu_decode_attention(w, device, *, sample_beams=64, repeats=None, budget_s=12.0):
+    """The oracle (CPU restatement of the reference) on a bounded sample."""
+    from oracle import paged_attention as oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cache_k = w.key_cache.float().cpu()
+    cache_v = w.value_cache.float().cpu()
+    sk, sv = w.shared_key.float().cpu(), w.shared_value.float().cpu()
+    q = w.query[:sample_beams].float().cpu()
+    bt = w.block_table[:sample_beams].cpu()
+    ln = w.lengths[:sample_beams].cpu()
+    started = time.perf_counter()
+    runs = 0
+    while True:
+        oracle.paged_attention(q, cache_k, cache_v, bt, ln, shared_key=sk, shared_value=sv)
+        runs += 1
+        elapsed = time.perf_counter() - started
+        if (repeats and runs >= repeats) or (not repeats and elapsed > budget_s):
+            break
+    per_sample = elapsed / runs
+    scale = w.query.shape[0] / sample_beams
+    return {"value": 1.0 / (per_sample * scale), "unit": "steps/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample_beams} of {w.query.shape[0]} beams, {runs} runs, "
+                      f"scaled linearly to the full step"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the CPU oracle on the same workload (rank 0 only)."""
+    if rank != 0:
+        return None
+    device = torch.device("cpu")
+    from graph_rewrite_system_b200.workloads import decode_attention_workload
+
+    w = decode_attention_workload(device, seed=0, dtype=torch.float32)
+    for _ in range(args.warmup):
+        cpu_decode_attention(w, device, repeats=1)
+    t0 = time.perf_counter()
+    per = []
+    for _ in range(args.steps):
+        per.append(cpu_decode_attention(w, device, repeats=1)["value"])
+    value = statistics.mean(per)
+    base = cpu_decode_attention(w, device, repeats=1)
+    return {
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "steps/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "decode-attention (CPU oracle, 64-beam sample scaled)"},
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": base["cores"],
+                         "kind": "port", "sample": base["sample"]},
+        "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "wall_seconds": time.perf_counter() - t0,
+    }
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--workload", choices=("decode-attention",), default="decode-attention")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    line = run_decode_attention(args, world, rank, device)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,85 @@
+"""Paged attention with the reference's Python API (paged_attention.py:217-306).
+
+``paged_attention(query, key_cache, value_cache, block_table, lengths, *,
+current_key=None, current_value=None, current_valid=None)`` attends each
+(beam, head, query) row to the first ``lengths[b]`` tokens of the beam's
+block-table pages plus, when given, the current token at position
+``lengths[b]`` (``current_valid[b]``).  Rows with no valid key are zero.
+The sm_100a kernels live in ``csrc/paged_attention.cu``; CPU tensors raise.
+
+``shared_key``/``shared_value`` ([N, H, D], beam-invariant) extend the
+reference API for the shared-prefix decode microbenchmark.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def paged_attention(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    lengths: torch.Tensor,
+    *,
+    current_key: torch.Tensor | None = None,
+    current_value: torch.Tensor | None = None,
+    current_valid: torch.Tensor | None = None,
+    shared_key: torch.Tensor | None = None,
+    shared_value: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    has_current = current_key is not None
+    if has_current != (current_value is not None and current_valid is not None):
+        raise ValueError("current key/value/valid must be supplied together")
+    if (shared_key is None) != (shared_value is None):
+        raise ValueError("shared key/value must be supplied together")
+    _lib.require_cuda(query, key_cache, value_cache, block_table, lengths,
+                      current_key, current_value, current_valid, shared_key, shared_value)
+    if query.dtype not in _lib.DTYPE_CODES or key_cache.dtype != query.dtype:
+        raise ValueError("paged_attention supports bf16 or fp32 query and cache of one dtype")
+    batch, heads, query_length, head_width = query.shape
+    if key_cache.shape[2:] != (heads, head_width) or value_cache.shape != key_cache.shape:
+        raise ValueError("cache must be [pages, page, heads, head_width]")
+    if key_cache.stride() != value_cache.stride() or key_cache.stride(3) != 1:
+        raise ValueError("key/value caches must share a layout with contiguous head_width")
+    if query.stride(3) != 1:
+        query = query.contiguous()
+    block_table = block_table.to(torch.int32)
+    lengths = lengths.to(torch.int32).contiguous()
+    if block_table.dim() != 2 or block_table.shape[0] != batch or block_table.stride(1) != 1:
+        block_table = block_table.reshape(batch, -1).contiguous()
+    output = torch.empty_like(query) if out is None else out
+    if not query_length or not batch:
+        return output.zero_() if out is not None else torch.zeros_like(query)
+    ck = cv = valid = None
+    ck_sb = ck_sh = 0
+    if has_current:
+        ck = current_key.to(query.dtype)
+        cv = current_value.to(query.dtype)
+        if ck.stride(2) != 1 or cv.stride() != ck.stride():
+            ck, cv = ck.contiguous(), cv.contiguous()
+        ck_sb, ck_sh = ck.stride(0), ck.stride(1)
+        valid = current_valid.to(torch.uint8).contiguous()
+    sk = sv = None
+    num_shared = 0
+    if shared_key is not None:
+        sk = shared_key.to(query.dtype).contiguous()
+        sv = shared_value.to(query.dtype).contiguous()
+        num_shared = sk.shape[0]
+    status = _lib.lib().grs_paged_attention(
+        _lib.DTYPE_CODES[query.dtype],
+        query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
+        key_cache.data_ptr(), value_cache.data_ptr(),
+        key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
+        block_table.data_ptr(), block_table.stride(0), lengths.data_ptr(),
+        _lib.ptr(ck), _lib.ptr(cv), ck_sb, ck_sh, _lib.ptr(valid),
+        _lib.ptr(sk), _lib.ptr(sv), num_shared,
+        output.data_ptr(), output.stride(0), output.stride(1), output.stride(2),
+        batch, heads, query_length, head_width, key_cache.shape[1], block_table.shape[1],
+        _lib.stream_of(query),
+    )
+    _lib.check(status, "paged_attention")
+    return output

@@ -1,0 +1,128 @@
+/* C ABI of the B200 beam-search decode kernels (libgrs_b200.so).
+ *
+ * Every entry point takes device pointers, element strides, sizes and a
+ * cudaStream_t passed as void*, enqueues its kernels on that stream and
+ * returns GRS_OK or a negative grs_status.  Nothing here allocates device
+ * memory unless it says so; nothing synchronises the stream.  Errors found by
+ * kernels (cache exhausted, bad page, refcount underflow) are written to a
+ * caller-provided device status word (int32, 0 = ok) that the host reads once
+ * per step.  Each entry point names the reference interface it replaces.
+ */
+#ifndef GRS_B200_H
+#define GRS_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GRS_API __attribute__((visibility("default")))
+#else
+#define GRS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  GRS_OK = 0,
+  GRS_ERR_EXHAUSTED = -1,    /* "paged KV cache exhausted" (paged_cache.py:87) */
+  GRS_ERR_BAD_PAGE = -2,     /* "retaining an unallocated page" (paged_cache.py:96) */
+  GRS_ERR_REFCOUNT = -3,     /* "negative page reference count" (paged_cache.py:103) */
+  GRS_ERR_SHAPE = -4,        /* bad shape / unsupported layout */
+  GRS_ERR_CUDA = -5,         /* a launch failed */
+  GRS_ERR_CORRUPT = -6,      /* "free-list corruption" (paged_cache.py:90) */
+  GRS_ERR_LENGTH = -7,       /* "prefix handle length/block table mismatch" (paged_cache.py:228) */
+  GRS_ERR_WORKSPACE = -8     /* caller workspace too small */
+} grs_status;
+
+enum { GRS_DTYPE_BF16 = 0, GRS_DTYPE_F32 = 1 };
+
+/* Library version string. */
+GRS_API const char* grs_version(void);
+
+/* ---- paged attention: paged_attention.py:217-306 (paged_attention) ------
+ * query [B,H,Q,D] (strides q_sb,q_sh,q_sq; D contiguous); key/value cache
+ * [pages,page,H,D] (strides kc_sp,kc_st,kc_sh; D contiguous); block_table
+ * int32 [B, >=1] (row stride bt_stride, max_blocks columns); lengths int32 [B];
+ * optional current_key/value [B,H,D] + current_valid uint8 [B] (all or none,
+ * paged_attention.py:230-232); optional shared_key/value [num_shared,H,D]
+ * contiguous, attended by every beam before its pages (not in the
+ * reference; the shared-prefix decode microbenchmark).  Rows with no valid
+ * key are written as zeros. */
+GRS_API int grs_paged_attention(int dtype, const void* query, int64_t q_sb, int64_t q_sh, int64_t q_sq,
+                        const void* key_cache, const void* value_cache, int64_t kc_sp,
+                        int64_t kc_st, int64_t kc_sh, const int32_t* block_table,
+                        int64_t bt_stride, const int32_t* lengths, const void* current_key,
+                        const void* current_value, int64_t ck_sb, int64_t ck_sh,
+                        const uint8_t* current_valid, const void* shared_key,
+                        const void* shared_value, int64_t num_shared, void* output,
+                        int64_t o_sb, int64_t o_sh, int64_t o_sq, int batch, int heads,
+                        int query_len, int head_width, int page_size, int max_blocks,
+                        void* stream);
+
+/* ---- PagedKVCache device state: paged_cache.py:16-105 -------------------
+ * refcounts int32 [capacity], free_list int32 [capacity] with its length in
+ * free_count (device int32), last_pos int32 [capacity] release scratch.
+ * grs_cache_init sets refcounts 0, free_list [capacity-1 .. 0]
+ * (paged_cache.py:74-75), last_pos -1. */
+GRS_API int grs_cache_init(int32_t* refcounts, int32_t* free_list, int32_t* free_count,
+                           int32_t* last_pos, int capacity, void* stream);
+
+/* paged_cache.py:107-208 (PagedKVCache.append_batch): for each of n parents
+ * (block-table rows + lengths) retain the shared pages, allocate the child
+ * page from the top of the free list (parent order), COW-copy the valid rows
+ * of a partial tail page and write one new row into every arena.  Arenas are
+ * contiguous: keys/values [layers, capacity, page, H*D], actions [capacity,
+ * page, W], readout keys/values [capacity, page, H*D] (nullable together with
+ * new_readout_*).  New rows: keys/values [layers, n, H*D], actions [n, W],
+ * readout [n, H*D], in the arena dtype (elem_bytes 2 = bf16, 4 = fp32).
+ * Writes child rows (child_cols columns, zero padded) and lengths. */
+GRS_API int grs_cache_append(int elem_bytes, int32_t* refcounts, int32_t* free_list,
+                             int32_t* free_count, int capacity, const int32_t* parent_table,
+                             int64_t parent_stride, const int32_t* parent_lengths, int n,
+                             int page_size, int32_t* child_table, int64_t child_stride,
+                             int32_t* child_lengths, int child_cols, void* keys, void* values,
+                             int layers, int heads_x_width, const void* new_keys,
+                             const void* new_values, void* actions, int model_width,
+                             const void* new_actions, void* readout_keys, void* readout_values,
+                             const void* new_readout_keys, const void* new_readout_values,
+                             int32_t* status, void* stream);
+
+/* paged_cache.py:99-105 (PagedKVCache.release) for n handles in order: pages
+ * reaching refcount 0 are appended to the free list in scan order. */
+GRS_API int grs_cache_release(int32_t* refcounts, int32_t* free_list, int32_t* free_count,
+                              int32_t* last_pos, int capacity, const int32_t* table,
+                              int64_t stride, const int32_t* lengths, int n, int cols,
+                              int page_size, int32_t* status, void* stream);
+
+/* paged_cache.py:223-228: flags GRS_ERR_LENGTH when ceil(length/page) differs
+ * from a handle's block count. */
+GRS_API int grs_cache_check_lengths(const int32_t* nblocks, const int32_t* lengths, int n,
+                                    int page_size, int32_t* status, void* stream);
+
+/* ---- proposals: gpu_proposals.py:69-192 (build_gpu_proposals) -----------
+ * Candidates (int64 batch_ids, sources; float32 probabilities) expand through
+ * the CSR rule index (GpuRuleIndex, gpu_proposals.py:20-50; int32 arrays);
+ * the stable per-parent cap and global rank select <= global_cap expanded
+ * actions: out_row (candidate row), out_xfer, out_next_gate (int64
+ * [global_cap], -1 padded), out_count (device int64), out_metrics
+ * (device int64 [2] = predicted_actions, eligible_actions).  max_expanded is
+ * an upper bound of the expansion size; workspace from
+ * grs_proposals_workspace_bytes(num_candidates, max_expanded). */
+GRS_API int64_t grs_proposals_workspace_bytes(int64_t max_candidates, int64_t max_expanded);
+GRS_API int grs_proposals_rank(const int64_t* batch_ids, const int64_t* sources,
+                               const float* probabilities, int64_t num_candidates,
+                               const int64_t* parent_gate_counts, int64_t num_parents,
+                               const int32_t* xfer_offsets, const int32_t* xfer_counts,
+                               const int32_t* xfer_ids, const int32_t* gate_deltas,
+                               const int32_t* all_xfer_counts, int num_sources,
+                               int64_t max_expanded, int per_parent_cap, int64_t global_cap,
+                               int64_t* out_row, int64_t* out_xfer, int64_t* out_next_gate,
+                               int64_t* out_count, int64_t* out_metrics, void* workspace,
+                               int64_t workspace_bytes, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GRS_B200_H */

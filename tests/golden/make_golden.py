@@ -1,0 +1,203 @@
+"""Generate the golden fixtures of tests/golden from the reference's own code.
+
+Run in a container where the reference repository is available:
+
+    python tests/golden/make_golden.py --reference /root/reference
+
+Each fixture stores seeded inputs and the outputs the reference's Python
+implementation produced for them (CPU, fp32).  The tests pin the CPU oracle
+against these files and compare the CUDA path with the oracle; nothing at
+test time reads the reference.
+"""
+from __future__ import annotations
+
+import argparse
+import math
+from pathlib import Path
+import sys
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+
+def paged_attention_case(ref, with_current: bool):
+    """The reference's own test case (test_paged_attention.py:8-60), fp32."""
+    torch.manual_seed(7)
+    b, cap, page, heads, hw, q = 5, 12, 8, 6, 32, 37
+    keys = torch.randn(cap, page, heads, hw)
+    values = torch.randn_like(keys)
+    table = torch.tensor([[0, 6, 9], [1, 6, 8], [2, 7, 9], [0, 6, 8], [3, 4, 5]], dtype=torch.int32)
+    lengths = torch.tensor([0, 3, 8, 9, 19], dtype=torch.int32)
+    query = torch.randn(b, heads, q, hw)
+    kwargs = {}
+    if with_current:
+        kwargs = dict(current_key=torch.randn(b, heads, hw), current_value=torch.randn(b, heads, hw),
+                      current_valid=torch.tensor([True, True, False, True, True]))
+    out = ref.paged_attention_reference(query, keys, values, table, lengths, **kwargs)
+    arrays = dict(query=query, keys=keys, values=values, block_table=table, lengths=lengths,
+                  output=out, **kwargs)
+    return {k: v.numpy() for k, v in arrays.items()}
+
+
+def cache_churn_case(paged_cache, *, seed: int, beams: int, depth: int, children: int,
+                     page: int, layers: int = 2, heads: int = 2, hw: int = 4, width: int = 8):
+    """Fork/COW/reclaim churn on the reference PagedKVCache (config-3 semantics:
+    each step forks every beam into `children`, keeps the top `beams` by seeded
+    uniform scores (stable, ties by index), appends one token per survivor and
+    releases the old handles)."""
+    g = torch.Generator().manual_seed(seed)
+    capacity = beams * (math.ceil(depth / page) + 3)
+    arena = paged_cache.PagedKVCache(layers=layers, capacity=capacity, page_size=page,
+                                     heads=heads, head_width=hw, model_width=width,
+                                     device=torch.device("cpu"), dtype=torch.float32)
+    handles = [arena.empty_handle()]
+    rec = {"capacity": np.int64(capacity), "page": np.int64(page), "layers": np.int64(layers),
+           "heads": np.int64(heads), "hw": np.int64(hw), "width": np.int64(width)}
+    for step in range(depth):
+        scores = torch.rand(len(handles) * children, generator=g)
+        order = torch.sort(scores, descending=True, stable=True).indices[:beams]
+        parents = (order // children).tolist()
+        n = len(parents)
+        kv = torch.randn(layers, n, heads, hw, generator=g)
+        vv = torch.randn(layers, n, heads, hw, generator=g)
+        act = torch.randn(n, width, generator=g)
+        rk = torch.randn(n, heads, hw, generator=g)
+        rv = torch.randn(n, heads, hw, generator=g)
+        new = arena.append_batch([handles[p] for p in parents], kv, vv, act, rk, rv)
+        for h in handles:
+            arena.release(h)
+        handles = new
+        cols = max(len(h.blocks) for h in handles)
+        table = np.zeros((n, cols), np.int32)
+        for i, h in enumerate(handles):
+            table[i, : len(h.blocks)] = h.blocks
+        rec[f"s{step}_parents"] = np.asarray(parents, np.int64)
+        rec[f"s{step}_keys"] = kv.numpy(); rec[f"s{step}_values"] = vv.numpy()
+        rec[f"s{step}_actions"] = act.numpy()
+        rec[f"s{step}_rkeys"] = rk.numpy(); rec[f"s{step}_rvalues"] = rv.numpy()
+        rec[f"s{step}_table"] = table
+        rec[f"s{step}_lengths"] = np.asarray([h.length for h in handles], np.int32)
+        rec[f"s{step}_refcounts"] = np.asarray(arena.refcounts, np.int32)
+        rec[f"s{step}_free"] = np.asarray(arena.free, np.int32)
+        # arena rows of every live handle token (valid positions only)
+        _, values_g, actions_g, mask = arena.gather(handles)
+        rec[f"s{step}_gather_values"] = values_g.numpy()
+        rec[f"s{step}_gather_actions"] = actions_g.numpy()
+    for h in handles:
+        arena.release(h)
+    rec["final_allocated"] = np.int64(arena.allocated_pages)
+    rec["depth"] = np.int64(depth)
+    return rec
+
+
+def proposals_cases(gp, bsb, prb, ti):
+    out = {}
+    # 1. The reference test's hand-built case (test_gpu_proposals.py:27-91).
+    beam = [bsb.BeamState(None, {"nodes": [], "edges": []}, {}, 0, {}, {}, set(), 0, g, 1, ())
+            for g in (20, 18, 21)]
+    s2x = {0: [0, 1], 1: [2], 2: [3, 4]}
+    deltas = [0, -1, 1, 2, -2]
+    rows = [[(0, 2, (2, 3), 0.7), (1, 4, (4,), 0.9)],
+            [(2, 1, (1, 5), 0.8), (0, 3, (3, 7), 0.6)],
+            [(1, 6, (6,), 0.95), (2, 8, (8,), 0.5)]]
+    flat = [(b, s, a, bind, p) for b, r in enumerate(rows) for s, a, bind, p in r]
+    bind = torch.full((len(flat), 2), -1, dtype=torch.long)
+    for i, r in enumerate(flat):
+        bind[i, : len(r[3])] = torch.tensor(r[3])
+    cand = ti.CandidateTensors(torch.tensor([r[0] for r in flat]), torch.tensor([r[1] for r in flat]),
+                               torch.tensor([r[2] for r in flat]), bind,
+                               torch.tensor([r[4] for r in flat]))
+    index = gp.GpuRuleIndex.build(s2x, deltas, 3, 1, torch.device("cpu"))
+    props, metrics, _ = gp.build_gpu_proposals(cand, beam, index, per_parent_cap=2, global_cap=4)
+    legacy, _ = prb.build_legacy_proposals(beam, rows, None, s2x, deltas, beam_size=2,
+                                           max_actions_per_parent=2, exploration_actions_per_parent=0,
+                                           proposal_factor=2, max_gate_increase=1)
+    assert [(p.parent, p.xfer_id, p.anchor_slot, p.binding) for p in props] == \
+        [(p.parent, p.xfer_id, p.anchor_slot, p.binding) for p in legacy]
+    out["small"] = _pack_proposals(cand, [b.gate_count for b in beam], s2x, deltas, 3, 1, 2, 4,
+                                   props, metrics)
+    # 2. Seeded random case with ties in probability and gate counts.
+    g = torch.Generator().manual_seed(11)
+    num_parents, per, num_sources, num_xfers = 40, 30, 9, 17
+    x2s = torch.randint(0, num_sources, (num_xfers,), generator=g).tolist()
+    s2x = {}
+    for x, s in enumerate(x2s):
+        s2x.setdefault(s, []).append(x)
+    deltas = torch.randint(-2, 3, (num_xfers,), generator=g).tolist()
+    gates = torch.randint(50, 56, (num_parents,), generator=g).tolist()
+    n = num_parents * per
+    batch = torch.arange(num_parents).repeat_interleave(per)
+    perm = torch.randperm(n, generator=g)
+    batch = batch[perm]
+    sources = torch.randint(0, num_sources, (n,), generator=g)
+    anchors = torch.randint(0, 100, (n,), generator=g)
+    bind = torch.randint(-1, 100, (n, 3), generator=g)
+    probs = (torch.randint(0, 12, (n,), generator=g).float() / 16.0).sigmoid()  # many ties
+    cand = ti.CandidateTensors(batch, sources, anchors, bind, probs)
+    beam = [bsb.BeamState(None, {"nodes": [], "edges": []}, {}, 0, {}, {}, set(), 0, gg, 1, ())
+            for gg in gates]
+    index = gp.GpuRuleIndex.build(s2x, deltas, num_sources, 1, torch.device("cpu"))
+    props, metrics, _ = gp.build_gpu_proposals(cand, beam, index, per_parent_cap=5, global_cap=120)
+    out["random"] = _pack_proposals(cand, gates, s2x, deltas, num_sources, 1, 5, 120, props, metrics)
+    return out
+
+
+def _pack_proposals(cand, gates, s2x, deltas, num_sources, max_inc, cap, gcap, props, metrics):
+    xfer_src = np.full(len(deltas), -1, np.int64)
+    for s, xs in s2x.items():
+        for x in xs:
+            xfer_src[x] = s
+    width = cand.bindings.shape[1]
+    bind = np.full((len(props), width), -1, np.int64)
+    for i, p in enumerate(props):
+        bind[i, : len(p.binding)] = p.binding
+    return dict(
+        batch_ids=cand.batch_ids.numpy(), sources=cand.sources.numpy(), anchors=cand.anchors.numpy(),
+        bindings=cand.bindings.numpy(), probabilities=cand.probabilities.numpy().astype(np.float32),
+        parent_gates=np.asarray(gates, np.int64), xfer_to_source=xfer_src,
+        gate_deltas=np.asarray(deltas, np.int64), num_sources=np.int64(num_sources),
+        max_gate_increase=np.int64(max_inc), per_parent_cap=np.int64(cap), global_cap=np.int64(gcap),
+        out_parent=np.asarray([p.parent for p in props], np.int64),
+        out_xfer=np.asarray([p.xfer_id for p in props], np.int64),
+        out_anchor=np.asarray([p.anchor_slot for p in props], np.int64),
+        out_binding=bind,
+        out_probability=np.asarray([p.probability for p in props], np.float64),
+        out_next_gate=np.asarray([p.next_gate_count for p in props], np.int64),
+        predicted=np.int64(metrics["predicted_actions"]), eligible=np.int64(metrics["eligible_actions"]),
+    )
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--only", default="")
+    args = parser.parse_args()
+    sys.path.insert(0, str(args.reference))
+    import paged_attention as ref_attention
+    import paged_cache as ref_cache
+    import gpu_proposals as ref_proposals
+    import beam_search_benchmark as ref_bsb
+    import paged_rollout_benchmark as ref_prb
+    import threshold_inference as ref_ti
+
+    only = set(filter(None, args.only.split(",")))
+    if not only or "attention" in only:
+        np.savez_compressed(HERE / "paged_attention_history.npz", **paged_attention_case(ref_attention, False))
+        np.savez_compressed(HERE / "paged_attention_current.npz", **paged_attention_case(ref_attention, True))
+    if not only or "cache" in only:
+        np.savez_compressed(HERE / "paged_cache_churn_p4.npz",
+                            **cache_churn_case(ref_cache, seed=3, beams=8, depth=11, children=3, page=4))
+        np.savez_compressed(HERE / "paged_cache_churn_p3.npz",
+                            **cache_churn_case(ref_cache, seed=5, beams=13, depth=9, children=5, page=3))
+    if not only or "proposals" in only:
+        for name, case in proposals_cases(ref_proposals, ref_bsb, ref_prb, ref_ti).items():
+            np.savez_compressed(HERE / f"proposals_{name}.npz", **case)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,118 @@
+"""CUDA paged attention vs the oracle (tolerances: fp32 1e-5 relative; bf16 2e-2)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle import paged_attention as oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(dev, g, dtype, with_current):
+    from graph_rewrite_system_b200.paged_attention import paged_attention
+
+    t = lambda k: torch.from_numpy(g[k]).to(dev)
+    kwargs = {}
+    if with_current:
+        kwargs = dict(current_key=t("current_key").to(dtype), current_value=t("current_value").to(dtype),
+                      current_valid=t("current_valid"))
+    return paged_attention(t("query").to(dtype), t("keys").to(dtype), t("values").to(dtype),
+                           t("block_table"), t("lengths"), **kwargs)
+
+
+@pytest.mark.parametrize("name,with_current", [("paged_attention_history.npz", False),
+                                               ("paged_attention_current.npz", True)])
+def test_golden_fp32(cuda_device, name, with_current):
+    g = load_golden(name)
+    out = _run(cuda_device, g, torch.float32, with_current).cpu().numpy()
+    np.testing.assert_allclose(out, g["output"], rtol=1e-5, atol=1e-5)
+    if not with_current:
+        assert not out[0].any()
+
+
+@pytest.mark.parametrize("name,with_current", [("paged_attention_history.npz", False),
+                                               ("paged_attention_current.npz", True)])
+def test_golden_bf16(cuda_device, name, with_current):
+    g = load_golden(name)
+    out = _run(cuda_device, g, torch.bfloat16, with_current).float().cpu().numpy()
+    # the reference's own bf16 tolerance (test_paged_attention.py:57)
+    np.testing.assert_allclose(out, g["output"], rtol=2e-2, atol=2e-2)
+
+
+def _random_case(seed, batch, heads, hw, page, cap, q, max_len, dtype, dev, shared=0,
+                 current=False):
+    g = torch.Generator().manual_seed(seed)
+    keys = torch.randn(cap, page, heads, hw, generator=g)
+    values = torch.randn(cap, page, heads, hw, generator=g)
+    lengths = torch.randint(0, max_len + 1, (batch,), generator=g, dtype=torch.int32)
+    lengths[0] = 0
+    lengths[-1] = max_len
+    cols = max(1, -(-max_len // page))
+    table = torch.randint(0, cap, (batch, cols), generator=g, dtype=torch.int32)
+    query = torch.randn(batch, heads, q, hw, generator=g)
+    kw = {}
+    if shared:
+        kw["shared_key"] = torch.randn(shared, heads, hw, generator=g)
+        kw["shared_value"] = torch.randn(shared, heads, hw, generator=g)
+    if current:
+        kw["current_key"] = torch.randn(batch, heads, hw, generator=g)
+        kw["current_value"] = torch.randn(batch, heads, hw, generator=g)
+        kw["current_valid"] = torch.rand(batch, generator=g) > 0.2
+    # round inputs to the kernel dtype so both sides see the same values
+    rnd = lambda x: x.to(dtype).float()
+    query, keys, values = rnd(query), rnd(keys), rnd(values)
+    kw = {k: (rnd(v) if v.is_floating_point() else v) for k, v in kw.items()}
+    expected = oracle.paged_attention(query, keys, values, table, lengths, **kw)
+    from graph_rewrite_system_b200.paged_attention import paged_attention
+
+    dkw = {k: v.to(dev).to(dtype) if v.is_floating_point() else v.to(dev) for k, v in kw.items()}
+    out = paged_attention(query.to(dev, dtype), keys.to(dev, dtype), values.to(dev, dtype),
+                          table.to(dev), lengths.to(dev), **dkw)
+    return out.float().cpu(), expected
+
+
+@pytest.mark.parametrize("hw", [8, 32, 64])
+def test_random_decode_with_current(cuda_device, hw):
+    out, exp = _random_case(1, 37, 6, hw, 8, 40, 1, 70, torch.float32, cuda_device, current=True)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=1e-5, atol=1e-5)
+
+
+def test_readout_mma_bf16(cuda_device):
+    # node readout shape: Q=381 queries per beam, T<=64, head width 32 -> tensor-core path
+    out, exp = _random_case(2, 24, 8, 32, 16, 120, 381, 64, torch.bfloat16, cuda_device)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+    assert not out[0].any()  # zero-length history row
+
+
+def test_readout_mma_multi_tile_bf16(cuda_device):
+    out, exp = _random_case(3, 9, 6, 32, 8, 90, 45, 150, torch.bfloat16, cuda_device)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+
+
+def test_readout_fp32_rows(cuda_device):
+    out, exp = _random_case(4, 7, 4, 32, 4, 30, 50, 20, torch.float32, cuda_device)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=1e-5, atol=1e-5)
+
+
+def test_shared_prefix_decode_bf16(cuda_device):
+    out, exp = _random_case(5, 64, 8, 32, 16, 300, 1, 64, torch.bfloat16, cuda_device, shared=381)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+
+
+def test_shared_prefix_decode_fp32(cuda_device):
+    out, exp = _random_case(6, 16, 8, 32, 16, 64, 1, 64, torch.float32, cuda_device, shared=37)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=1e-5, atol=1e-5)
+
+
+def test_partial_current_triple_rejected(cuda_device):
+    from graph_rewrite_system_b200.paged_attention import paged_attention
+
+    q = torch.zeros(1, 1, 1, 32, device=cuda_device)
+    kc = torch.zeros(1, 4, 1, 32, device=cuda_device)
+    with pytest.raises(ValueError):
+        paged_attention(q, kc, kc, torch.zeros(1, 1, dtype=torch.int32, device=cuda_device),
+                        torch.zeros(1, dtype=torch.int32, device=cuda_device),
+                        current_key=torch.zeros(1, 1, 32, device=cuda_device))
