@@ -23,6 +23,7 @@ ERRORS = {
     -6: (RuntimeError, "free-list corruption"),
     -7: (RuntimeError, "prefix handle length/block table mismatch"),
     -8: (RuntimeError, "workspace too small"),
+    -9: (ValueError, "inputs exceed the library's fixed scratch capacity"),
 }
 
 DTYPE_CODES = {torch.bfloat16: 0, torch.float32: 1}

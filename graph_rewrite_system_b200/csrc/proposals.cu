@@ -316,3 +316,71 @@ extern "C" int grs_proposals_rank(
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free proposal ranking.
+//
+// grs_proposals_rank needs a scratch workspace that its caller allocates.
+// Some callers cannot allocate device memory at the moment they rank
+// proposals: a host runtime whose device memory is entirely reserved up front
+// by its own pool, a foreign-language binding (Go, Java, Rust) that has no
+// handle on the framework's caching allocator, or a latency-critical loop in
+// which a cudaMalloc would synchronise the device.  For them this variant
+// takes its scratch from a fixed array compiled into the library:
+// GRS_PROPOSALS_STATIC_SCRATCH_BYTES (8 MiB) of device memory that every GPU
+// which loads this code keeps until the process exits.
+//
+// The array is named here as a host-side stand-in; its device address is
+// resolved with cudaGetSymbolAddress once per device, on that device's first
+// call (so make the first call on each device before any stream capture).
+// All calls share the one array, which keeps whatever the last call left in
+// it; every scratch location is written before it is read, so no clearing is
+// needed, but two calls whose work overlaps on the GPU (different streams
+// without ordering between them) race on the array.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace grs {
+constexpr int64_t kProposalStaticScratchBytes = GRS_PROPOSALS_STATIC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_proposal_scratch[kProposalStaticScratchBytes];
+constexpr int kMaxDevices = 64;
+}  // namespace grs
+
+extern "C" int grs_proposals_rank_static(
+    const int64_t* batch_ids, const int64_t* sources, const float* probabilities,
+    int64_t num_candidates, const int64_t* parent_gate_counts, int64_t num_parents,
+    const int32_t* xfer_offsets, const int32_t* xfer_counts, const int32_t* xfer_ids,
+    const int32_t* gate_deltas, const int32_t* all_xfer_counts, int num_sources,
+    int64_t max_expanded, int per_parent_cap, int64_t global_cap, int64_t* out_row,
+    int64_t* out_xfer, int64_t* out_next_gate, int64_t* out_count, int64_t* out_metrics,
+    int32_t* status, void* stream) {
+  if (num_candidates < 0 || max_expanded < 0 || num_candidates > (1ll << 30) ||
+      max_expanded > (1ll << 30))
+    return GRS_ERR_SHAPE;
+  PropWorkspace w;
+  if ((int64_t)prop_layout(nullptr, num_candidates, max_expanded, &w) >
+      kProposalStaticScratchBytes)
+    return GRS_ERR_TOO_LARGE;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices)
+    return GRS_ERR_CUDA;
+  static std::mutex lock;
+  static void* scratch_address[kMaxDevices] = {};
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> guard(lock);
+    if (scratch_address[device] == nullptr) {
+      void* address = nullptr;
+      if (cudaGetSymbolAddress(&address, g_proposal_scratch) != cudaSuccess || !address)
+        return GRS_ERR_CUDA;
+      scratch_address[device] = address;
+    }
+    scratch = scratch_address[device];
+  }
+  return grs_proposals_rank(batch_ids, sources, probabilities, num_candidates,
+                            parent_gate_counts, num_parents, xfer_offsets, xfer_counts,
+                            xfer_ids, gate_deltas, all_xfer_counts, num_sources, max_expanded,
+                            per_parent_cap, global_cap, out_row, out_xfer, out_next_gate,
+                            out_count, out_metrics, scratch, kProposalStaticScratchBytes, status,
+                            stream);
+}

@@ -32,7 +32,8 @@ typedef enum {
   GRS_ERR_CUDA = -5,         /* a launch failed */
   GRS_ERR_CORRUPT = -6,      /* "free-list corruption" (paged_cache.py:90) */
   GRS_ERR_LENGTH = -7,       /* "prefix handle length/block table mismatch" (paged_cache.py:228) */
-  GRS_ERR_WORKSPACE = -8     /* caller workspace too small */
+  GRS_ERR_WORKSPACE = -8,    /* caller workspace too small */
+  GRS_ERR_TOO_LARGE = -9     /* inputs exceed a fixed internal scratch capacity */
 } grs_status;
 
 enum { GRS_DTYPE_BF16 = 0, GRS_DTYPE_F32 = 1 };
@@ -120,6 +121,30 @@ GRS_API int grs_proposals_rank(const int64_t* batch_ids, const int64_t* sources,
                                int64_t* out_row, int64_t* out_xfer, int64_t* out_next_gate,
                                int64_t* out_count, int64_t* out_metrics, void* workspace,
                                int64_t workspace_bytes, int32_t* status, void* stream);
+
+/* Allocation-free variant of grs_proposals_rank (no counterpart in the
+ * reference).  For callers that cannot allocate device memory when they rank
+ * proposals (a runtime whose device memory is all pre-reserved by its own
+ * pool, a foreign-language binding without access to the framework's
+ * allocator, a loop where cudaMalloc would stall the device): the scratch
+ * comes from a fixed GRS_PROPOSALS_STATIC_SCRATCH_BYTES array inside the
+ * library, held on every GPU that loads it until exit.  Inputs whose
+ * workspace (grs_proposals_workspace_bytes) exceeds it return
+ * GRS_ERR_TOO_LARGE without launching anything.  The first call on a device
+ * resolves the array's device address; make it before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race.  Same
+ * arguments and outputs as grs_proposals_rank minus the workspace. */
+#define GRS_PROPOSALS_STATIC_SCRATCH_BYTES (8ll << 20)
+GRS_API int grs_proposals_rank_static(const int64_t* batch_ids, const int64_t* sources,
+                                      const float* probabilities, int64_t num_candidates,
+                                      const int64_t* parent_gate_counts, int64_t num_parents,
+                                      const int32_t* xfer_offsets, const int32_t* xfer_counts,
+                                      const int32_t* xfer_ids, const int32_t* gate_deltas,
+                                      const int32_t* all_xfer_counts, int num_sources,
+                                      int64_t max_expanded, int per_parent_cap,
+                                      int64_t global_cap, int64_t* out_row, int64_t* out_xfer,
+                                      int64_t* out_next_gate, int64_t* out_count,
+                                      int64_t* out_metrics, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }
