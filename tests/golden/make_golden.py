@@ -196,7 +196,159 @@ def main() -> None:
     if not only or "proposals" in only:
         for name, case in proposals_cases(ref_proposals, ref_bsb, ref_prb, ref_ti).items():
             np.savez_compressed(HERE / f"proposals_{name}.npz", **case)
+    if not only or "model" in only:
+        np.savez_compressed(HERE / "model_cpu_equivalence.npz", **model_case(args.reference))
     print("golden fixtures written to", HERE)
+
+
+
+
+def random_prefixes(ref_graph, circuit_snapshot, rules, num_beams, num_actions, seed):
+    """Seeded valid action prefixes: at each step pick uniformly among every
+    (source, anchor) whose structural binding exists in the current graph
+    (the reference's incremental_graph.structural_binding), then a uniform
+    xfer of that source; destination slots continue the slot counter."""
+    import random
+
+    rng = random.Random(seed)
+    s2x = rules.source_to_xfers()
+    samples = []
+    for beam in range(num_beams):
+        circuit = ref_graph.IncrementalCircuit(circuit_snapshot)
+        next_slot = max(n[0] for n in circuit_snapshot["nodes"]) + 1
+        actions = []
+        for _ in range(num_actions):
+            options = []
+            for source_id, pattern in enumerate(rules.source_patterns):
+                ops = ref_graph.parse_pattern(pattern)
+                for anchor in sorted(circuit.nodes):
+                    binding = ref_graph.structural_binding(circuit, ops, anchor)
+                    if binding is not None:
+                        options.append((source_id, binding))
+            source_id, binding = options[rng.randrange(len(options))]
+            xfer = rng.choice(s2x[source_id])
+            dst = ref_graph.parse_pattern(rules.xfer_destinations[xfer])
+            dst_slots = tuple(range(next_slot, next_slot + len(dst)))
+            circuit.apply(ref_graph.parse_pattern(rules.xfer_sources[xfer]), dst, binding, dst_slots)
+            next_slot += len(dst)
+            actions.append({"xfer_id": xfer, "source_id": source_id,
+                            "binding_slots": list(binding), "dst_slots": list(dst_slots)})
+        samples.append({"initial_graph": circuit_snapshot, "actions": actions, "matches": [],
+                        "prefix_length": num_actions, "local_streak": 0, "previous_action": None,
+                        "previous_delta": None, "previous_local_streak": 0})
+    return samples
+
+
+def model_case(reference: Path, *, seed=0, beams=8, actions=8):
+    """Full-prefix encode, one-token paged decode, paged readout, match logits,
+    structural decode and threshold candidates of the reference model
+    (CPU equivalence configuration, seeded weights)."""
+    import dataset as ref_dataset
+    import incremental_graph as ref_graph
+    import paged_cache as ref_cache
+    import paged_model as ref_model
+    import threshold_inference as ref_ti
+    from graph_rewrite_system_b200 import synthetic
+    from oracle.model import parameter_shapes
+
+    rules = synthetic.small_rules()
+    cfg = synthetic.CPU_EQUIVALENCE_MODEL
+    ref_rules = ref_dataset.RuleMetadata.from_payload({
+        "source_patterns": list(rules.source_patterns),
+        "xfer_to_source": list(rules.xfer_to_source),
+        "xfer_sources": list(rules.xfer_sources),
+        "xfer_destinations": list(rules.xfer_destinations)})
+    model = ref_model.PagedActionBindingModel(
+        ref_rules, num_xfers=rules.num_xfers, width=cfg.width,
+        retrieval_width=cfg.retrieval_width, graph_layers=cfg.graph_layers,
+        action_layers=cfg.action_layers, action_heads=cfg.action_heads,
+        max_sequence_length=cfg.max_sequence_length,
+        readout_graph_layers=cfg.readout_graph_layers, readout_attention_backend="paged",
+        dropout=0.0).eval()
+    shapes = parameter_shapes(cfg, rules)
+    params = synthetic.deterministic_parameters(shapes, seed)
+    state = model.state_dict()
+    names = {n for n, _ in model.named_parameters()}
+    assert names == set(shapes), (names ^ set(shapes))
+    for k, v in params.items():
+        assert tuple(state[k].shape) == v.shape, k
+        state[k] = torch.from_numpy(v)
+    model.load_state_dict(state)
+
+    circuit = synthetic.random_dag(48, 8, seed + 1)
+    snapshot = circuit.snapshot()
+    samples = random_prefixes(ref_graph, snapshot, rules, beams, actions, seed + 2)
+    batch = ref_dataset.collate_prefixes(samples, ref_rules)
+    out = {}
+    for key in ("initial_types", "edge_batch", "edge_src", "edge_dst", "edge_relation",
+                "current_types", "current_edge_batch", "current_edge_src", "current_edge_dst",
+                "current_edge_relation", "action_xfers", "action_sources", "binding_slots",
+                "destination_slots", "destination_types", "current_rewrite_distance"):
+        out["batch_" + key] = batch[key].numpy()
+    with torch.no_grad():
+        full_states, full_live, full_types = model.encode(batch)
+        out["encode_states"] = full_states.numpy()
+        out["encode_live"] = full_live.numpy()
+        out["encode_types"] = full_types.numpy()
+        # one-token paged decode, then the paged readout
+        s0 = {k: batch[k] for k in ("initial_types", "edge_batch", "edge_src", "edge_dst",
+                                    "edge_relation")}
+        states, live, types = model.initialize_incremental(s0)
+        out["initial_states"] = states.numpy()
+        arena = ref_cache.PagedKVCache(layers=cfg.action_layers, capacity=64, page_size=4,
+                                       heads=cfg.action_heads,
+                                       head_width=cfg.width // cfg.action_heads,
+                                       model_width=cfg.width, device=torch.device("cpu"),
+                                       dtype=torch.float32)
+        handles = [arena.empty_handle()] * beams
+        tokens, keys0 = [], []
+        for a in range(actions):
+            table, lengths = arena.block_table(handles)
+            res = model.advance_incremental(
+                states, live, types, None, None,
+                states.new_empty((beams, 0, cfg.width)), torch.empty((beams, 0), dtype=torch.bool),
+                xfer_ids=batch["action_xfers"][:, a], source_ids=batch["action_sources"][:, a],
+                source_slots=batch["binding_slots"][:, a],
+                destination_slots=batch["destination_slots"][:, a],
+                destination_types=batch["destination_types"][:, a],
+                paged_key_cache=arena.keys, paged_value_cache=arena.values,
+                block_table=table, past_lengths=lengths)
+            states, live, types, new_k, new_v, action, _ = res
+            rk, rv = model.project_action_readout_kv(action)
+            new_handles = arena.append_batch(handles, new_k, new_v, action, rk, rv)
+            for h in handles:
+                arena.release(h)
+            handles = new_handles
+            tokens.append(action.numpy())
+            keys0.append(new_k[0].numpy())
+        out["advance_tokens"] = np.stack(tokens)
+        out["advance_keys_layer0"] = np.stack(keys0)
+        out["advance_states"] = states.numpy()
+        out["advance_live"] = live.numpy()
+        out["advance_types"] = types.numpy()
+        table, lengths = arena.block_table(handles)
+        readout, _, _ = model.readout_incremental(
+            states, live, types, states.new_empty((beams, 0, cfg.width)),
+            torch.empty((beams, 0), dtype=torch.bool), batch,
+            readout_key_cache=arena.readout_keys, readout_value_cache=arena.readout_values,
+            block_table=table, lengths=lengths)
+        out["readout_states"] = readout.numpy()
+        logits, eligible = model.match_logits(readout, live, types)
+        out["logits"] = logits.numpy()
+        out["eligible"] = eligible.numpy()
+        config = {"groups": {g: {"scale": 1.0, "bias": 0.0, "raw_threshold": -1e9}
+                             for g in ("near", "far")}}
+        cand = ref_ti.threshold_candidate_tensors(model, batch, logits, eligible, config,
+                                                  max_candidates_per_state=24)
+        for k in ("batch_ids", "sources", "anchors", "bindings", "probabilities"):
+            out["candidates_" + k] = getattr(cand, k).numpy()
+        # structural decode of every (slot, source) pair with an eligible anchor
+        bi, sl, so = eligible.nonzero(as_tuple=True)
+        bindings, valid = model.structural_decode(batch, types, live, bi, so, sl)
+        out["decode_batch"], out["decode_sources"], out["decode_anchors"] = bi.numpy(), so.numpy(), sl.numpy()
+        out["decode_bindings"], out["decode_valid"] = bindings.numpy(), valid.numpy()
+    out["seed"] = np.int64(seed)
+    return out
 
 
 if __name__ == "__main__":
