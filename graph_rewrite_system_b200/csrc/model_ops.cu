@@ -1,0 +1,594 @@
+// Row-wise fused kernels of the paged action model (reference paged_model.py,
+// model.py).  GEMMs are plain cuBLAS calls made by the host; every other
+// operation of the one-token step, the node readout and the readout graph is
+// one of the kernels below.  Each kernel is templated on the activation type
+// (fp32 for the CPU-equivalence configuration, bf16 for the rollout) and
+// computes in fp32.  Rows are processed one warp per row; each lane owns the
+// row elements lane, lane + 32, ... (coalesced 32-lane accesses).
+#include "grs_common.cuh"
+
+namespace grs {
+
+__device__ __forceinline__ float gelu_exact(float x) {
+  return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+}
+
+template <typename T> struct DT;
+template <> struct DT<float> { static constexpr int code = GRS_DTYPE_F32; };
+template <> struct DT<__nv_bfloat16> { static constexpr int code = GRS_DTYPE_BF16; };
+
+constexpr int ROW_WARPS = 8;  // rows per CTA
+
+// ---------------------------------------------------------------------------
+// s = x + scale[row] * y;   (y, scale optional)
+// zc = zero_row[row] && zero_beam[beam];   wc = where_row && where_beam && where_len > 0
+// if zero_before: s = zc ? s : 0
+// sum_out = s
+// r = wc ? LN(s) : x;  if !zero_before: r = zc ? r : 0;   ln_out = r
+// beam = row / rows_per_beam.  Null masks are true.
+// ---------------------------------------------------------------------------
+struct AddLnArgs {
+  const void* x; int64_t x_stride;
+  const void* y; int64_t y_stride;
+  const float* scale;
+  const float* gamma; const float* beta;
+  void* sum_out; int64_t sum_stride;
+  void* ln_out; int64_t ln_stride;
+  const uint8_t* zero_row; const uint8_t* zero_beam;
+  const uint8_t* where_row; const uint8_t* where_beam; const int32_t* where_len;
+  int64_t rows; int rows_per_beam; int width; float eps; int zero_before;
+};
+
+template <typename T, int VPL>
+__global__ void __launch_bounds__(ROW_WARPS * 32) add_ln_kernel(AddLnArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  const int64_t beam = row / a.rows_per_beam;
+  const T* x = reinterpret_cast<const T*>(a.x) + row * a.x_stride;
+  const T* y = a.y ? reinterpret_cast<const T*>(a.y) + row * a.y_stride : nullptr;
+  const float sc = a.scale ? a.scale[row] : 1.f;
+  bool zc = true, wc = true;
+  if (a.zero_row) zc = zc && a.zero_row[row];
+  if (a.zero_beam) zc = zc && a.zero_beam[beam];
+  if (a.where_row) wc = wc && a.where_row[row];
+  if (a.where_beam) wc = wc && a.where_beam[beam];
+  if (a.where_len) wc = wc && a.where_len[beam] > 0;
+  float xv[VPL], s[VPL];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int i = lane + 32 * j;
+    xv[j] = 0.f; s[j] = 0.f;
+    if (i < a.width) {
+      xv[j] = to_float(x[i]);
+      s[j] = xv[j] + (y ? sc * to_float(y[i]) : 0.f);
+      if (a.zero_before && !zc) s[j] = 0.f;
+      sum += s[j];
+    }
+  }
+  if (a.sum_out) {
+    T* so = reinterpret_cast<T*>(a.sum_out) + row * a.sum_stride;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int i = lane + 32 * j;
+      if (i < a.width) so[i] = from_float<T>(s[j]);
+    }
+  }
+  if (!a.ln_out) return;
+  const float mean = warp_sum(sum) / a.width;
+  float var = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int i = lane + 32 * j;
+    if (i < a.width) { const float d = s[j] - mean; var += d * d; }
+  }
+  const float rstd = rsqrtf(warp_sum(var) / a.width + a.eps);
+  T* lo = reinterpret_cast<T*>(a.ln_out) + row * a.ln_stride;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int i = lane + 32 * j;
+    if (i < a.width) {
+      float r = wc ? (s[j] - mean) * rstd * a.gamma[i] + a.beta[i] : xv[j];
+      if (!a.zero_before && !zc) r = 0.f;
+      lo[i] = from_float<T>(r);
+    }
+  }
+}
+
+// In place: y[r, c] = GELU(y[r, c] + bias[c]) (bias optional).
+template <typename T>
+__global__ void bias_gelu_kernel(T* y, int64_t rows, int cols, int64_t stride,
+                                 const float* bias, int apply_gelu) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * cols) return;
+  const int64_t r = idx / cols;
+  const int c = (int)(idx % cols);
+  T* p = y + r * stride + c;
+  float v = to_float(*p) + (bias ? bias[c] : 0.f);
+  *p = from_float<T>(apply_gelu ? gelu_exact(v) : v);
+}
+
+// states[b, s] = (gate_embedding[max(type, 0)] + marker) * (type >= 0)
+// (paged_model.py:246-250); live[b, s] = type >= 0.
+template <typename T>
+__global__ void embed_initial_kernel(const int64_t* types, int64_t rows, int width,
+                                     const float* gate_emb, const float* marker, T* states,
+                                     int64_t stride, uint8_t* live) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t t = types[row];
+  if (lane == 0) live[row] = t >= 0;
+  const float* e = gate_emb + (t < 0 ? 0 : t) * width;
+  for (int i = lane; i < width; i += 32)
+    states[row * stride + i] = from_float<T>(t >= 0 ? e[i] + marker[i] : 0.f);
+}
+
+// Message-passing aggregation of InitialGraphLayer (model.py:36-51) over the
+// port arrays: each node gathers forward messages from its in-ports and
+// backward messages from its out-ports, adds the relation embeddings and
+// divides by its degree.  No atomics: the port arrays are the CSR.
+//   fb [B*S, 2W]: forward_message(x) | backward_message(x); rel [32, W] (fp32)
+//   ports [B, S, 4] int32 each; out writes agg into agg [B*S] rows (stride).
+template <typename T, int VPL>
+__global__ void __launch_bounds__(ROW_WARPS * 32) graph_aggregate_kernel(
+    const T* fb, int64_t fb_stride, const float* rel, const int32_t* in_node,
+    const int32_t* in_port, const int32_t* out_node, const int32_t* out_port, int64_t rows,
+    int slots, int width, T* agg, int64_t agg_stride) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t beam_base = (row / slots) * slots;
+  float acc[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) acc[j] = 0.f;
+  int deg = 0;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int src = in_node[row * 4 + p];
+    if (src >= 0) {
+      const int r = in_port[row * 4 + p] * 4 + p;
+      const T* f = fb + (beam_base + src) * fb_stride;
+      const float* e = rel + (int64_t)r * width;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int i = lane + 32 * j;
+        if (i < width) acc[j] += to_float(f[i]) + e[i];
+      }
+      ++deg;
+    }
+    const int dst = out_node[row * 4 + p];
+    if (dst >= 0) {
+      const int r = 16 + p * 4 + out_port[row * 4 + p];
+      const T* bk = fb + (beam_base + dst) * fb_stride + width;
+      const float* e = rel + (int64_t)r * width;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int i = lane + 32 * j;
+        if (i < width) acc[j] += to_float(bk[i]) + e[i];
+      }
+      ++deg;
+    }
+  }
+  const float inv = 1.f / (float)(deg > 0 ? deg : 1);
+  T* o = agg + row * agg_stride;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int i = lane + 32 * j;
+    if (i < width) o[i] = from_float<T>(acc[j] * inv);
+  }
+}
+
+// Action inputs (paged_model.py:502-523): bound[b, k] = states[b, max(slot,0)],
+// source_mask[b, k] = slot >= 0 && active; ctx_in[b] = [xfer_emb[max(x,0)],
+// source_reps[max(s,0)], mean of bound over the mask]; active[b] = x >= 0.
+template <typename T>
+__global__ void action_inputs_kernel(const T* states, int64_t state_stride, int slots,
+                                     const int64_t* xfer_ids, const int64_t* source_ids,
+                                     const int64_t* source_slots, int pattern, int width,
+                                     const float* xfer_emb, const float* source_reps, T* bound,
+                                     T* ctx_in, uint8_t* source_mask, uint8_t* active, int batch) {
+  const int b = blockIdx.x;
+  if (b >= batch) return;
+  const int64_t x = xfer_ids[b];
+  const bool act = x >= 0;
+  const int64_t s = source_ids[b] < 0 ? 0 : source_ids[b];
+  int count = 0;
+  for (int k = 0; k < pattern; ++k) count += (source_slots[(int64_t)b * pattern + k] >= 0 && act);
+  const float inv = 1.f / (float)(count > 0 ? count : 1);
+  if (threadIdx.x == 0) active[b] = act;
+  if (threadIdx.x < pattern) {
+    const int64_t slot = source_slots[(int64_t)b * pattern + threadIdx.x];
+    source_mask[(int64_t)b * pattern + threadIdx.x] = slot >= 0 && act;
+  }
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    float pool = 0.f;
+    for (int k = 0; k < pattern; ++k) {
+      const int64_t slot = source_slots[(int64_t)b * pattern + k];
+      const int64_t safe = slot < 0 ? 0 : slot;
+      const T v = states[((int64_t)b * slots + safe) * state_stride + i];
+      bound[((int64_t)b * pattern + k) * width + i] = v;
+      if (slot >= 0 && act) pool += to_float(v);
+    }
+    T* c = ctx_in + (int64_t)b * 3 * width;
+    c[i] = from_float<T>(xfer_emb[(x < 0 ? 0 : x) * width + i]);
+    c[width + i] = from_float<T>(source_reps[s * width + i]);
+    c[2 * width + i] = from_float<T>(pool * inv);
+  }
+}
+
+// token[b] = (raw[b] + position[len[b]]) * active[b]   (paged_model.py:524-525)
+template <typename T>
+__global__ void position_token_kernel(const T* raw, const float* position, const int32_t* lengths,
+                                      const uint8_t* active, T* token, int batch, int width) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)batch * width) return;
+  const int b = (int)(idx / width), i = (int)(idx % width);
+  const float v = active[b] ? to_float(raw[idx]) + position[(int64_t)lengths[b] * width + i] : 0.f;
+  token[idx] = from_float<T>(v);
+}
+
+// _update_live_nodes hidden layer (paged_model.py:223-238), per slot row:
+//   logits_k = q . key[b,k] / sqrt(W) (masked -1e4), attn = softmax_k,
+//   affinity = sigmoid(max_k logits),
+//   h = GELU(xa + sum_k attn_k * vw[b,k] + c[b])
+// with q = states W_query^T, xa = states W1[:, :W]^T (one GEMM, qxa row =
+// [q | xa]), vw[b,k] = (bound W_value^T) W1[:, W:2W]^T, c[b] = ctx W1[:, 2W:]^T + b1.
+template <typename T, int VPLQ, int VPLH>
+__global__ void __launch_bounds__(ROW_WARPS * 32) update_live_hidden_kernel(
+    const T* qxa, int64_t qxa_stride, const T* keys, const T* vw, const T* cvec,
+    const uint8_t* source_mask, int pattern, int64_t rows, int slots, int width, T* hidden,
+    int64_t hidden_stride, float* affinity) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t b = row / slots;
+  const T* q = qxa + row * qxa_stride;
+  float qv[VPLQ];
+#pragma unroll
+  for (int j = 0; j < VPLQ; ++j) {
+    const int i = lane + 32 * j;
+    qv[j] = i < width ? to_float(q[i]) : 0.f;
+  }
+  float logit[8];
+  const float scale = rsqrtf((float)width);
+  float mx = -INFINITY;
+  for (int k = 0; k < pattern; ++k) {
+    const T* kr = keys + (b * pattern + k) * width;
+    float d = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPLQ; ++j) {
+      const int i = lane + 32 * j;
+      if (i < width) d += qv[j] * to_float(kr[i]);
+    }
+    d = warp_sum(d) * scale;
+    if (!source_mask[b * pattern + k]) d = -1e4f;
+    logit[k] = d;
+    mx = fmaxf(mx, d);
+  }
+  float den = 0.f;
+  for (int k = 0; k < pattern; ++k) { logit[k] = __expf(logit[k] - mx); den += logit[k]; }
+  const float inv = 1.f / den;
+  if (lane == 0) affinity[row] = 1.f / (1.f + __expf(-mx));
+  const T* xa = q + width;
+  const int hw = 2 * width;
+  T* h = hidden + row * hidden_stride;
+#pragma unroll
+  for (int j = 0; j < VPLH; ++j) {
+    const int i = lane + 32 * j;
+    if (i < hw) {
+      float v = to_float(xa[i]) + to_float(cvec[b * hw + i]);
+      for (int k = 0; k < pattern; ++k) v += logit[k] * inv * to_float(vw[(b * pattern + k) * hw + i]);
+      h[i] = from_float<T>(gelu_exact(v));
+    }
+  }
+}
+
+// destination_state hidden layer (paged_model.py:592-601):
+//   h[b, j] = GELU(r[b] + type_table[type] + position_table[j]) for valid
+//   destinations, where r = raw W0[:, :W]^T + b0, type_table = gate_emb
+//   W0[:, W:2W]^T and position_table = pattern_position W0[:, 2W:]^T.
+template <typename T>
+__global__ void destination_hidden_kernel(const T* r, const float* type_table,
+                                          const float* pos_table, const int64_t* dest_slots,
+                                          const int64_t* dest_types, const uint8_t* active,
+                                          int pattern, int batch, int hw, T* hidden) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)batch * pattern * hw) return;
+  const int i = (int)(idx % hw);
+  const int64_t bj = idx / hw;
+  const int j = (int)(bj % pattern);
+  const int b = (int)(bj / pattern);
+  const bool valid = dest_slots[bj] >= 0 && active[b];
+  float v = 0.f;
+  if (valid) {
+    const int64_t t = dest_types[bj];
+    v = gelu_exact(to_float(r[(int64_t)b * hw + i]) + type_table[t * hw + i] + pos_table[(int64_t)j * hw + i]);
+  }
+  hidden[idx] = from_float<T>(v);
+}
+
+// Kill source slots then create destination slots (paged_model.py:569-604).
+template <typename T>
+__global__ void apply_slots_kernel(T* states, int64_t state_stride, uint8_t* live, int64_t* types,
+                                   int slots, const int64_t* source_slots,
+                                   const uint8_t* source_mask, int spattern,
+                                   const int64_t* dest_slots, const int64_t* dest_types,
+                                   const uint8_t* active, int dpattern, const T* created,
+                                   int width, int batch) {
+  const int b = blockIdx.x;
+  if (b >= batch) return;
+  for (int k = 0; k < spattern; ++k) {
+    if (!source_mask[(int64_t)b * spattern + k]) continue;
+    const int64_t slot = source_slots[(int64_t)b * spattern + k];
+    const int64_t row = (int64_t)b * slots + slot;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) states[row * state_stride + i] = from_float<T>(0.f);
+    if (threadIdx.x == 0) { live[row] = 0; types[row] = -1; }
+  }
+  __syncthreads();
+  if (!active[b]) return;
+  for (int j = 0; j < dpattern; ++j) {
+    const int64_t slot = dest_slots[(int64_t)b * dpattern + j];
+    if (slot < 0) continue;
+    const int64_t row = (int64_t)b * slots + slot;
+    const T* c = created + ((int64_t)b * dpattern + j) * width;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) states[row * state_stride + i] = c[i];
+    if (threadIdx.x == 0) { live[row] = 1; types[row] = dest_types[(int64_t)b * dpattern + j]; }
+  }
+}
+
+// match_logits epilogue (model.py:382-389): logits = acc / sqrt(R) + bias,
+// eligible = live && type == first_type[v], ineligible -> -1e4 (fp32 out).
+template <typename T>
+__global__ void match_logits_kernel(const T* acc, int64_t acc_stride, const float* source_bias,
+                                    const int64_t* first_types, const uint8_t* live,
+                                    const int64_t* types, int64_t rows, int num_sources,
+                                    float inv_sqrt_r, float* logits, uint8_t* eligible) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * num_sources) return;
+  const int64_t r = idx / num_sources;
+  const int v = (int)(idx % num_sources);
+  const bool e = live[r] && types[r] == first_types[v];
+  eligible[idx] = e;
+  logits[idx] = e ? to_float(acc[r * acc_stride + v]) * inv_sqrt_r + source_bias[v] : -1e4f;
+}
+
+// out[i] = in[index[i]] row by row; an input row of in_bytes is copied into
+// an output row of out_bytes and the tail (out_bytes > in_bytes) is filled
+// with fill_byte (0 for states and live flags, 0xff for -1 ids).
+__global__ void gather_beams_kernel(const char* in, char* out, const int64_t* index,
+                                    int64_t rows, int64_t in_bytes, int64_t out_bytes,
+                                    int fill_byte) {
+  const int64_t r = blockIdx.x;
+  if (r >= rows) return;
+  const char* s = in + index[r] * in_bytes;
+  char* d = out + r * out_bytes;
+  const int64_t copy = in_bytes < out_bytes ? in_bytes : out_bytes;
+  if ((copy & 15) == 0 && (in_bytes & 15) == 0 && (out_bytes & 15) == 0 &&
+      ((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+    for (int64_t v = threadIdx.x; v < copy / 16; v += blockDim.x)
+      reinterpret_cast<uint4*>(d)[v] = reinterpret_cast<const uint4*>(s)[v];
+  } else {
+    for (int64_t v = threadIdx.x; v < copy; v += blockDim.x) d[v] = s[v];
+  }
+  for (int64_t v = copy + threadIdx.x; v < out_bytes; v += blockDim.x) d[v] = (char)fill_byte;
+}
+
+// Port arrays from an edge list (model.py:402-418): relation = sp * 4 + dp.
+__global__ void edges_to_ports_kernel(const int64_t* eb, const int64_t* es, const int64_t* ed,
+                                      const int64_t* er, int64_t edges, int slots,
+                                      int32_t* out_node, int32_t* out_port, int32_t* in_node,
+                                      int32_t* in_port) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= edges) return;
+  const int64_t sp = er[e] / 4, dp = er[e] % 4;
+  const int64_t src = eb[e] * slots + es[e], dst = eb[e] * slots + ed[e];
+  out_node[src * 4 + sp] = (int32_t)ed[e];
+  out_port[src * 4 + sp] = (int32_t)dp;
+  in_node[dst * 4 + dp] = (int32_t)es[e];
+  in_port[dst * 4 + dp] = (int32_t)sp;
+}
+
+// ---------------------------------------------------------------------------
+inline int vpl_for(int width) {
+  const int v = (width + 31) / 32;
+  if (v <= 1) return 1;
+  if (v <= 2) return 2;
+  if (v <= 4) return 4;
+  if (v <= 8) return 8;
+  if (v <= 16) return 16;
+  if (v <= 32) return 32;
+  return -1;
+}
+
+}  // namespace grs
+
+using namespace grs;
+
+#define GRS_VPL_SWITCH(VAR, width, ...)            \
+  switch (vpl_for(width)) {                        \
+    case 1: { constexpr int VAR = 1; __VA_ARGS__; break; }  \
+    case 2: { constexpr int VAR = 2; __VA_ARGS__; break; }  \
+    case 4: { constexpr int VAR = 4; __VA_ARGS__; break; }  \
+    case 8: { constexpr int VAR = 8; __VA_ARGS__; break; }  \
+    case 16: { constexpr int VAR = 16; __VA_ARGS__; break; } \
+    case 32: { constexpr int VAR = 32; __VA_ARGS__; break; } \
+    default: return GRS_ERR_SHAPE;                 \
+  }
+
+#define GRS_DTYPE_SWITCH(T, dtype, ...)                                   \
+  if ((dtype) == GRS_DTYPE_F32) { using T = float; __VA_ARGS__; }          \
+  else if ((dtype) == GRS_DTYPE_BF16) { using T = __nv_bfloat16; __VA_ARGS__; } \
+  else return GRS_ERR_SHAPE;
+
+extern "C" int grs_add_layernorm(int dtype, const void* x, int64_t x_stride, const void* y,
+                                 int64_t y_stride, const float* scale, const float* gamma,
+                                 const float* beta, void* sum_out, int64_t sum_stride,
+                                 void* ln_out, int64_t ln_stride, const uint8_t* zero_row,
+                                 const uint8_t* zero_beam, const uint8_t* where_row,
+                                 const uint8_t* where_beam, const int32_t* where_len,
+                                 int64_t rows, int rows_per_beam, int width, float eps,
+                                 int zero_before, void* stream) {
+  if (rows <= 0) return GRS_OK;
+  if (rows_per_beam <= 0 || width <= 0) return GRS_ERR_SHAPE;
+  AddLnArgs a{x, x_stride, y, y_stride, scale, gamma, beta, sum_out, sum_stride, ln_out,
+              ln_stride, zero_row, zero_beam, where_row, where_beam, where_len, rows,
+              rows_per_beam, width, eps, zero_before};
+  const int grid = ceil_div(rows, ROW_WARPS);
+  GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
+      add_ln_kernel<T, V><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(a)))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_bias_gelu(int dtype, void* y, int64_t rows, int cols, int64_t stride,
+                             const float* bias, int apply_gelu, void* stream) {
+  if (rows <= 0) return GRS_OK;
+  const int64_t n = rows * cols;
+  GRS_DTYPE_SWITCH(T, dtype, bias_gelu_kernel<T><<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      (T*)y, rows, cols, stride, bias, apply_gelu))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_embed_initial(int dtype, const int64_t* types, int64_t rows, int width,
+                                 const float* gate_emb, const float* marker, void* states,
+                                 int64_t stride, uint8_t* live, void* stream) {
+  if (rows <= 0) return GRS_OK;
+  GRS_DTYPE_SWITCH(T, dtype, embed_initial_kernel<T><<<ceil_div(rows, ROW_WARPS), ROW_WARPS * 32, 0,
+                                                       (cudaStream_t)stream>>>(
+      types, rows, width, gate_emb, marker, (T*)states, stride, live))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride, const float* rel,
+                                   const int32_t* in_node, const int32_t* in_port,
+                                   const int32_t* out_node, const int32_t* out_port, int64_t rows,
+                                   int slots, int width, void* agg, int64_t agg_stride,
+                                   void* stream) {
+  if (rows <= 0) return GRS_OK;
+  if (slots <= 0) return GRS_ERR_SHAPE;
+  const int grid = ceil_div(rows, ROW_WARPS);
+  GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
+      graph_aggregate_kernel<T, V><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(
+          (const T*)fb, fb_stride, rel, in_node, in_port, out_node, out_port, rows, slots, width,
+          (T*)agg, agg_stride)))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_action_inputs(int dtype, const void* states, int64_t state_stride, int slots,
+                                 const int64_t* xfer_ids, const int64_t* source_ids,
+                                 const int64_t* source_slots, int pattern, int width,
+                                 const float* xfer_emb, const float* source_reps, void* bound,
+                                 void* ctx_in, uint8_t* source_mask, uint8_t* active, int batch,
+                                 void* stream) {
+  if (batch <= 0) return GRS_OK;
+  if (pattern > 32) return GRS_ERR_SHAPE;
+  GRS_DTYPE_SWITCH(T, dtype, action_inputs_kernel<T><<<batch, 128, 0, (cudaStream_t)stream>>>(
+      (const T*)states, state_stride, slots, xfer_ids, source_ids, source_slots, pattern, width,
+      xfer_emb, source_reps, (T*)bound, (T*)ctx_in, source_mask, active, batch))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_position_token(int dtype, const void* raw, const float* position,
+                                  const int32_t* lengths, const uint8_t* active, void* token,
+                                  int batch, int width, void* stream) {
+  if (batch <= 0) return GRS_OK;
+  const int64_t n = (int64_t)batch * width;
+  GRS_DTYPE_SWITCH(T, dtype, position_token_kernel<T><<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const T*)raw, position, lengths, active, (T*)token, batch, width))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_update_live_hidden(int dtype, const void* qxa, int64_t qxa_stride,
+                                      const void* keys, const void* vw, const void* cvec,
+                                      const uint8_t* source_mask, int pattern, int64_t rows,
+                                      int slots, int width, void* hidden, int64_t hidden_stride,
+                                      float* affinity, void* stream) {
+  if (rows <= 0) return GRS_OK;
+  if (pattern <= 0 || pattern > 8 || slots <= 0) return GRS_ERR_SHAPE;
+  const int grid = ceil_div(rows, ROW_WARPS);
+  const int vq = vpl_for(width), vh = vpl_for(2 * width);
+  if (vq < 0 || vh < 0) return GRS_ERR_SHAPE;
+#define GRS_ULH(VQ, VH)                                                                        \
+  if (vq == VQ && vh == VH) {                                                                  \
+    GRS_DTYPE_SWITCH(T, dtype, update_live_hidden_kernel<T, VQ, VH><<<grid, ROW_WARPS * 32, 0, \
+                                                                     (cudaStream_t)stream>>>(  \
+        (const T*)qxa, qxa_stride, (const T*)keys, (const T*)vw, (const T*)cvec, source_mask,  \
+        pattern, rows, slots, width, (T*)hidden, hidden_stride, affinity))                      \
+    GRS_CUDA_CHECK_LAUNCH();                                                                   \
+    return GRS_OK;                                                                             \
+  }
+  GRS_ULH(1, 2) GRS_ULH(2, 4) GRS_ULH(4, 8) GRS_ULH(8, 16) GRS_ULH(16, 32) GRS_ULH(1, 1)
+  GRS_ULH(2, 2) GRS_ULH(4, 4) GRS_ULH(8, 8) GRS_ULH(16, 16)
+#undef GRS_ULH
+  return GRS_ERR_SHAPE;
+}
+
+extern "C" int grs_destination_hidden(int dtype, const void* r, const float* type_table,
+                                      const float* pos_table, const int64_t* dest_slots,
+                                      const int64_t* dest_types, const uint8_t* active,
+                                      int pattern, int batch, int hidden_width, void* hidden,
+                                      void* stream) {
+  const int64_t n = (int64_t)batch * pattern * hidden_width;
+  if (n <= 0) return GRS_OK;
+  GRS_DTYPE_SWITCH(T, dtype, destination_hidden_kernel<T><<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const T*)r, type_table, pos_table, dest_slots, dest_types, active, pattern, batch,
+      hidden_width, (T*)hidden))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_apply_slots(int dtype, void* states, int64_t state_stride, uint8_t* live,
+                               int64_t* types, int slots, const int64_t* source_slots,
+                               const uint8_t* source_mask, int spattern, const int64_t* dest_slots,
+                               const int64_t* dest_types, const uint8_t* active, int dpattern,
+                               const void* created, int width, int batch, void* stream) {
+  if (batch <= 0) return GRS_OK;
+  GRS_DTYPE_SWITCH(T, dtype, apply_slots_kernel<T><<<batch, 128, 0, (cudaStream_t)stream>>>(
+      (T*)states, state_stride, live, types, slots, source_slots, source_mask, spattern,
+      dest_slots, dest_types, active, dpattern, (const T*)created, width, batch))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_match_logits(int dtype, const void* acc, int64_t acc_stride,
+                                const float* source_bias, const int64_t* first_types,
+                                const uint8_t* live, const int64_t* types, int64_t rows,
+                                int num_sources, float inv_sqrt_r, float* logits,
+                                uint8_t* eligible, void* stream) {
+  const int64_t n = rows * num_sources;
+  if (n <= 0) return GRS_OK;
+  GRS_DTYPE_SWITCH(T, dtype, match_logits_kernel<T><<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const T*)acc, acc_stride, source_bias, first_types, live, types, rows, num_sources,
+      inv_sqrt_r, logits, eligible))
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_gather_beams(const void* in, void* out, const int64_t* index, int64_t rows,
+                                int64_t in_bytes, int64_t out_bytes, int fill_byte,
+                                void* stream) {
+  if (rows <= 0) return GRS_OK;
+  if (in_bytes < 0 || out_bytes < 0) return GRS_ERR_SHAPE;
+  gather_beams_kernel<<<(unsigned)rows, 256, 0, (cudaStream_t)stream>>>(
+      (const char*)in, (char*)out, index, rows, in_bytes, out_bytes, fill_byte);
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_edges_to_ports(const int64_t* eb, const int64_t* es, const int64_t* ed,
+                                  const int64_t* er, int64_t edges, int slots, int32_t* out_node,
+                                  int32_t* out_port, int32_t* in_node, int32_t* in_port,
+                                  void* stream) {
+  if (edges <= 0) return GRS_OK;
+  edges_to_ports_kernel<<<ceil_div(edges, 256), 256, 0, (cudaStream_t)stream>>>(
+      eb, es, ed, er, edges, slots, out_node, out_port, in_node, in_port);
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}

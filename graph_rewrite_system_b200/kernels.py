@@ -1,0 +1,170 @@
+"""Thin typed wrappers over the model kernels of libgrs_b200.so.
+
+Each function takes torch CUDA tensors, checks the layout it needs and calls
+one C-ABI entry point on the current stream.  GEMMs are plain cuBLAS calls
+through ``torch.mm``/``torch.addmm`` (``linear``).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+P, I64, INT, F32 = _lib.c_ptr, _lib.c_i64, _lib.c_int, _lib.c_f32
+
+_lib.register("grs_add_layernorm", [INT, P, I64, P, I64, P, P, P, P, I64, P, I64, P, P, P, P, P,
+                                    I64, INT, INT, F32, INT, P])
+_lib.register("grs_bias_gelu", [INT, P, I64, INT, I64, P, INT, P])
+_lib.register("grs_embed_initial", [INT, P, I64, INT, P, P, P, I64, P, P])
+_lib.register("grs_graph_aggregate", [INT, P, I64, P, P, P, P, P, I64, INT, INT, P, I64, P])
+_lib.register("grs_action_inputs", [INT, P, I64, INT, P, P, P, INT, INT, P, P, P, P, P, P, INT, P])
+_lib.register("grs_position_token", [INT, P, P, P, P, P, INT, INT, P])
+_lib.register("grs_update_live_hidden", [INT, P, I64, P, P, P, P, INT, I64, INT, INT, P, I64, P, P])
+_lib.register("grs_destination_hidden", [INT, P, P, P, P, P, P, INT, INT, INT, P, P])
+_lib.register("grs_apply_slots", [INT, P, I64, P, P, INT, P, P, INT, P, P, P, INT, P, INT, INT, P])
+_lib.register("grs_match_logits", [INT, P, I64, P, P, P, P, I64, INT, F32, P, P, P])
+_lib.register("grs_gather_beams", [P, P, P, I64, I64, I64, INT, P])
+_lib.register("grs_edges_to_ports", [P, P, P, P, I64, INT, P, P, P, P, P])
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _lib.DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported activation dtype {t.dtype}") from None
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _row_stride(t: torch.Tensor) -> int:
+    if t.stride(-1) != 1:
+        raise ValueError("rows must be contiguous in their last dimension")
+    return t.stride(-2) if t.dim() >= 2 else t.shape[-1]
+
+
+def linear(x: torch.Tensor, weight_t: torch.Tensor, bias: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [M, K] @ weight_t [K, N] (+ bias) with cuBLAS."""
+    if bias is None:
+        return torch.mm(x, weight_t, out=out)
+    return torch.addmm(bias, x, weight_t, out=out)
+
+
+def add_layernorm(x, y=None, *, scale=None, gamma=None, beta=None, sum_out=None, ln_out=None,
+                  zero_row=None, zero_beam=None, where_row=None, where_beam=None,
+                  where_len=None, rows_per_beam=1, zero_before=False, eps=1e-5):
+    rows = x.shape[0]
+    width = x.shape[-1]
+    _lib.check(_lib.lib().grs_add_layernorm(
+        dtype_code(x), x.data_ptr(), _row_stride(x), _p(y), 0 if y is None else _row_stride(y),
+        _p(scale), _p(gamma), _p(beta), _p(sum_out), 0 if sum_out is None else _row_stride(sum_out),
+        _p(ln_out), 0 if ln_out is None else _row_stride(ln_out), _p(zero_row), _p(zero_beam),
+        _p(where_row), _p(where_beam), _p(where_len), rows, rows_per_beam, width, eps,
+        int(zero_before), stream()), "add_layernorm")
+
+
+def bias_gelu(y: torch.Tensor, bias: torch.Tensor | None, gelu: bool = True) -> torch.Tensor:
+    _lib.check(_lib.lib().grs_bias_gelu(dtype_code(y), y.data_ptr(), y.shape[0], y.shape[1],
+                                        _row_stride(y), _p(bias), int(gelu), stream()), "bias_gelu")
+    return y
+
+
+def embed_initial(types, gate_emb, marker, states, live):
+    rows = types.numel()
+    _lib.check(_lib.lib().grs_embed_initial(dtype_code(states), types.data_ptr(), rows,
+                                            states.shape[-1], gate_emb.data_ptr(), marker.data_ptr(),
+                                            states.data_ptr(), _row_stride(states), live.data_ptr(),
+                                            stream()), "embed_initial")
+
+
+def graph_aggregate(fb, rel, ports, slots, agg):
+    in_node, in_port, out_node, out_port = ports
+    _lib.check(_lib.lib().grs_graph_aggregate(
+        dtype_code(fb), fb.data_ptr(), _row_stride(fb), rel.data_ptr(), in_node.data_ptr(),
+        in_port.data_ptr(), out_node.data_ptr(), out_port.data_ptr(), fb.shape[0], slots,
+        agg.shape[-1], agg.data_ptr(), _row_stride(agg), stream()), "graph_aggregate")
+
+
+def action_inputs(states, xfer_ids, source_ids, source_slots, xfer_emb, source_reps, bound,
+                  ctx_in, source_mask, active):
+    b, s, w = states.shape
+    _lib.check(_lib.lib().grs_action_inputs(
+        dtype_code(states), states.data_ptr(), states.stride(1), s, xfer_ids.data_ptr(),
+        source_ids.data_ptr(), source_slots.data_ptr(), source_slots.shape[1], w,
+        xfer_emb.data_ptr(), source_reps.data_ptr(), bound.data_ptr(), ctx_in.data_ptr(),
+        source_mask.data_ptr(), active.data_ptr(), b, stream()), "action_inputs")
+
+
+def position_token(raw, position, lengths, active, token):
+    _lib.check(_lib.lib().grs_position_token(dtype_code(raw), raw.data_ptr(), position.data_ptr(),
+                                             lengths.data_ptr(), active.data_ptr(),
+                                             token.data_ptr(), raw.shape[0], raw.shape[1],
+                                             stream()), "position_token")
+
+
+def update_live_hidden(qxa, keys, vw, cvec, source_mask, slots, width, hidden, affinity):
+    _lib.check(_lib.lib().grs_update_live_hidden(
+        dtype_code(qxa), qxa.data_ptr(), _row_stride(qxa), keys.data_ptr(), vw.data_ptr(),
+        cvec.data_ptr(), source_mask.data_ptr(), source_mask.shape[1], qxa.shape[0], slots, width,
+        hidden.data_ptr(), _row_stride(hidden), affinity.data_ptr(), stream()), "update_live_hidden")
+
+
+def destination_hidden(r, type_table, pos_table, dest_slots, dest_types, active, hidden):
+    b, pattern = dest_slots.shape
+    _lib.check(_lib.lib().grs_destination_hidden(
+        dtype_code(r), r.data_ptr(), type_table.data_ptr(), pos_table.data_ptr(),
+        dest_slots.data_ptr(), dest_types.data_ptr(), active.data_ptr(), pattern, b,
+        r.shape[1], hidden.data_ptr(), stream()), "destination_hidden")
+
+
+def apply_slots(states, live, types, source_slots, source_mask, dest_slots, dest_types, active,
+                created):
+    b, s, w = states.shape
+    _lib.check(_lib.lib().grs_apply_slots(
+        dtype_code(states), states.data_ptr(), states.stride(1), live.data_ptr(), types.data_ptr(),
+        s, source_slots.data_ptr(), source_mask.data_ptr(), source_slots.shape[1],
+        dest_slots.data_ptr(), dest_types.data_ptr(), active.data_ptr(), dest_slots.shape[1],
+        created.data_ptr(), w, b, stream()), "apply_slots")
+
+
+def match_logits(acc, source_bias, first_types, live, types, inv_sqrt_r, logits, eligible):
+    rows = acc.shape[0]
+    _lib.check(_lib.lib().grs_match_logits(
+        dtype_code(acc), acc.data_ptr(), _row_stride(acc), source_bias.data_ptr(),
+        first_types.data_ptr(), live.data_ptr(), types.data_ptr(), rows, first_types.numel(),
+        inv_sqrt_r, logits.data_ptr(), eligible.data_ptr(), stream()), "match_logits")
+
+
+def gather_beams(src: torch.Tensor, index: torch.Tensor, out: torch.Tensor, fill_byte: int = 0):
+    """out[i] = src[index[i]] over the leading dim; trailing dims may differ in
+    their second size (slot padding), filled with fill_byte."""
+    rows = out.shape[0]
+    in_bytes = src[0].numel() * src.element_size() if src.shape[0] else 0
+    out_bytes = out[0].numel() * out.element_size() if rows else 0
+    if not src.is_contiguous() or not out.is_contiguous():
+        raise ValueError("gather_beams needs contiguous tensors")
+    _lib.check(_lib.lib().grs_gather_beams(src.data_ptr(), out.data_ptr(), index.data_ptr(), rows,
+                                           in_bytes, out_bytes, fill_byte, stream()),
+               "gather_beams")
+    return out
+
+
+def edges_to_ports(edge_batch, edge_src, edge_dst, edge_relation, batch, slots, device):
+    shape = (batch, slots, 4)
+    ports = [torch.full(shape, -1, device=device, dtype=torch.int32) for _ in range(4)]
+    out_node, out_port, in_node, in_port = ports
+    e = edge_batch.numel()
+    if e:
+        conv = lambda t: t.to(device=device, dtype=torch.int64).contiguous()
+        eb, es, ed, er = map(conv, (edge_batch, edge_src, edge_dst, edge_relation))
+        _lib.check(_lib.lib().grs_edges_to_ports(eb.data_ptr(), es.data_ptr(), ed.data_ptr(),
+                                                 er.data_ptr(), e, slots, out_node.data_ptr(),
+                                                 out_port.data_ptr(), in_node.data_ptr(),
+                                                 in_port.data_ptr(), stream()), "edges_to_ports")
+    return in_node, in_port, out_node, out_port

@@ -146,6 +146,87 @@ GRS_API int grs_proposals_rank_static(const int64_t* batch_ids, const int64_t* s
                                       int64_t* out_next_gate, int64_t* out_count,
                                       int64_t* out_metrics, int32_t* status, void* stream);
 
+/* ---- paged action model: row-wise fused kernels ---------------------------
+ * Activation dtype GRS_DTYPE_F32 or GRS_DTYPE_BF16; parameters fp32; rows are
+ * B*S slot rows (rows_per_beam = S) or B token rows (rows_per_beam = 1).
+ *
+ * grs_add_layernorm: residual + LayerNorm with the masks of the reference:
+ *   s = x + scale[row]*y; zc = zero_row && zero_beam; wc = where_row &&
+ *   where_beam && where_len>0; zero_before: s = zc ? s : 0; sum_out = s;
+ *   ln_out = wc ? LN(s) : x, then (if !zero_before) zc ? . : 0.
+ *   Covers InitialGraphLayer's norm (model.py:52-53), the node readout
+ *   (paged_model.py:375-379), _update_live_nodes (paged_model.py:239-241) and
+ *   the causal residual/norm chain (paged_model.py:77-93, 555-558). */
+GRS_API int grs_add_layernorm(int dtype, const void* x, int64_t x_stride, const void* y,
+                              int64_t y_stride, const float* scale, const float* gamma,
+                              const float* beta, void* sum_out, int64_t sum_stride, void* ln_out,
+                              int64_t ln_stride, const uint8_t* zero_row,
+                              const uint8_t* zero_beam, const uint8_t* where_row,
+                              const uint8_t* where_beam, const int32_t* where_len, int64_t rows,
+                              int rows_per_beam, int width, float eps, int zero_before,
+                              void* stream);
+/* y = GELU(y + bias) in place (exact erf GELU, nn.GELU()); GELU optional. */
+GRS_API int grs_bias_gelu(int dtype, void* y, int64_t rows, int cols, int64_t stride,
+                          const float* bias, int apply_gelu, void* stream);
+/* s0 embedding (paged_model.py:246-250). */
+GRS_API int grs_embed_initial(int dtype, const int64_t* types, int64_t rows, int width,
+                              const float* gate_emb, const float* marker, void* states,
+                              int64_t stride, uint8_t* live, void* stream);
+/* InitialGraphLayer aggregation (model.py:36-51) over port arrays
+ * in/out_node, in/out_port int32 [B, S, 4]; fb = [forward | backward]
+ * messages [B*S, 2W]; rel fp32 [32, W]; writes the degree-normalised sum. */
+GRS_API int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride, const float* rel,
+                                const int32_t* in_node, const int32_t* in_port,
+                                const int32_t* out_node, const int32_t* out_port, int64_t rows,
+                                int slots, int width, void* agg, int64_t agg_stride,
+                                void* stream);
+/* Bound-slot gather, pooling and action-context input (paged_model.py:494-523). */
+GRS_API int grs_action_inputs(int dtype, const void* states, int64_t state_stride, int slots,
+                              const int64_t* xfer_ids, const int64_t* source_ids,
+                              const int64_t* source_slots, int pattern, int width,
+                              const float* xfer_emb, const float* source_reps, void* bound,
+                              void* ctx_in, uint8_t* source_mask, uint8_t* active, int batch,
+                              void* stream);
+/* token = (raw + action_position[length]) * active (paged_model.py:524-525). */
+GRS_API int grs_position_token(int dtype, const void* raw, const float* position,
+                               const int32_t* lengths, const uint8_t* active, void* token,
+                               int batch, int width, void* stream);
+/* _update_live_nodes bound-key attention + action_delta hidden layer
+ * (paged_model.py:223-238) for every slot row; writes the GELU hidden
+ * [rows, 2W] and the affinity sigmoid(max logit) [rows]. */
+GRS_API int grs_update_live_hidden(int dtype, const void* qxa, int64_t qxa_stride,
+                                   const void* keys, const void* vw, const void* cvec,
+                                   const uint8_t* source_mask, int pattern, int64_t rows,
+                                   int slots, int width, void* hidden, int64_t hidden_stride,
+                                   float* affinity, void* stream);
+/* destination_state hidden layer per (beam, destination) (paged_model.py:592-601). */
+GRS_API int grs_destination_hidden(int dtype, const void* r, const float* type_table,
+                                   const float* pos_table, const int64_t* dest_slots,
+                                   const int64_t* dest_types, const uint8_t* active, int pattern,
+                                   int batch, int hidden_width, void* hidden, void* stream);
+/* Kill source slots, create destination slots (paged_model.py:569-604). */
+GRS_API int grs_apply_slots(int dtype, void* states, int64_t state_stride, uint8_t* live,
+                            int64_t* types, int slots, const int64_t* source_slots,
+                            const uint8_t* source_mask, int spattern, const int64_t* dest_slots,
+                            const int64_t* dest_types, const uint8_t* active, int dpattern,
+                            const void* created, int width, int batch, void* stream);
+/* match_logits epilogue (model.py:382-389): fp32 logits + eligible mask. */
+GRS_API int grs_match_logits(int dtype, const void* acc, int64_t acc_stride,
+                             const float* source_bias, const int64_t* first_types,
+                             const uint8_t* live, const int64_t* types, int64_t rows,
+                             int num_sources, float inv_sqrt_r, float* logits, uint8_t* eligible,
+                             void* stream);
+/* Beam reindex (index_select of the beam dimension, paged_rollout_benchmark.py
+ * :497-499 / :1192-1195) with slot padding: out row i = in row index[i]
+ * (in_bytes), tail up to out_bytes filled with fill_byte. */
+GRS_API int grs_gather_beams(const void* in, void* out, const int64_t* index, int64_t rows,
+                             int64_t in_bytes, int64_t out_bytes, int fill_byte, void* stream);
+/* Port arrays from an edge list (model.py:402-418); arrays pre-filled with -1. */
+GRS_API int grs_edges_to_ports(const int64_t* edge_batch, const int64_t* edge_src,
+                               const int64_t* edge_dst, const int64_t* edge_relation,
+                               int64_t edges, int slots, int32_t* out_node, int32_t* out_port,
+                               int32_t* in_node, int32_t* in_port, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

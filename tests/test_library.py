@@ -36,6 +36,7 @@ def test_python_bindings_cover_header():
     import graph_rewrite_system_b200.paged_attention  # noqa: F401
     import graph_rewrite_system_b200.paged_cache  # noqa: F401
     import graph_rewrite_system_b200.gpu_proposals  # noqa: F401
+    import graph_rewrite_system_b200.kernels  # noqa: F401
 
     bound = set(_lib.exported_symbols())
     missing = [n for n in declared_entry_points() if n not in bound]
