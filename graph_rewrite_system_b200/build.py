@@ -23,7 +23,7 @@ LIBRARY = PACKAGE / "libgrs_b200.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
-    "-O3", "-lineinfo", "-std=c++17", "--use_fast_math", "-Xcompiler", "-fPIC",
+    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
     "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
 ]
 

@@ -36,9 +36,9 @@ __global__ void prop_count_kernel(const int64_t* __restrict__ sources, int64_t c
   int cnt = 0, all = 0;
   if (i < c) {
     const int64_t s = sources[i];
-    if (s < 0 || s >= num_sources) {
+    if (s >= num_sources) {
       set_status(status, GRS_ERR_SHAPE);
-    } else {
+    } else if (s >= 0) {  // source < 0 marks a padding row (no candidate)
       cnt = xfer_counts[s];
       all = all_counts[s];
     }

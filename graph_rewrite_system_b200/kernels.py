@@ -168,3 +168,38 @@ def edges_to_ports(edge_batch, edge_src, edge_dst, edge_relation, batch, slots, 
                                                  out_port.data_ptr(), in_node.data_ptr(),
                                                  in_port.data_ptr(), stream()), "edges_to_ports")
     return in_node, in_port, out_node, out_port
+
+
+_lib.register("grs_select_candidates", [P, P, P, INT, INT, INT, INT, F32, F32, F32, F32, F32, F32,
+                                        P, P, P, P, P, P])
+_lib.register("grs_structural_decode", [P, P, INT, P, P, P, P, P, P, P, P, P, P, P, P, INT, INT,
+                                        P, P, P, I64, P, P, INT, P])
+
+
+def select_candidates(logits, eligible, distance, k, groups, out_batch, out_source, out_anchor,
+                      out_prob, out_score=None):
+    b, s, ns = logits.shape
+    near, far = groups["near"], groups["far"]
+    _lib.check(_lib.lib().grs_select_candidates(
+        logits.data_ptr(), eligible.data_ptr(), distance.data_ptr(), b, s, ns, k,
+        float(near["scale"]), float(near["bias"]), float(near["raw_threshold"]),
+        float(far["scale"]), float(far["bias"]), float(far["raw_threshold"]),
+        out_batch.data_ptr(), out_source.data_ptr(), out_anchor.data_ptr(), out_prob.data_ptr(),
+        _p(out_score), stream()), "select_candidates")
+
+
+def structural_decode(types, live, ports, rules, batch_ids, sources, anchors, bindings, valid,
+                      clear_invalid=False):
+    """rules: dict of the model's int64 rule buffers."""
+    in_node, in_port, out_node, out_port = ports
+    slots = types.shape[1]
+    pe = rules["pattern_edges"]
+    _lib.check(_lib.lib().grs_structural_decode(
+        types.data_ptr(), live.data_ptr(), slots, out_node.data_ptr(), out_port.data_ptr(),
+        in_node.data_ptr(), in_port.data_ptr(), rules["source_types"].data_ptr(),
+        rules["source_lengths"].data_ptr(), rules["binding_child"].data_ptr(),
+        rules["binding_parent"].data_ptr(), rules["binding_parent_port"].data_ptr(),
+        rules["binding_child_port"].data_ptr(), rules["binding_direction"].data_ptr(),
+        pe.data_ptr(), pe.shape[1], bindings.shape[1], batch_ids.data_ptr(), sources.data_ptr(),
+        anchors.data_ptr(), sources.numel(), bindings.data_ptr(), valid.data_ptr(),
+        int(clear_invalid), stream()), "structural_decode")

@@ -517,3 +517,27 @@ class PagedActionBindingModel(nn.Module):
                        gate_types.to(torch.int64).contiguous(), 1.0 / math.sqrt(self.retrieval_width),
                        logits, eligible)
         return logits, eligible
+
+    # ---- structural decode ------------------------------------------------------
+    def rule_tables(self) -> dict[str, torch.Tensor]:
+        return {name: getattr(self, name).contiguous() for name in (
+            "source_types", "source_lengths", "binding_child", "binding_parent",
+            "binding_parent_port", "binding_child_port", "binding_direction", "pattern_edges")}
+
+    @torch.no_grad()
+    def structural_decode(self, batch, gate_types, live, batch_ids, source_ids, anchor_slots,
+                          ports=None):
+        """Port-following decoder for complete ordered bindings (model.py:391-478).
+        Returns (bindings int64 [n, max_pattern], valid bool [n])."""
+        b, s = gate_types.shape
+        dev = gate_types.device
+        if ports is None:
+            ports = self._ports(batch, b, s, dev)
+        n = batch_ids.numel()
+        bindings = torch.empty(n, self.max_pattern, device=dev, dtype=torch.int64)
+        valid = torch.empty(n, device=dev, dtype=torch.bool)
+        sources = source_ids.to(torch.int64).clone()
+        K.structural_decode(gate_types.to(torch.int64).contiguous(), live.contiguous(), ports,
+                            self.rule_tables(), batch_ids.to(torch.int64).contiguous(), sources,
+                            anchor_slots.to(torch.int64).contiguous(), bindings, valid)
+        return bindings, valid

@@ -102,7 +102,8 @@ GRS_API int grs_cache_check_lengths(const int32_t* nblocks, const int32_t* lengt
                                     int page_size, int32_t* status, void* stream);
 
 /* ---- proposals: gpu_proposals.py:69-192 (build_gpu_proposals) -----------
- * Candidates (int64 batch_ids, sources; float32 probabilities) expand through
+ * Candidates (int64 batch_ids, sources; float32 probabilities; a source < 0
+ * marks a padding row that expands to nothing) expand through
  * the CSR rule index (GpuRuleIndex, gpu_proposals.py:20-50; int32 arrays);
  * the stable per-parent cap and global rank select <= global_cap expanded
  * actions: out_row (candidate row), out_xfer, out_next_gate (int64
@@ -226,6 +227,37 @@ GRS_API int grs_edges_to_ports(const int64_t* edge_batch, const int64_t* edge_sr
                                const int64_t* edge_dst, const int64_t* edge_relation,
                                int64_t edges, int slots, int32_t* out_node, int32_t* out_port,
                                int32_t* in_node, int32_t* in_port, void* stream);
+
+/* ---- candidates: threshold_inference.py:208-297, model.py:391-478 --------
+ * grs_select_candidates: per beam row, near/far calibration by rewrite
+ * distance (near = distance <= 2), raw-logit threshold, eligibility, then the
+ * k best calibrated scores sorted (score desc, flat index asc).  Outputs
+ * [batch, k] rows: out_batch (row), out_source (-1 = no candidate),
+ * out_anchor, out_prob = sigmoid(score), optional out_score.
+ * logits fp32 / eligible uint8 [batch, slots, num_sources]; distance int32
+ * [batch, slots]; k <= 2048. */
+GRS_API int grs_select_candidates(const float* logits, const uint8_t* eligible,
+                                  const int32_t* distance, int batch, int slots, int num_sources,
+                                  int k, float near_scale, float near_bias, float near_thr,
+                                  float far_scale, float far_bias, float far_thr,
+                                  int64_t* out_batch, int64_t* out_source, int64_t* out_anchor,
+                                  float* out_prob, float* out_score, void* stream);
+/* grs_structural_decode: complete ordered bindings by port following
+ * (model.py:391-478) for `count` candidates (sources < 0 are skipped);
+ * bindings int64 [count, max_pattern] (-1 padded), valid uint8 [count];
+ * clear_invalid sets sources[c] = -1 for invalid candidates.  Port arrays
+ * int32 [B, slots, 4]; rule tables are the model's buffers. */
+GRS_API int grs_structural_decode(const int64_t* types, const uint8_t* live, int slots,
+                                  const int32_t* out_node, const int32_t* out_port,
+                                  const int32_t* in_node, const int32_t* in_port,
+                                  const int64_t* source_types, const int64_t* source_lengths,
+                                  const int64_t* child, const int64_t* parent,
+                                  const int64_t* parent_port, const int64_t* child_port,
+                                  const int64_t* direction, const int64_t* pattern_edges,
+                                  int max_edges, int max_pattern, const int64_t* batch_ids,
+                                  int64_t* sources, const int64_t* anchors, int64_t count,
+                                  int64_t* bindings, uint8_t* valid, int clear_invalid,
+                                  void* stream);
 
 #ifdef __cplusplus
 }

@@ -171,6 +171,102 @@ def _pack_proposals(cand, gates, s2x, deltas, num_sources, max_inc, cap, gcap, p
     )
 
 
+def topology_case(*, seed=0, beams=90, depth=7, qubits=4, gates=40, per_step=120):
+    """Lazy topology + raw-fingerprint dedup through the reference's own
+    lazy_child (indexed backend) and accept loop (paged_rollout_benchmark.py
+    :1013-1046), on seeded proposals drawn from every structurally valid
+    (source, anchor) of every parent, shuffled, with injected repeats
+    (duplicates) and bindings through dead slots (invalid)."""
+    import json
+    import random
+
+    import beam_search_benchmark as bsb
+    import incremental_graph as ig
+    import lazy_rollout_benchmark as lrb
+    from graph_rewrite_system_b200 import synthetic
+
+    rng = random.Random(seed)
+    rules = synthetic.synthetic_rules()
+    s2x, deltas = rules.source_to_xfers(), rules.gate_deltas()
+    src_pat = tuple(ig.parse_pattern(p) for p in rules.xfer_sources)
+    dst_pat = tuple(ig.parse_pattern(p) for p in rules.xfer_destinations)
+    circuit = synthetic.random_circuit(qubits, gates, seed)
+    snapshot = circuit.snapshot()
+    beam = [bsb.BeamState(graph=None, snapshot=snapshot, guid_to_slot={}, next_slot=gates,
+                          last_touched={}, rewrite_distance={n[0]: 5 for n in snapshot["nodes"]},
+                          previous_preferred=set(), local_streak=0, gate_count=gates, depth=0,
+                          history=(), topology_index=lrb.indexed_topology(snapshot))]
+    seen = {lrb.raw_topology_hash(snapshot)}
+    out = {"circuit_nodes": [list(n) for n in circuit.nodes],
+           "circuit_edges": [list(e) for e in circuit.edges], "steps": []}
+    for step in range(depth):
+        proposals = []
+        for parent, state in enumerate(beam):
+            topo = state.topology_index
+            inc = ig.IncrementalCircuit({"nodes": [(s_, t_, -1) for s_, t_ in topo.nodes.items()],
+                                         "edges": list(topo.edges)})
+            for source_id, pattern in enumerate(rules.source_patterns):
+                ops = ig.parse_pattern(pattern)
+                for anchor in sorted(topo.nodes):
+                    binding = ig.structural_binding(inc, ops, anchor)
+                    if binding is None:
+                        continue
+                    for xfer in s2x[source_id]:
+                        if deltas[xfer] <= 1:
+                            proposals.append(bsb.Proposal(parent, xfer, anchor, binding,
+                                                          rng.random(),
+                                                          state.gate_count + deltas[xfer]))
+        rng.shuffle(proposals)
+        proposals = proposals[:per_step]
+        for _ in range(len(proposals) // 10):       # repeats -> duplicates
+            proposals.insert(rng.randrange(len(proposals) + 1), rng.choice(proposals))
+        for _ in range(len(proposals) // 20):       # dead slot -> invalid
+            p = rng.choice(proposals)
+            dead = rng.randrange(beam[p.parent].next_slot, beam[p.parent].next_slot + 50)
+            binding = (dead,) + tuple(p.binding[1:])
+            proposals.insert(rng.randrange(len(proposals) + 1),
+                             bsb.Proposal(p.parent, p.xfer_id, p.anchor_slot, binding,
+                                          p.probability, p.next_gate_count))
+        records = []
+        attempted = invalid = duplicates = 0
+        for index, proposal in enumerate(proposals):
+            if len(records) >= beams:
+                break
+            attempted += 1
+            child, fingerprint, is_dup = lrb.lazy_child(beam[proposal.parent], proposal, src_pat,
+                                                        dst_pat, False, "raw", seen, "indexed")
+            if is_dup:
+                duplicates += 1
+                continue
+            if child is None:
+                invalid += 1
+                continue
+            seen.add(fingerprint)
+            records.append((child, index))
+        records.sort(key=lambda r: (r[0].gate_count, len(r[0].history)))
+        records = records[:beams]
+        children = []
+        for child, index in records:
+            topo = child.topology_index
+            children.append({
+                "proposal": index,
+                "nodes": sorted([int(a), int(b)] for a, b in topo.nodes.items()),
+                "edges": sorted(list(map(int, e)) for e in topo.edges),
+                "next_slot": int(child.next_slot),
+                "last_touched": [int(x) for x in child.last_touched],
+                "rewrite_distance": [int(x) for x in child.rewrite_distance],
+                "previous_preferred": sorted(int(x) for x in child.previous_preferred),
+                "local_streak": int(child.local_streak), "gate_count": int(child.gate_count),
+                "depth": int(child.depth)})
+        out["steps"].append({
+            "proposals": [[p.parent, p.xfer_id, p.anchor_slot, list(p.binding),
+                           p.next_gate_count] for p in proposals],
+            "attempted": attempted, "invalid": invalid, "duplicates": duplicates,
+            "children": children})
+        beam = [r[0] for r in records]
+    return {"json": np.array(json.dumps(out))}
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
@@ -198,6 +294,8 @@ def main() -> None:
             np.savez_compressed(HERE / f"proposals_{name}.npz", **case)
     if not only or "model" in only:
         np.savez_compressed(HERE / "model_cpu_equivalence.npz", **model_case(args.reference))
+    if not only or "topology" in only:
+        np.savez_compressed(HERE / "topology_accept.npz", **topology_case())
     print("golden fixtures written to", HERE)
 
 

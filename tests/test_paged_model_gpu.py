@@ -110,3 +110,58 @@ def test_paged_model_bf16_within_tolerance(cuda_device):
         np.linalg.norm(g["logits"][eligible]) < 2e-2
     for key in ("advance_live", "advance_types"):
         assert np.array_equal(out[key].cpu().numpy(), g[key]), key
+
+
+def test_structural_decode_and_candidates_match_reference(cuda_device):
+    from graph_rewrite_system_b200 import synthetic
+    from graph_rewrite_system_b200.threshold_inference import threshold_candidate_tensors
+
+    g = load_golden("model_cpu_equivalence.npz")
+    rules, cfg = synthetic.small_rules(), synthetic.CPU_EQUIVALENCE_MODEL
+    model = build_model(cuda_device, torch.float32, rules, cfg, int(g["seed"]))
+    batch = {k[len("batch_"):]: torch.from_numpy(v).to(cuda_device) for k, v in g.items()
+             if k.startswith("batch_")}
+    types = torch.from_numpy(g["advance_types"]).to(cuda_device)
+    live = torch.from_numpy(g["advance_live"]).to(cuda_device)
+    d = lambda k: torch.from_numpy(g[k]).to(cuda_device)
+    bindings, valid = model.structural_decode(batch, types, live, d("decode_batch"),
+                                              d("decode_sources"), d("decode_anchors"))
+    assert np.array_equal(bindings.cpu().numpy(), g["decode_bindings"])
+    assert np.array_equal(valid.cpu().numpy(), g["decode_valid"])
+    cand = threshold_candidate_tensors(model, batch, d("logits"), d("eligible"),
+                                       synthetic.SELECT_ALL_THRESHOLDS,
+                                       max_candidates_per_state=24)
+    for k in ("batch_ids", "sources", "anchors", "bindings"):
+        assert np.array_equal(getattr(cand, k).cpu().numpy(), g["candidates_" + k]), k
+    np.testing.assert_allclose(cand.probabilities.cpu().numpy(), g["candidates_probabilities"],
+                               rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("k", [1, 7, 80, 500])
+def test_select_candidates_topk_with_ties(cuda_device, k):
+    """Random bf16-rounded logits (many exact ties) vs the oracle's stable order."""
+    from graph_rewrite_system_b200 import kernels as K
+    from graph_rewrite_system_b200.synthetic import SELECT_ALL_THRESHOLDS
+
+    gen = torch.Generator().manual_seed(k)
+    b, s, ns = 6, 97, 13
+    logits = torch.randn(b, s, ns, generator=gen).bfloat16().float()
+    eligible = torch.rand(b, s, ns, generator=gen) > 0.4
+    eligible[2] = False
+    logits = logits.masked_fill(~eligible, -1e4)
+    distance = torch.randint(0, 6, (b, s), generator=gen, dtype=torch.int32)
+    flat = logits.flatten(1).masked_fill(~eligible.flatten(1), -torch.inf)
+    order = torch.argsort(flat, dim=1, descending=True, stable=True)[:, :k]
+    scores = torch.gather(flat, 1, order)
+    dev = cuda_device
+    n = b * k
+    outs = [torch.empty(n, device=dev, dtype=torch.int64) for _ in range(3)]
+    prob = torch.empty(n, device=dev)
+    K.select_candidates(logits.to(dev), eligible.to(dev), distance.to(dev), k,
+                        SELECT_ALL_THRESHOLDS["groups"], *outs, prob)
+    _, src, anc = (o.cpu().view(b, k) for o in outs)
+    present = scores.isfinite()
+    assert torch.equal(src >= 0, present)
+    assert torch.equal(anc[present] * ns + src[present], order[present])
+    np.testing.assert_allclose(prob.cpu().view(b, k)[present].numpy(),
+                               scores[present].sigmoid().numpy(), rtol=1e-6)
