@@ -6,6 +6,13 @@
 Workloads (seeded synthetic inputs; the reference's hwb6 circuit, rule set
 and checkpoint are not available):
 
+* ``rollout`` (default): the full beam-search step - synthetic 6-qubit,
+  259-gate circuit, width-256 / 8-head / 4 causal + 4 readout-graph-layer
+  model with seeded random weights, bf16, beam 1000, depth 64 (W warm-up
+  levels then K timed levels; defaults 4 + 60), page 16, 80 candidates per
+  state ranked to 16 per parent and 16000 globally.  A step is one search
+  level.  The decode-attention microbenchmark below is measured in the same
+  run and reported under ``paged_attention``.
 * ``decode-attention``: the shared-prefix paged decode microbenchmark -
   512 beams, one query token each, 8 heads x 32, bf16, 381 shared s0 node
   keys, 64 action K/V entries per beam in pages of 16, block tables from a
@@ -270,6 +277,111 @@ def cpu_decode_attention(w, device, *, sample_beams=64, repeats=None, budget_s=1
                       f"scaled linearly to the full step"}
 
 
+# ---------------------------------------------------------------------------
+# rollout workload
+# ---------------------------------------------------------------------------
+def build_rollout(device, *, beam_size=1000, depth=64, seed=0):
+    from graph_rewrite_system_b200 import synthetic
+    from graph_rewrite_system_b200.paged_model import PagedActionBindingModel
+    from graph_rewrite_system_b200.rollout import DeviceBeamSearch
+    from graph_rewrite_system_b200.synthetic import parameter_shapes
+
+    rules = synthetic.synthetic_rules()
+    cfg = synthetic.ROLLOUT_MODEL
+    model = PagedActionBindingModel(
+        rules, num_xfers=rules.num_xfers, width=cfg.width, retrieval_width=cfg.retrieval_width,
+        graph_layers=cfg.graph_layers, action_layers=cfg.action_layers,
+        action_heads=cfg.action_heads, max_sequence_length=cfg.max_sequence_length,
+        readout_graph_layers=cfg.readout_graph_layers, dropout=0.0,
+        compute_dtype=torch.bfloat16)
+    state = model.state_dict()
+    for name, value in synthetic.deterministic_parameters(parameter_shapes(cfg, rules),
+                                                          seed).items():
+        state[name] = torch.from_numpy(value)
+    model.load_state_dict(state)
+    model = model.to(device).eval()
+    rc = synthetic.RolloutConfig(beam_size=beam_size, depth=depth, seed=seed)
+    circuit = synthetic.random_circuit(rc.num_qubits, rc.num_gates, seed)
+    return DeviceBeamSearch(model, rules, circuit, rc, device), rc
+
+
+def run_rollout(args, world, rank, device):
+    from graph_rewrite_system_b200.rollout import StageTimer
+
+    depth = args.warmup + args.steps
+    search, rc = build_rollout(device, depth=depth, seed=0)
+    stream = torch.cuda.current_stream(device)
+    # one full untimed search first (module load, allocator warm-up)
+    search.run(min(depth, args.warmup + 2))
+    search.reset()
+    for _ in range(args.warmup):
+        search.step()
+    torch.cuda.synchronize(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    timer = StageTimer()
+    search.timer = timer
+    barrier(world, device)
+    torch.cuda.synchronize(device)
+    done = 0
+    with ClockSampler(device.index) as clocks:
+        for i in range(args.steps):
+            starts[i].record(stream)
+            row = search.step()
+            ends[i].record(stream)
+            done += 1
+            if row is None:
+                break
+        torch.cuda.synchronize(device)
+    timer.collect()
+    search.timer = None
+    barrier(world, device)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts[:done], ends[:done])]
+    total_ms = max_over_ranks(sum(step_ms), world, device)
+    search.check()
+    rows = search.rows
+    last = rows[-1]
+    # end to end through the public API: host circuit in, full search, beam summary out
+    e2e_start = torch.cuda.Event(enable_timing=True)
+    e2e_end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    e2e_start.record(stream)
+    search.run(depth)
+    summary = search.beam_summary()
+    e2e_end.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world, device)
+    h2d = (len(search.circuit.nodes) * 2 + len(search.circuit.edges) * 4) * 8
+    d2h = 11 * 8 + len(summary["gate_count"]) * 8 * 4 // max(1, depth)
+    stage_ms = {k: v / done for k, v in sorted(timer.totals.items())}
+    line = {
+        "metric": METRIC, "value": world * done * 1e3 / total_ms, "unit": "steps/s",
+        "n_gpus": world, "steps": done, "warmup": args.warmup,
+        "ms_per_step": total_ms / done, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "full rollout step: synthetic 6-qubit 259-gate circuit, "
+                               "d_model 256, 8 heads, 4 causal + 4 message-passing layers, "
+                               "random init, beam 1000, depth 64, page 16, 80 candidates -> "
+                               "16 per parent -> 16000 proposals",
+                   "beam": rc.beam_size, "depth": depth, "timed_levels": f"{args.warmup + 1}"
+                   f"..{args.warmup + done}", "page_size": rc.page_size,
+                   "l2": "inputs larger than L2 (beam state ~0.2 GB bf16 per activation)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "e2e": {"value": world * depth * 1e3 / e2e_ms, "unit": "steps/s",
+                "h2d_bytes_per_step": h2d // depth, "d2h_bytes_per_step": d2h,
+                "scope": "DeviceBeamSearch.run(): s0 upload, all levels, beam summary download"},
+        "search": {"last_level": {k: getattr(last, k) for k in (
+                       "input_states", "output_states", "best_speculative_gate_count",
+                       "predicted_actions", "eligible_actions_before_parent_cap",
+                       "proposals_after_caps", "attempted_actions", "accepted_actions",
+                       "invalid_structural_actions", "duplicate_speculative_successors",
+                       "allocated_cache_pages", "logical_cache_pages")},
+                   "stage_ms_per_step": stage_ms},
+        "clocks": clocks.summary(),
+    }
+    return line
+
+
 def run_reference(args, world, rank):
     """--impl reference: the CPU oracle on the same workload (rank 0 only)."""
     if rank != 0:
@@ -303,10 +415,10 @@ def run_reference(args, world, rank):
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
-    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--steps", type=int, default=60)
+    parser.add_argument("--warmup", type=int, default=4)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    parser.add_argument("--workload", choices=("decode-attention",), default="decode-attention")
+    parser.add_argument("--workload", choices=("rollout", "decode-attention"), default="rollout")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
     if args.warmup < 3:
@@ -321,7 +433,14 @@ def main() -> None:
     world, rank, local = dist_setup(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    line = run_decode_attention(args, world, rank, device)
+    if args.workload == "rollout":
+        line = run_rollout(args, world, rank, device)
+        attn_args = argparse.Namespace(steps=20, warmup=5, no_cpu_baseline=True)
+        attention = run_decode_attention(attn_args, world, rank, device)
+        line["paged_attention"] = {k: attention[k] for k in ("value", "unit", "ms_per_step",
+                                                             "roofline", "config")}
+    else:
+        line = run_decode_attention(args, world, rank, device)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import ctypes
 from pathlib import Path
+import re
 
 import torch
 
@@ -35,31 +36,65 @@ c_int = ctypes.c_int
 c_ptr = ctypes.c_void_p
 c_f32 = ctypes.c_float
 
-# argtypes per entry point; kept beside the header so a mismatch is obvious.
-_SIGNATURES: dict[str, list] = {
-    "grs_version": [],
-    "grs_paged_attention": [
-        c_int, c_ptr, c_i64, c_i64, c_i64,
-        c_ptr, c_ptr, c_i64, c_i64, c_i64,
-        c_ptr, c_i64, c_ptr,
-        c_ptr, c_ptr, c_i64, c_i64, c_ptr,
-        c_ptr, c_ptr, c_i64,
-        c_ptr, c_i64, c_i64, c_i64,
-        c_int, c_int, c_int, c_int, c_int, c_int, c_ptr,
-    ],
-}
+HEADER_PATH = Path(__file__).resolve().parent.parent / "include" / "grs_b200.h"
+
+_C_TYPES = {"int": c_int, "int64_t": c_i64, "float": c_f32, "double": ctypes.c_double}
 
 
-def register(name: str, argtypes: list) -> None:
-    """Declare an additional entry point's ctypes signature."""
-    _SIGNATURES[name] = argtypes
-    if _lib is not None:
-        fn = getattr(_lib, name)
-        fn.argtypes = argtypes
-        fn.restype = c_int
+def _parse_header(text: str) -> dict[str, tuple[object, list]]:
+    """(restype, argtypes) of every GRS_API declaration: pointers become
+    c_void_p, scalars their ctypes type."""
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    out = {}
+    for ret, name, params in re.findall(
+            r"GRS_API\s+((?:const\s+)?[\w]+\s*\**)\s*(grs_\w+)\s*\(([^)]*)\)\s*;", text):
+        args = []
+        params = params.strip()
+        if params and params != "void":
+            for param in params.split(","):
+                param = " ".join(param.replace("*", " * ").split())
+                if "*" in param:
+                    args.append(c_ptr)
+                    continue
+                base = param.replace("const ", "").split()[0]
+                if base not in _C_TYPES:
+                    raise ImportError(f"unsupported parameter type in {name}: {param}")
+                args.append(_C_TYPES[base])
+        ret = ret.replace("const", "").strip()
+        if "*" in ret:
+            restype = ctypes.c_char_p if ret.startswith("char") else c_ptr
+        else:
+            restype = _C_TYPES[ret.split()[0]]
+        out[name] = (restype, args)
+    return out
 
 
-def lib() -> ctypes.CDLL:
+_SIGNATURES: dict[str, tuple[object, list]] = _parse_header(HEADER_PATH.read_text())
+
+
+class _Bound:
+    """The library's entry points with header-derived signatures; a call with
+    the wrong number of arguments raises instead of reaching the C ABI."""
+
+    def __init__(self, handle: ctypes.CDLL):
+        self.handle = handle
+        for name, (restype, argtypes) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+            setattr(self, name, self._checked(name, fn, len(argtypes)))
+
+    @staticmethod
+    def _checked(name, fn, count):
+        def call(*args):
+            if len(args) != count:
+                raise TypeError(f"{name} takes {count} arguments ({len(args)} given)")
+            return fn(*args)
+        call.__name__ = name
+        return call
+
+
+def lib() -> _Bound:
     global _lib
     if _lib is None:
         if not LIBRARY_PATH.exists():
@@ -67,12 +102,7 @@ def lib() -> ctypes.CDLL:
                 f"{LIBRARY_PATH} is missing: build it with "
                 "`python -m graph_rewrite_system_b200.build` (no fallback exists)"
             )
-        handle = ctypes.CDLL(str(LIBRARY_PATH))
-        for name, argtypes in _SIGNATURES.items():
-            fn = getattr(handle, name)
-            fn.argtypes = argtypes
-            fn.restype = ctypes.c_char_p if name == "grs_version" else c_int
-        _lib = handle
+        _lib = _Bound(ctypes.CDLL(str(LIBRARY_PATH)))
     return _lib
 
 

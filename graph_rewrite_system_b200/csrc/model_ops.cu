@@ -135,20 +135,21 @@ template <typename T, int VPL>
 __global__ void __launch_bounds__(ROW_WARPS * 32) graph_aggregate_kernel(
     const T* fb, int64_t fb_stride, const float* rel, const int32_t* in_node,
     const int32_t* in_port, const int32_t* out_node, const int32_t* out_port, int64_t rows,
-    int slots, int width, T* agg, int64_t agg_stride) {
+    int slots, int port_slots, int width, T* agg, int64_t agg_stride) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int64_t beam_base = (row / slots) * slots;
+  const int64_t prow = (row / slots) * port_slots + row % slots;
   float acc[VPL];
 #pragma unroll
   for (int j = 0; j < VPL; ++j) acc[j] = 0.f;
   int deg = 0;
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const int src = in_node[row * 4 + p];
+    const int src = in_node[prow * 4 + p];
     if (src >= 0) {
-      const int r = in_port[row * 4 + p] * 4 + p;
+      const int r = in_port[prow * 4 + p] * 4 + p;
       const T* f = fb + (beam_base + src) * fb_stride;
       const float* e = rel + (int64_t)r * width;
 #pragma unroll
@@ -158,9 +159,9 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) graph_aggregate_kernel(
       }
       ++deg;
     }
-    const int dst = out_node[row * 4 + p];
+    const int dst = out_node[prow * 4 + p];
     if (dst >= 0) {
-      const int r = 16 + p * 4 + out_port[row * 4 + p];
+      const int r = 16 + p * 4 + out_port[prow * 4 + p];
       const T* bk = fb + (beam_base + dst) * fb_stride + width;
       const float* e = rel + (int64_t)r * width;
 #pragma unroll
@@ -466,15 +467,15 @@ extern "C" int grs_embed_initial(int dtype, const int64_t* types, int64_t rows, 
 extern "C" int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride, const float* rel,
                                    const int32_t* in_node, const int32_t* in_port,
                                    const int32_t* out_node, const int32_t* out_port, int64_t rows,
-                                   int slots, int width, void* agg, int64_t agg_stride,
-                                   void* stream) {
+                                   int slots, int port_slots, int width, void* agg,
+                                   int64_t agg_stride, void* stream) {
   if (rows <= 0) return GRS_OK;
-  if (slots <= 0) return GRS_ERR_SHAPE;
+  if (slots <= 0 || port_slots < slots) return GRS_ERR_SHAPE;
   const int grid = ceil_div(rows, ROW_WARPS);
   GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
       graph_aggregate_kernel<T, V><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(
-          (const T*)fb, fb_stride, rel, in_node, in_port, out_node, out_port, rows, slots, width,
-          (T*)agg, agg_stride)))
+          (const T*)fb, fb_stride, rel, in_node, in_port, out_node, out_port, rows, slots,
+          port_slots, width, (T*)agg, agg_stride)))
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }

@@ -20,21 +20,6 @@ import torch
 from . import _lib
 from .types import BeamState, CandidateTensors, Proposal
 
-_lib.register("grs_proposals_workspace_bytes", [_lib.c_i64, _lib.c_i64])
-_lib.register("grs_proposals_rank", [
-    _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_i64, _lib.c_ptr, _lib.c_i64,
-    _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_int,
-    _lib.c_i64, _lib.c_int, _lib.c_i64, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr,
-    _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_i64, _lib.c_ptr, _lib.c_ptr,
-])
-# Allocation-free variant (same arguments minus the workspace pointer/size);
-# its scratch is a fixed array inside the library.
-_lib.register("grs_proposals_rank_static", [
-    _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_i64, _lib.c_ptr, _lib.c_i64,
-    _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_int,
-    _lib.c_i64, _lib.c_int, _lib.c_i64, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr,
-    _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr,
-])
 
 
 @dataclass(frozen=True)

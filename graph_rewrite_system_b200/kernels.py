@@ -10,21 +10,7 @@ import torch
 
 from . import _lib
 
-P, I64, INT, F32 = _lib.c_ptr, _lib.c_i64, _lib.c_int, _lib.c_f32
 
-_lib.register("grs_add_layernorm", [INT, P, I64, P, I64, P, P, P, P, I64, P, I64, P, P, P, P, P,
-                                    I64, INT, INT, F32, INT, P])
-_lib.register("grs_bias_gelu", [INT, P, I64, INT, I64, P, INT, P])
-_lib.register("grs_embed_initial", [INT, P, I64, INT, P, P, P, I64, P, P])
-_lib.register("grs_graph_aggregate", [INT, P, I64, P, P, P, P, P, I64, INT, INT, P, I64, P])
-_lib.register("grs_action_inputs", [INT, P, I64, INT, P, P, P, INT, INT, P, P, P, P, P, P, INT, P])
-_lib.register("grs_position_token", [INT, P, P, P, P, P, INT, INT, P])
-_lib.register("grs_update_live_hidden", [INT, P, I64, P, P, P, P, INT, I64, INT, INT, P, I64, P, P])
-_lib.register("grs_destination_hidden", [INT, P, P, P, P, P, P, INT, INT, INT, P, P])
-_lib.register("grs_apply_slots", [INT, P, I64, P, P, INT, P, P, INT, P, P, P, INT, P, INT, INT, P])
-_lib.register("grs_match_logits", [INT, P, I64, P, P, P, P, I64, INT, F32, P, P, P])
-_lib.register("grs_gather_beams", [P, P, P, I64, I64, I64, INT, P])
-_lib.register("grs_edges_to_ports", [P, P, P, P, I64, INT, P, P, P, P, P])
 
 
 def dtype_code(t: torch.Tensor) -> int:
@@ -84,11 +70,13 @@ def embed_initial(types, gate_emb, marker, states, live):
 
 
 def graph_aggregate(fb, rel, ports, slots, agg):
+    """ports: (in_node, in_port, out_node, out_port) int32 [B, port_slots, 4]."""
     in_node, in_port, out_node, out_port = ports
     _lib.check(_lib.lib().grs_graph_aggregate(
         dtype_code(fb), fb.data_ptr(), _row_stride(fb), rel.data_ptr(), in_node.data_ptr(),
         in_port.data_ptr(), out_node.data_ptr(), out_port.data_ptr(), fb.shape[0], slots,
-        agg.shape[-1], agg.data_ptr(), _row_stride(agg), stream()), "graph_aggregate")
+        in_node.shape[1], agg.shape[-1], agg.data_ptr(), _row_stride(agg), stream()),
+        "graph_aggregate")
 
 
 def action_inputs(states, xfer_ids, source_ids, source_slots, xfer_emb, source_reps, bound,
@@ -170,10 +158,6 @@ def edges_to_ports(edge_batch, edge_src, edge_dst, edge_relation, batch, slots, 
     return in_node, in_port, out_node, out_port
 
 
-_lib.register("grs_select_candidates", [P, P, P, INT, INT, INT, INT, F32, F32, F32, F32, F32, F32,
-                                        P, P, P, P, P, P])
-_lib.register("grs_structural_decode", [P, P, INT, P, P, P, P, P, P, P, P, P, P, P, P, INT, INT,
-                                        P, P, P, I64, P, P, INT, P])
 
 
 def select_candidates(logits, eligible, distance, k, groups, out_batch, out_source, out_anchor,

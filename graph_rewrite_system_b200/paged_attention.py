@@ -62,7 +62,9 @@ def paged_attention(
         if ck.stride(2) != 1 or cv.stride() != ck.stride():
             ck, cv = ck.contiguous(), cv.contiguous()
         ck_sb, ck_sh = ck.stride(0), ck.stride(1)
-        valid = current_valid.to(torch.uint8).contiguous()
+        valid = current_valid
+        if valid.dtype not in (torch.uint8, torch.bool) or not valid.is_contiguous():
+            valid = valid.to(torch.uint8).contiguous()
     sk = sv = None
     num_shared = 0
     if shared_key is not None:

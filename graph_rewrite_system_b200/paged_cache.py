@@ -27,21 +27,6 @@ import torch
 
 from . import _lib
 
-_lib.register("grs_cache_init", [_lib.c_ptr] * 4 + [_lib.c_int, _lib.c_ptr])
-_lib.register("grs_cache_append", [
-    _lib.c_int, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_int, _lib.c_ptr, _lib.c_i64,
-    _lib.c_ptr, _lib.c_int, _lib.c_int, _lib.c_ptr, _lib.c_i64, _lib.c_ptr, _lib.c_int,
-    _lib.c_ptr, _lib.c_ptr, _lib.c_int, _lib.c_int, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr,
-    _lib.c_int, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr,
-    _lib.c_ptr,
-])
-_lib.register("grs_cache_release", [
-    _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_ptr, _lib.c_int, _lib.c_ptr, _lib.c_i64,
-    _lib.c_ptr, _lib.c_int, _lib.c_int, _lib.c_int, _lib.c_ptr, _lib.c_ptr,
-])
-_lib.register("grs_cache_check_lengths", [
-    _lib.c_ptr, _lib.c_ptr, _lib.c_int, _lib.c_int, _lib.c_ptr, _lib.c_ptr,
-])
 
 
 @dataclass(frozen=True)

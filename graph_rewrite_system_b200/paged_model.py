@@ -419,6 +419,29 @@ class PagedActionBindingModel(nn.Module):
         gate_types = gate_types.to(torch.int64).contiguous()
         if int(past_lengths.max().item() if past_lengths.numel() else 0) >= self.max_sequence_length:
             raise ValueError("incremental prefix exceeds max_sequence_length")
+        next_states, next_live, next_types, new_keys, new_values, action = self.advance_device(
+            states, live, gate_types, xfer_ids, source_ids, source_slots, destination_slots,
+            destination_types, paged_key_cache, paged_value_cache, block_table, past_lengths)
+        next_mask = None
+        if return_mask:
+            max_past = int(past_lengths.max().item()) if b else 0
+            history = torch.arange(max_past, device=dev).unsqueeze(0) < past_lengths.unsqueeze(1)
+            next_mask = torch.cat((history, xfer_ids.ge(0).unsqueeze(1)), 1)
+        return next_states, next_live, next_types, new_keys, new_values, action, next_mask
+
+    @torch.no_grad()
+    def advance_device(self, states, live, gate_types, xfer_ids, source_ids, source_slots,
+                       destination_slots, destination_types, paged_key_cache, paged_value_cache,
+                       block_table, past_lengths):
+        """One-token step without host synchronisation: states [B, S, W] already
+        hold every referenced slot; ids int64, past_lengths int32 on the device.
+        Returns (next_states, next_live, next_types, new_keys [L,B,H,D],
+        new_values, action_token)."""
+        w, W = self.prepare(), self.width
+        dev, dt = states.device, self.compute_dtype
+        b = states.shape[0]
+        h = self.action_heads
+        hd = W // h
         s = states.shape[1]
         pattern = source_slots.shape[1]
         bound = torch.empty(b, pattern, W, device=dev, dtype=dt)
@@ -431,8 +454,9 @@ class PagedActionBindingModel(nn.Module):
         raw = K.linear(hidden, w["ac3_t"], w["ac3_b"])
         token = torch.empty_like(raw)
         K.position_token(raw, w["action_position"], past_lengths, active, token)
-        valid = active.to(torch.uint8)
-        new_keys, new_values = [], []
+        valid = active
+        new_keys = torch.empty(self.action_layers_count, b, h, hd, device=dev, dtype=dt)
+        new_values = torch.empty_like(new_keys)
         ln = torch.empty_like(token)
         token2 = torch.empty_like(token)
         for layer in range(self.action_layers_count):
@@ -450,21 +474,15 @@ class PagedActionBindingModel(nn.Module):
             f3 = K.linear(f0, w[p + "f3_t"], w[p + "f3_b"])
             token = torch.empty_like(token2)
             K.add_layernorm(token2, f3, sum_out=token, zero_beam=active, zero_before=True)
-            new_keys.append(k)
-            new_values.append(v)
+            new_keys[layer].copy_(k)
+            new_values[layer].copy_(v)
         action = torch.empty_like(token)
         K.add_layernorm(token, gamma=w["out_norm_w"], beta=w["out_norm_b"], ln_out=action,
                         zero_beam=active)
         next_states, next_live, next_types = self._update_and_apply(
             states, live, gate_types, bound, source_mask, raw, active, source_slots,
             destination_slots, destination_types)
-        next_mask = None
-        if return_mask:
-            max_past = int(past_lengths.max().item()) if b else 0
-            history = torch.arange(max_past, device=dev).unsqueeze(0) < past_lengths.unsqueeze(1)
-            next_mask = torch.cat((history, active.unsqueeze(1)), 1)
-        return (next_states, next_live, next_types, torch.stack(new_keys), torch.stack(new_values),
-                action, next_mask)
+        return next_states, next_live, next_types, new_keys, new_values, action
 
     def _update_and_apply(self, states, live, gate_types, bound, source_mask, raw, active,
                           source_slots, destination_slots, destination_types):

@@ -1,0 +1,302 @@
+"""Device-resident beam search: the loop of paged_rollout_benchmark.py:898-1207
+without Quartz (no exact refresh or audit), every stage on the GPU.
+
+One search level (``step``):
+
+1. paged node readout + readout graph over the device port graph
+   (paged_model_matches, :243-386; replaces the host collation of
+   tensorized_batch.py);
+2. match logits, near/far threshold, per-state top-k and structural decode
+   into a padded candidate table (threshold_candidate_tensors);
+3. expansion, per-parent cap and global rank (build_gpu_proposals);
+4. rewrite planning with XOR fingerprints, first-occurrence dedup against
+   the global seen set, accept the first beam_size, stable sort by gate count
+   (the lazy_child accept loop, :1013-1046);
+5. child topology materialisation with the BFS rewrite distance;
+6. one-token model advance of the children, readout K/V projection, paged
+   cache append (fork/COW) and release of the parents (advance_selected,
+   :390-556).
+
+The host synchronises once per level, after the accept, to read a small
+summary (accepted count, metrics, the next slot extent) that sizes the next
+launches.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+import math
+import time
+
+import torch
+
+from . import _lib
+from . import kernels as K
+from .gpu_proposals import GpuRuleIndex, rank_proposals_device
+from .paged_cache import PagedKVCache
+from .paged_model import PagedActionBindingModel
+from .synthetic import (Circuit, RolloutConfig, RuleMetadata, SELECT_ALL_THRESHOLDS)
+from .threshold_inference import select_candidates_device
+from .topology import TopologyBuffers, initial_topology, xfer_table
+
+
+def _round_up(v: int, m: int) -> int:
+    return (v + m - 1) // m * m
+
+
+def _pow2_at_least(v: int) -> int:
+    return 1 << max(1, int(v - 1).bit_length())
+
+
+@dataclass
+class StepRow:
+    """Per-level record with the reference's step-row field names (:1239-1276)."""
+
+    step: int
+    input_states: int
+    output_states: int
+    best_speculative_gate_count: int
+    predicted_actions: int
+    eligible_actions_before_parent_cap: int
+    proposals_after_caps: int
+    attempted_actions: int
+    accepted_actions: int
+    invalid_structural_actions: int
+    duplicate_speculative_successors: int
+    allocated_cache_pages: int
+    logical_cache_pages: int
+    page_sharing_ratio: float
+
+
+class StageTimer:
+    """CUDA events at stage boundaries on the current stream (the device-side
+    counterpart of the reference's --profile-stages, :268-273)."""
+
+    def __init__(self):
+        self.marks: list[tuple[str, torch.cuda.Event]] = []
+        self.totals: dict[str, float] = {}
+
+    def mark(self, name: str) -> None:
+        event = torch.cuda.Event(enable_timing=True)
+        event.record()
+        self.marks.append((name, event))
+
+    def collect(self) -> None:
+        """Accumulate the closed intervals (call after a synchronisation)."""
+        for (name, start), (_, end) in zip(self.marks, self.marks[1:]):
+            self.totals[name] = self.totals.get(name, 0.0) + start.elapsed_time(end)
+        self.marks = self.marks[-1:] if self.marks else []
+
+    def reset(self) -> None:
+        self.marks, self.totals = [], {}
+
+
+class DeviceBeamSearch:
+    """Beam search over rewrite sequences with the state resident in HBM."""
+
+    def __init__(self, model: PagedActionBindingModel, rules: RuleMetadata, circuit: Circuit,
+                 config: RolloutConfig, device, thresholds: dict = SELECT_ALL_THRESHOLDS):
+        self.model, self.rules, self.circuit, self.cfg = model, rules, circuit, config
+        self.device = torch.device(device)
+        self.thresholds = thresholds
+        dev = self.device
+        self.s0_slots = max(s for s, _ in circuit.nodes) + 1
+        self.max_dst = max(len(d) for d in rules.destination_gate_types)
+        self.max_src = max(len(s) for s in rules.source_gate_types)
+        self.slot_cap = _round_up(self.s0_slots + config.depth * max(self.max_dst, 1), 8)
+        self.topology = [TopologyBuffers(config.beam_size, self.slot_cap, dev) for _ in range(2)]
+        self.table = xfer_table(rules, dev)
+        self.xfer_to_source = torch.tensor(rules.xfer_to_source, device=dev, dtype=torch.int64)
+        self.rule_index = GpuRuleIndex.build(rules.source_to_xfers(), rules.gate_deltas(),
+                                             rules.num_sources, config.max_gate_increase, dev)
+        hd = model.width // model.action_heads
+        self.cache = PagedKVCache(layers=model.action_layers_count, capacity=config.cache_pages,
+                                  page_size=config.page_size, heads=model.action_heads,
+                                  head_width=hd, model_width=model.width, device=dev,
+                                  dtype=model.compute_dtype)
+        self.seen_capacity = _pow2_at_least(4 * (1 + config.depth * config.beam_size))
+        self.step_capacity = _pow2_at_least(2 * config.global_cap)
+        self.seen = torch.zeros(self.seen_capacity, device=dev, dtype=torch.int64)
+        self.step_keys = torch.empty(self.step_capacity, device=dev, dtype=torch.int64)
+        self.step_first = torch.empty(self.step_capacity, device=dev, dtype=torch.int32)
+        self.status = torch.zeros(1, device=dev, dtype=torch.int32)
+        self.summary = torch.zeros(6, device=dev, dtype=torch.int64)
+        self.rows: list[StepRow] = []
+        self.timer: StageTimer | None = None
+
+    def _mark(self, name: str) -> None:
+        if self.timer is not None:
+            self.timer.mark(name)
+
+    # ---- state ---------------------------------------------------------------
+    @torch.no_grad()
+    def reset(self) -> None:
+        """Beam = [s0] with an empty prefix (paged_rollout_benchmark.py:774-856)."""
+        dev, model = self.device, self.model
+        nodes, edges = self.circuit.nodes, self.circuit.edges
+        s = _round_up(self.s0_slots, 8)
+        types = torch.full((1, s), -1, dtype=torch.int64)
+        for slot, gate in nodes:
+            types[0, slot] = gate
+        e = torch.tensor(edges, dtype=torch.int64).reshape(-1, 4)
+        batch = {"initial_types": types.to(dev),
+                 "edge_batch": torch.zeros(e.shape[0], dtype=torch.int64, device=dev),
+                 "edge_src": e[:, 0].to(dev), "edge_dst": e[:, 1].to(dev),
+                 "edge_relation": (e[:, 2] * 4 + e[:, 3]).to(dev)}
+        self.states, self.live, self.types = model.initialize_incremental(batch)
+        self.topo = initial_topology(self.topology[0], nodes, edges, s)
+        self.current = 0
+        self.block_table = torch.zeros(1, 1, device=dev, dtype=torch.int32)
+        self.lengths = torch.zeros(1, device=dev, dtype=torch.int32)
+        self.seen.zero_()
+        _lib.check(_lib.lib().grs_topology_seen_insert(
+            self.topo.fingerprint.data_ptr(), 1, self.seen.data_ptr(), self.seen_capacity,
+            self.status.data_ptr(), K.stream()), "seen_insert")
+        self.beams, self.slots, self.depth = 1, s, 0
+        self.rows = []
+
+    # ---- one level --------------------------------------------------------------
+    @torch.no_grad()
+    def step(self) -> StepRow | None:
+        cfg, model, dev = self.cfg, self.model, self.device
+        b, s, depth = self.beams, self.slots, self.depth
+        topo = self.topo
+        ports = topo.ports()
+        # 1-2. readout and match logits
+        self._mark("readout")
+        readout, _, _ = model.readout_incremental(
+            self.states, self.live, self.types, readout_key_cache=self.cache.readout_keys,
+            readout_value_cache=self.cache.readout_values, block_table=self.block_table,
+            lengths=self.lengths, ports=ports)
+        self._mark("match_logits")
+        logits, eligible = model.match_logits(readout, self.live, self.types)
+        self._mark("candidates")
+        cand = select_candidates_device(model, self.types, self.live, ports, topo.distance, logits,
+                                        eligible, self.thresholds, cfg.max_candidates_per_state)
+        # 3. proposals (effective parent cap of paged_rollout_benchmark.py:963-966)
+        cap = max(cfg.per_parent_cap, math.ceil(cfg.beam_size / max(1, b)) * 2)
+        self._mark("proposals")
+        ranked = rank_proposals_device(cand["batch_ids"], cand["sources"], cand["probabilities"],
+                                       topo.gate, self.rule_index, per_parent_cap=cap,
+                                       global_cap=cfg.global_cap, status=self.status)
+        # 4. plan + accept
+        gcap = cfg.global_cap
+        valid = torch.empty(gcap, device=dev, dtype=torch.uint8)
+        fp = torch.empty(gcap, device=dev, dtype=torch.int64)
+        classes = torch.empty(gcap, device=dev, dtype=torch.uint8)
+        child_proposal = torch.empty(cfg.beam_size, device=dev, dtype=torch.int64)
+        cb = cand["bindings"]
+        stream = K.stream()
+        lib = _lib.lib()
+        self._mark("plan_accept")
+        _lib.check(lib.grs_topology_plan(
+            gcap, ranked.count.data_ptr(), ranked.rows.data_ptr(), ranked.xfer_ids.data_ptr(),
+            ranked.next_gate.data_ptr(), cand["batch_ids"].data_ptr(), cb.data_ptr(), cb.shape[1],
+            self.table.data_ptr(), topo.types.data_ptr(), topo.out_node.data_ptr(),
+            topo.out_port.data_ptr(), topo.in_node.data_ptr(), topo.in_port.data_ptr(), s,
+            topo.next_slot.data_ptr(), topo.fingerprint.data_ptr(), valid.data_ptr(), fp.data_ptr(),
+            self.status.data_ptr(), stream), "topology_plan")
+        _lib.check(lib.grs_topology_accept(
+            gcap, ranked.count.data_ptr(), valid.data_ptr(), fp.data_ptr(),
+            ranked.next_gate.data_ptr(), cfg.beam_size, self.step_keys.data_ptr(),
+            self.step_first.data_ptr(), self.step_capacity, self.seen.data_ptr(),
+            self.seen_capacity, classes.data_ptr(), child_proposal.data_ptr(),
+            self.summary.data_ptr(), ranked.rows.data_ptr(), ranked.xfer_ids.data_ptr(),
+            cand["batch_ids"].data_ptr(), self.table.data_ptr(), topo.next_slot.data_ptr(),
+            self.status.data_ptr(), stream), "topology_accept")
+        # one synchronisation per level
+        self._mark("host_sync")
+        host = torch.cat((self.summary, ranked.count, ranked.metrics,
+                          self.cache.allocated_pages_tensor().long(), self.status.long())).cpu()
+        (accepted, attempted, invalid, dup, extent, best, proposals, predicted, eligible_n,
+         allocated, status) = host.tolist()
+        if status:
+            self.status.zero_()
+            _lib.check(int(status), "beam search step")
+        row = StepRow(depth + 1, b, accepted, best, predicted, eligible_n, proposals, attempted,
+                      accepted, invalid, dup, allocated, 0, 0.0)
+        if not accepted:
+            self.rows.append(row)
+            return None
+        s_new = max(s, _round_up(int(extent), 8))
+        # 5. child topology
+        self._mark("materialize")
+        nxt = self.topology[1 - self.current].state(accepted, s_new)
+        i64 = dict(device=dev, dtype=torch.int64)
+        a_parent, a_xfer, a_source = (torch.empty(accepted, **i64) for _ in range(3))
+        a_src = torch.empty(accepted, self.max_src, **i64)
+        a_dst = torch.empty(accepted, max(self.max_dst, 1), **i64)
+        a_dst_types = torch.empty_like(a_dst)
+        _lib.check(lib.grs_topology_materialize(
+            accepted, child_proposal.data_ptr(), self.summary.data_ptr(), ranked.rows.data_ptr(),
+            ranked.xfer_ids.data_ptr(), ranked.next_gate.data_ptr(), fp.data_ptr(),
+            cand["batch_ids"].data_ptr(), cand["anchors"].data_ptr(), cb.data_ptr(), cb.shape[1],
+            self.table.data_ptr(), self.xfer_to_source.data_ptr(), s, s_new,
+            topo.types.data_ptr(), topo.out_node.data_ptr(), topo.out_port.data_ptr(),
+            topo.in_node.data_ptr(), topo.in_port.data_ptr(), topo.touched.data_ptr(),
+            topo.preferred.data_ptr(), topo.next_slot.data_ptr(), topo.streak.data_ptr(),
+            nxt.types.data_ptr(), nxt.out_node.data_ptr(), nxt.out_port.data_ptr(),
+            nxt.in_node.data_ptr(), nxt.in_port.data_ptr(), nxt.touched.data_ptr(),
+            nxt.preferred.data_ptr(), nxt.distance.data_ptr(), nxt.next_slot.data_ptr(),
+            nxt.streak.data_ptr(), nxt.gate.data_ptr(), nxt.fingerprint.data_ptr(),
+            a_parent.data_ptr(), a_xfer.data_ptr(), a_source.data_ptr(), a_src.data_ptr(),
+            a_src.shape[1], a_dst.data_ptr(), a_dst_types.data_ptr(), a_dst.shape[1], depth,
+            self.status.data_ptr(), stream), "topology_materialize")
+        # 6. model advance of the children, cache append, release the parents
+        self._mark("advance")
+        w = model.width
+        states_par = torch.empty(accepted, s_new, w, device=dev, dtype=model.compute_dtype)
+        K.gather_beams(self.states, a_parent, states_par)
+        live_par = torch.empty(accepted, s_new, device=dev, dtype=torch.bool)
+        K.gather_beams(self.live, a_parent, live_par)
+        types_par = torch.empty(accepted, s_new, **i64)
+        K.gather_beams(self.types, a_parent, types_par, fill_byte=0xFF)
+        table_par = torch.empty(accepted, self.block_table.shape[1], device=dev, dtype=torch.int32)
+        K.gather_beams(self.block_table, a_parent, table_par)
+        lengths_par = torch.empty(accepted, device=dev, dtype=torch.int32)
+        K.gather_beams(self.lengths, a_parent, lengths_par)
+        states, live, types, new_k, new_v, action = model.advance_device(
+            states_par, live_par, types_par, a_xfer, a_source, a_src, a_dst, a_dst_types,
+            self.cache.keys, self.cache.values, table_par, lengths_par)
+        rk, rv = model.project_action_readout_kv(action)
+        self._mark("cache_append_release")
+        child_cols = -(-(depth + 1) // cfg.page_size)
+        child_table, child_lengths = self.cache.append_device(
+            table_par, lengths_par, new_k, new_v, action, rk, rv, child_cols=child_cols)
+        self.cache.release_device(self.block_table, self.lengths)
+        self.states, self.live, self.types = states, live, types
+        self.block_table, self.lengths = child_table, child_lengths
+        self.topo, self.current = nxt, 1 - self.current
+        self.last_actions = (a_parent, a_xfer, a_src)
+        self.beams, self.slots, self.depth = accepted, s_new, depth + 1
+        row.logical_cache_pages = accepted * child_cols
+        self._mark("end")
+        self.rows.append(row)
+        return row
+
+    def check(self) -> None:
+        code = int(self.status.item())
+        if code:
+            self.status.zero_()
+            _lib.check(code, "beam search")
+        self.cache.check_status()
+
+    @torch.no_grad()
+    def run(self, depth: int | None = None) -> list[StepRow]:
+        self.reset()
+        for _ in range(depth or self.cfg.depth):
+            if self.step() is None:
+                break
+        self.check()
+        return self.rows
+
+    # ---- inspection -------------------------------------------------------------
+    def last_children(self) -> list[tuple[int, int, tuple[int, ...]]]:
+        """(parent, xfer, binding) of the beams produced by the last step."""
+        parent, xfer, src = (t.tolist() for t in self.last_actions)
+        return [(p, x, tuple(v for v in b if v >= 0)) for p, x, b in zip(parent, xfer, src)]
+
+    def beam_summary(self) -> dict:
+        """Gate counts, next slots and fingerprints of the current beam (host)."""
+        return {"gate_count": self.topo.gate.tolist(), "next_slot": self.topo.next_slot.tolist(),
+                "fingerprint": self.topo.fingerprint.tolist(),
+                "local_streak": self.topo.streak.tolist()}

@@ -329,3 +329,63 @@ def deterministic_parameters(shapes: dict[str, tuple[int, ...]], seed: int,
             values = values + 1.0
         out[name] = values
     return out
+
+
+def parameter_shapes(cfg: ModelConfig, rules: RuleMetadata) -> dict[str, tuple[int, ...]]:
+    """Names and shapes of the reference model's trainable parameters
+    (paged_model.py:97-195, model.py:143-206) for a configuration."""
+    w, r = cfg.width, cfg.retrieval_width
+    ns, nx = rules.num_sources, rules.num_xfers
+    max_pattern = max(map(len, rules.source_gate_types))
+    shapes = {
+        "gate_embedding.weight": (rules.num_gate_types, w),
+        "source_embedding.weight": (ns, w),
+        "xfer_embedding.weight": (nx, w),
+        "pattern_position.weight": (max_pattern, w),
+        "initial_marker": (w,),
+        "pattern_composer.0.weight": (2 * w, w), "pattern_composer.0.bias": (2 * w,),
+        "pattern_composer.2.weight": (w, 2 * w), "pattern_composer.2.bias": (w,),
+        "current_graph_marker": (w,),
+        "action_context.0.weight": (2 * w, 3 * w), "action_context.0.bias": (2 * w,),
+        "action_context.3.weight": (w, 2 * w), "action_context.3.bias": (w,),
+        "node_query.weight": (w, w), "binding_key.weight": (w, w),
+        "binding_value.weight": (w, w),
+        "action_delta.0.weight": (2 * w, 3 * w), "action_delta.0.bias": (2 * w,),
+        "action_delta.3.weight": (w, 2 * w), "action_delta.3.bias": (w,),
+        "action_norm.weight": (w,), "action_norm.bias": (w,),
+        "destination_state.0.weight": (2 * w, 3 * w), "destination_state.0.bias": (2 * w,),
+        "destination_state.2.weight": (w, 2 * w), "destination_state.2.bias": (w,),
+        "retrieval_node.weight": (r, w), "retrieval_source.weight": (r, w),
+        "source_bias": (ns,),
+        "pointer_node.weight": (r, w),
+        "pointer_query.0.weight": (2 * w, 3 * w), "pointer_query.0.bias": (2 * w,),
+        "pointer_query.2.weight": (r, 2 * w), "pointer_query.2.bias": (r,),
+        "action_position.weight": (cfg.max_sequence_length, w),
+        "action_output_norm.weight": (w,), "action_output_norm.bias": (w,),
+        "node_action_query.weight": (w, w), "node_action_key.weight": (w, w),
+        "node_action_value.weight": (w, w), "node_action_output.weight": (w, w),
+        "node_action_norm.weight": (w,), "node_action_norm.bias": (w,),
+    }
+    for prefix, count in (("graph_layers", cfg.graph_layers),
+                          ("readout_graph_layers", cfg.readout_graph_layers)):
+        for i in range(count):
+            p = f"{prefix}.{i}."
+            shapes.update({
+                p + "forward_message.weight": (w, w), p + "backward_message.weight": (w, w),
+                p + "relation.weight": (32, w),
+                p + "update.0.weight": (2 * w, 2 * w), p + "update.0.bias": (2 * w,),
+                p + "update.2.weight": (w, 2 * w), p + "update.2.bias": (w,),
+                p + "norm.weight": (w,), p + "norm.bias": (w,),
+            })
+    if cfg.readout_graph_layers:
+        shapes["readout_graph_output.weight"] = (w, w)
+    for i in range(cfg.action_layers):
+        p = f"causal_action_layers.{i}."
+        shapes.update({
+            p + "input_norm.weight": (w,), p + "input_norm.bias": (w,),
+            p + "qkv.weight": (3 * w, w), p + "output.weight": (w, w),
+            p + "ffn_norm.weight": (w,), p + "ffn_norm.bias": (w,),
+            p + "ffn.0.weight": (4 * w, w), p + "ffn.0.bias": (4 * w,),
+            p + "ffn.3.weight": (w, 4 * w), p + "ffn.3.bias": (w,),
+        })
+    return shapes

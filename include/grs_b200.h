@@ -174,13 +174,14 @@ GRS_API int grs_embed_initial(int dtype, const int64_t* types, int64_t rows, int
                               const float* gate_emb, const float* marker, void* states,
                               int64_t stride, uint8_t* live, void* stream);
 /* InitialGraphLayer aggregation (model.py:36-51) over port arrays
- * in/out_node, in/out_port int32 [B, S, 4]; fb = [forward | backward]
- * messages [B*S, 2W]; rel fp32 [32, W]; writes the degree-normalised sum. */
+ * in/out_node, in/out_port int32 [B, port_slots, 4] (port_slots >= slots);
+ * fb = [forward | backward] messages [B*slots, 2W]; rel fp32 [32, W]; writes
+ * the degree-normalised sum. */
 GRS_API int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride, const float* rel,
                                 const int32_t* in_node, const int32_t* in_port,
                                 const int32_t* out_node, const int32_t* out_port, int64_t rows,
-                                int slots, int width, void* agg, int64_t agg_stride,
-                                void* stream);
+                                int slots, int port_slots, int width, void* agg,
+                                int64_t agg_stride, void* stream);
 /* Bound-slot gather, pooling and action-context input (paged_model.py:494-523). */
 GRS_API int grs_action_inputs(int dtype, const void* states, int64_t state_stride, int slots,
                               const int64_t* xfer_ids, const int64_t* source_ids,
@@ -258,6 +259,64 @@ GRS_API int grs_structural_decode(const int64_t* types, const uint8_t* live, int
                                   int64_t* sources, const int64_t* anchors, int64_t count,
                                   int64_t* bindings, uint8_t* valid, int clear_invalid,
                                   void* stream);
+
+/* ---- lazy topology: lazy_rollout_benchmark.py:105-485 and the accept loop
+ * paged_rollout_benchmark.py:1013-1046 --------------------------------------
+ * Per beam: types int64 [B, S] (-1 dead), port arrays out/in node/port int32
+ * [B, S, 4] (-1 none), touch step int32 [B, S] (-1 never), previous-preferred
+ * uint8 [B, S], rewrite distance int32 [B, S], next_slot/streak int32 [B],
+ * gate count int64 [B], fingerprint uint64 [B] (XOR of splitmix64 node and
+ * edge components).  `table` is the per-xfer rewrite table of width
+ * grs_topology_table_width() built by the host from the patterns. */
+GRS_API int grs_topology_table_width(void);
+/* Plan every ranked proposal (rows/xfers/next_gate from grs_proposals_rank,
+ * device count): validity and child fingerprint (plan_indexed_rewrite). */
+GRS_API int grs_topology_plan(int64_t count_cap, const int64_t* count, const int64_t* rows,
+                              const int64_t* xfers, const int64_t* next_gate,
+                              const int64_t* cand_batch, const int64_t* cand_bindings,
+                              int cand_pattern, const int32_t* table, const int64_t* types,
+                              int32_t* out_node, int32_t* out_port, int32_t* in_node,
+                              int32_t* in_port, int slots, const int32_t* next_slot,
+                              const uint64_t* fingerprint, uint8_t* valid, uint64_t* fp_out,
+                              int32_t* status, void* stream);
+/* Accept loop: first occurrence by rank among valid, unseen fingerprints;
+ * the first beam_size are accepted, inserted into the seen set and stably
+ * sorted by next gate count into child_proposal.  summary int64 [6] =
+ * accepted, attempted, invalid, duplicates, max child next slot, best
+ * (smallest) child gate count.  Hash
+ * tables are power-of-two open-addressing arrays (uint64 keys, 0 = empty). */
+GRS_API int grs_topology_accept(int64_t count_cap, const int64_t* count, const uint8_t* valid,
+                                const uint64_t* fp, const int64_t* next_gate, int beam_size,
+                                uint64_t* step_keys, int32_t* step_first, int64_t step_capacity,
+                                uint64_t* seen, int64_t seen_capacity, uint8_t* classes,
+                                int64_t* child_proposal, int64_t* summary, const int64_t* rows,
+                                const int64_t* xfers, const int64_t* cand_batch,
+                                const int32_t* table, const int32_t* next_slot, int32_t* status,
+                                void* stream);
+GRS_API int grs_topology_seen_insert(const uint64_t* fp, int64_t n, uint64_t* seen,
+                                     int64_t seen_capacity, int32_t* status, void* stream);
+/* Build every accepted child (materialize_indexed_rewrite, dense_last_touched,
+ * previous_preferred, local_streak, BFS rewrite distance) into the child
+ * buffers (row stride `slots`, parents read with row stride `p_slots`) and
+ * emit the per-child action tensors of the model advance. */
+GRS_API int grs_topology_materialize(
+    int max_children, const int64_t* child_proposal, const int64_t* summary, const int64_t* rows,
+    const int64_t* xfers, const int64_t* next_gate, const uint64_t* fp, const int64_t* cand_batch,
+    const int64_t* cand_anchor, const int64_t* cand_bindings, int cand_pattern,
+    const int32_t* table, const int64_t* xfer_to_source, int p_slots, int slots,
+    const int64_t* p_types, const int32_t* p_out_node, const int32_t* p_out_port, const int32_t* p_in_node,
+    const int32_t* p_in_port, const int32_t* p_touched, const uint8_t* p_pref,
+    const int32_t* p_next_slot, const int32_t* p_streak, int64_t* c_types, int32_t* c_out_node,
+    int32_t* c_out_port, int32_t* c_in_node, int32_t* c_in_port, int32_t* c_touched,
+    uint8_t* c_pref, int32_t* c_distance, int32_t* c_next_slot, int32_t* c_streak,
+    int64_t* c_gate, uint64_t* c_fp, int64_t* a_parent, int64_t* a_xfer, int64_t* a_source,
+    int64_t* a_src_slots, int src_pattern, int64_t* a_dst_slots, int64_t* a_dst_types,
+    int dst_pattern, int depth, int32_t* status, void* stream);
+/* XOR fingerprint of beam rows from their types and out-ports (indexed_topology). */
+GRS_API int grs_topology_fingerprint(const int64_t* types, const int32_t* out_node,
+                                     const int32_t* out_port, const int32_t* in_node,
+                                     const int32_t* in_port, int batch, int slots, uint64_t* fp,
+                                     void* stream);
 
 #ifdef __cplusplus
 }

@@ -32,17 +32,19 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_python_bindings_cover_header():
+    """Every declaration is bound with a signature parsed from the header, and
+    a call with the wrong argument count is refused before reaching C."""
+    import pytest
     from graph_rewrite_system_b200 import _lib
-    import graph_rewrite_system_b200.paged_attention  # noqa: F401
-    import graph_rewrite_system_b200.paged_cache  # noqa: F401
-    import graph_rewrite_system_b200.gpu_proposals  # noqa: F401
-    import graph_rewrite_system_b200.kernels  # noqa: F401
+    import graph_rewrite_system_b200.rollout  # noqa: F401  (imports every host module)
 
     bound = set(_lib.exported_symbols())
-    missing = [n for n in declared_entry_points() if n not in bound]
-    assert not missing, f"no ctypes binding for: {missing}"
+    assert bound == set(declared_entry_points())
+    assert len(_lib._SIGNATURES["grs_topology_materialize"][1]) == 47
     lib = _lib.lib()
     assert lib.grs_version().startswith(b"grs_b200")
+    with pytest.raises(TypeError):
+        lib.grs_cache_init(0, 0, 0, 0, 1)
 
 
 def test_cpu_tensors_rejected():
