@@ -18,7 +18,7 @@ template <typename T, int D>
 struct RowsArgs {
   const T* q; int64_t q_sb, q_sh, q_sq;
   const T* kc; const T* vc; int64_t kc_sp, kc_st, kc_sh;
-  const int32_t* bt; int64_t bt_s; const int32_t* lengths;
+  const int32_t* bt; int64_t bt_s; const int32_t* lengths; int num_pages;
   const T* ck; const T* cv; int64_t ck_sb, ck_sh; const uint8_t* cvalid;
   const T* sk; const T* sv; int num_shared;
   T* out; int64_t o_sb, o_sh, o_sq;
@@ -39,6 +39,7 @@ __device__ __forceinline__ const T* token_key(const RowsArgs<T, D>& a, int b, in
   t -= a.num_shared;
   if (t < past) {
     int page = a.bt[(int64_t)b * a.bt_s + t / a.page];
+    if (page < 0 || page >= a.num_pages) return nullptr;  // not a cache page: no key
     const T* base = is_v ? a.vc : a.kc;
     return base + (int64_t)page * a.kc_sp + (int64_t)(t % a.page) * a.kc_st + (int64_t)h * a.kc_sh;
   }
@@ -74,8 +75,8 @@ __global__ void __launch_bounds__(256) paged_attention_rows_kernel(RowsArgs<T, D
   for (int base = 0; base < T_total; base += 32) {
     const int t = base + lane;
     float s = -INFINITY;
-    if (t < T_total) {
-      const T* kp = token_key(a, b, h, t, past, false);
+    const T* kp = t < T_total ? token_key(a, b, h, t, past, false) : nullptr;
+    if (kp) {
       float dot = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) dot += qv[d] * to_float(kp[d]);
@@ -83,8 +84,8 @@ __global__ void __launch_bounds__(256) paged_attention_rows_kernel(RowsArgs<T, D
     }
     const float cmax = warp_max(s);
     const float m_new = fmaxf(m, cmax);
-    const float p = (t < T_total) ? exp2f(s - m_new) : 0.f;
-    const float corr = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
+    const float p = kp ? exp2f(s - m_new) : 0.f;
+    const float corr = (m == -INFINITY || m_new == -INFINITY) ? 0.f : exp2f(m - m_new);
     l = l * corr + warp_sum(p);
 #pragma unroll
     for (int i = 0; i < ND; ++i) acc[i] *= corr;
@@ -93,6 +94,7 @@ __global__ void __launch_bounds__(256) paged_attention_rows_kernel(RowsArgs<T, D
     for (int j = 0; j < nkeys; ++j) {
       const float pj = __shfl_sync(0xffffffffu, p, j);
       const T* vp = token_key(a, b, h, base + j, past, true);
+      if (!vp) continue;
 #pragma unroll
       for (int i = 0; i < ND; ++i) {
         const int d = lane + 32 * i;
@@ -138,7 +140,7 @@ __device__ __forceinline__ uint32_t pack_bf16_raw(__nv_bfloat16 lo, __nv_bfloat1
 struct ReadoutArgs {
   const __nv_bfloat16* q; int64_t q_sb, q_sh, q_sq;
   const __nv_bfloat16* kc; const __nv_bfloat16* vc; int64_t kc_sp, kc_st, kc_sh;
-  const int32_t* bt; int64_t bt_s; const int32_t* lengths;
+  const int32_t* bt; int64_t bt_s; const int32_t* lengths; int num_pages;
   __nv_bfloat16* out; int64_t o_sb, o_sh, o_sq;
   int B, H, Q, page; float scale_log2;
 };
@@ -264,8 +266,8 @@ __device__ __forceinline__ void readout_stage(const ReadoutArgs& a, int b, int t
     const int t = idx / (4 * a.H);
     const int tok = t0 + t;
     uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (tok < length) {
-      const int page = a.bt[(int64_t)b * a.bt_s + tok / a.page];
+    const int page = tok < length ? a.bt[(int64_t)b * a.bt_s + tok / a.page] : -1;
+    if (page >= 0 && page < a.num_pages) {
       const int64_t off = (int64_t)page * a.kc_sp + (int64_t)(tok % a.page) * a.kc_st +
                           (int64_t)h * a.kc_sh + v * 8;
       kv = __ldg(reinterpret_cast<const uint4*>(a.kc + off));
@@ -353,7 +355,7 @@ int launch_rows(const RowsArgs<T, D>& a, cudaStream_t stream) {
 template <typename T>
 int dispatch_rows(int D, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sq,
                   const void* kc, const void* vc, int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
-                  const int32_t* bt, int64_t bt_s, const int32_t* lengths,
+                  const int32_t* bt, int64_t bt_s, const int32_t* lengths, int num_pages,
                   const void* ck, const void* cv, int64_t ck_sb, int64_t ck_sh,
                   const uint8_t* cvalid, const void* sk, const void* sv, int num_shared,
                   void* out, int64_t o_sb, int64_t o_sh, int64_t o_sq,
@@ -362,7 +364,7 @@ int dispatch_rows(int D, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sq
 #define GRS_ROWS_CASE(DD)                                                                   \
   case DD: {                                                                                \
     RowsArgs<T, DD> a{(const T*)q, q_sb, q_sh, q_sq, (const T*)kc, (const T*)vc, kc_sp,     \
-                      kc_st, kc_sh, bt, bt_s, lengths, (const T*)ck, (const T*)cv, ck_sb,   \
+                      kc_st, kc_sh, bt, bt_s, lengths, num_pages, (const T*)ck, (const T*)cv, ck_sb, \
                       ck_sh, cvalid, (const T*)sk, (const T*)sv, num_shared, (T*)out, o_sb, \
                       o_sh, o_sq, B, H, Q, page, scale_log2};                               \
     return launch_rows<T, DD>(a, stream);                                                   \
@@ -390,7 +392,7 @@ extern "C" int grs_paged_attention(
     const void* current_key, const void* current_value, int64_t ck_sb, int64_t ck_sh,
     const uint8_t* current_valid, const void* shared_key, const void* shared_value,
     int64_t num_shared, void* output, int64_t o_sb, int64_t o_sh, int64_t o_sq, int batch,
-    int heads, int query_len, int head_width, int page_size, int max_blocks,
+    int heads, int query_len, int head_width, int page_size, int max_blocks, int num_pages,
     void* stream_ptr) {
   cudaStream_t stream = (cudaStream_t)stream_ptr;
   if (batch < 0 || heads <= 0 || query_len < 0 || page_size <= 0 || num_shared < 0)
@@ -406,7 +408,7 @@ extern "C" int grs_paged_attention(
     if (batch == 0) return GRS_OK;
     ReadoutArgs a{(const __nv_bfloat16*)query, q_sb, q_sh, q_sq,
                   (const __nv_bfloat16*)key_cache, (const __nv_bfloat16*)value_cache,
-                  kc_sp, kc_st, kc_sh, block_table, bt_stride, lengths,
+                  kc_sp, kc_st, kc_sh, block_table, bt_stride, lengths, num_pages,
                   (__nv_bfloat16*)output, o_sb, o_sh, o_sq, batch, heads, query_len,
                   page_size, 1.4426950408889634f / sqrtf(32.f)};
     const size_t smem = (size_t)2 * heads * RO_TILE * RO_PAD * sizeof(__nv_bfloat16);
@@ -430,14 +432,16 @@ extern "C" int grs_paged_attention(
   if (dtype == GRS_DTYPE_BF16)
     return dispatch_rows<__nv_bfloat16>(head_width, query, q_sb, q_sh, q_sq, key_cache,
                                         value_cache, kc_sp, kc_st, kc_sh, block_table,
-                                        bt_stride, lengths, current_key, current_value, ck_sb,
+                                        bt_stride, lengths, num_pages, current_key,
+                                        current_value, ck_sb,
                                         ck_sh, current_valid, shared_key, shared_value,
                                         (int)num_shared, output, o_sb, o_sh, o_sq, batch,
                                         heads, query_len, page_size, stream);
   if (dtype == GRS_DTYPE_F32)
     return dispatch_rows<float>(head_width, query, q_sb, q_sh, q_sq, key_cache, value_cache,
                                 kc_sp, kc_st, kc_sh, block_table, bt_stride, lengths,
-                                current_key, current_value, ck_sb, ck_sh, current_valid,
+                                num_pages, current_key, current_value, ck_sb, ck_sh,
+                                current_valid,
                                 shared_key, shared_value, (int)num_shared, output, o_sb,
                                 o_sh, o_sq, batch, heads, query_len, page_size, stream);
   return GRS_ERR_SHAPE;

@@ -42,9 +42,15 @@ __global__ void cache_fork_kernel(int32_t* __restrict__ refcounts,
   const int32_t* prow = ptable + (int64_t)i * pstride;
   int32_t* crow = ctable + (int64_t)i * cstride;
   if (keep + 1 > ccols) { set_status(status, GRS_ERR_SHAPE); return; }
+  // Error paths record a status and write page 0 so that no table ever holds
+  // an out-of-range page id.
   for (int j = 0; j < keep; ++j) {
     const int p = prow[j];
-    if (p < 0 || p >= capacity) { set_status(status, GRS_ERR_BAD_PAGE); return; }
+    if (p < 0 || p >= capacity) {
+      set_status(status, GRS_ERR_BAD_PAGE);
+      crow[j] = 0;
+      continue;
+    }
     const int old = atomicAdd(&refcounts[p], 1);
     if (old <= 0) set_status(status, GRS_ERR_BAD_PAGE);
     crow[j] = p;
@@ -54,10 +60,11 @@ __global__ void cache_fork_kernel(int32_t* __restrict__ refcounts,
   if (i >= fc) {
     set_status(status, GRS_ERR_EXHAUSTED);
   } else {
-    page_id = free_list[fc - 1 - i];
-    if (page_id < 0 || page_id >= capacity || refcounts[page_id] != 0) {
+    const int candidate = free_list[fc - 1 - i];
+    if (candidate < 0 || candidate >= capacity || refcounts[candidate] != 0) {
       set_status(status, GRS_ERR_CORRUPT);
     } else {
+      page_id = candidate;
       refcounts[page_id] = 1;
     }
   }
@@ -116,6 +123,7 @@ __global__ void cache_write_kernel(CacheArenas ar, const int32_t* __restrict__ p
   const int offset = len % ar.page;
   const int nb = blocks_for(len, ar.page);
   const int dst = ctable[(int64_t)i * cstride + (offset == 0 ? nb : nb - 1)];
+  if (dst < 0 || dst >= ar.capacity) return;
   const int64_t kv_row = (int64_t)ar.hd * ar.elem;
   const int64_t kv_page = kv_row * ar.page;
   const int64_t kv_layer = kv_page * ar.capacity;
@@ -123,6 +131,7 @@ __global__ void cache_write_kernel(CacheArenas ar, const int32_t* __restrict__ p
   const int64_t act_page = act_row * ar.page;
   if (offset != 0) {
     const int src = ptable[(int64_t)i * pstride + nb - 1];
+    if (src < 0 || src >= ar.capacity) return;
     for (int l = 0; l < ar.layers; ++l) {
       copy_rows((char*)ar.keys + l * kv_layer, kv_page, src, dst, offset, kv_row);
       copy_rows((char*)ar.values + l * kv_layer, kv_page, src, dst, offset, kv_row);

@@ -384,3 +384,281 @@ extern "C" int grs_proposals_rank_static(
                             out_count, out_metrics, scratch, kProposalStaticScratchBytes, status,
                             stream);
 }
+
+// ---------------------------------------------------------------------------
+// Parent-grouped ranking.  When the candidates of parent b are the rows
+// [b*k, (b+1)*k) (the padded layout of the device candidate selection, rows
+// with source < 0 are absent), the per-parent cap needs no global sort: one
+// CTA per parent expands its candidates in row order, sorts the expansion in
+// shared memory by (next gate, probability desc, xfer, expansion index) - the
+// key order of gpu_proposals.py:128-135 with the stable sort's tie rule - and
+// keeps the first per_parent_cap.  The concatenation of the per-parent lists
+// in parent order is exactly the order the reference's stable global sort
+// sees, so one stable radix sort of <= parents*cap packed keys finishes.
+// ---------------------------------------------------------------------------
+namespace grs {
+
+constexpr int GRP_THREADS = 512;
+constexpr int GRP_MAX_EXPANDED = 4096;
+
+__global__ void __launch_bounds__(GRP_THREADS) prop_grouped_parent_kernel(
+    const int64_t* __restrict__ sources, const float* __restrict__ probs, int k,
+    const int64_t* __restrict__ parent_gates, const int32_t* __restrict__ xfer_offsets,
+    const int32_t* __restrict__ xfer_counts, const int32_t* __restrict__ xfer_ids,
+    const int32_t* __restrict__ gate_deltas, const int32_t* __restrict__ all_counts,
+    int num_sources, int cap, int32_t* __restrict__ sel_row, int32_t* __restrict__ sel_xfer,
+    int32_t* __restrict__ sel_next, int64_t* __restrict__ metrics, int32_t* __restrict__ status) {
+  extern __shared__ unsigned long long keys[];   // [GRP_MAX_EXPANDED]
+  __shared__ int warp_tot[GRP_THREADS / 32];
+  __shared__ int s_base;
+  __shared__ unsigned long long s_pred, s_elig;
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) { s_base = 0; s_pred = 0; s_elig = 0; }
+  __syncthreads();
+  const int64_t pgate = parent_gates[b];
+  // expansion in row order: block scan of the per-row xfer counts
+  for (int r0 = 0; r0 < k; r0 += GRP_THREADS) {
+    const int r = r0 + tid;
+    int cnt = 0, all = 0;
+    int64_t src = -1;
+    if (r < k) {
+      src = sources[(int64_t)b * k + r];
+      if (src >= num_sources) { set_status(status, GRS_ERR_SHAPE); src = -1; }
+      if (src >= 0) { cnt = xfer_counts[src]; all = all_counts[src]; }
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int before = s_base;
+    for (int w = 0; w < warp; ++w) before += warp_tot[w];
+    const int start = before + incl - cnt;
+    if (cnt) {
+      atomicAdd(&s_pred, (unsigned long long)all);
+      atomicAdd(&s_elig, (unsigned long long)cnt);
+      const uint32_t pk = desc_float_key(probs[(int64_t)b * k + r]);
+      const int xo = xfer_offsets[src];
+      for (int w = 0; w < cnt; ++w) {
+        const int e = start + w;
+        if (e >= GRP_MAX_EXPANDED) { set_status(status, GRS_ERR_WORKSPACE); break; }
+        const int x = xfer_ids[xo + w];
+        const int delta = gate_deltas[x];
+        if (delta < -8 || delta > 7 || x > 0xffff) set_status(status, GRS_ERR_SHAPE);
+        keys[e] = ((unsigned long long)(uint32_t)(delta + 8) << 60) |
+                  ((unsigned long long)pk << 28) | ((unsigned long long)(x & 0xffff) << 12) |
+                  (unsigned long long)(e & 0xfff);
+      }
+    } else if (all) {
+      atomicAdd(&s_pred, (unsigned long long)all);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int tot = 0;
+      for (int w = 0; w < GRP_THREADS / 32; ++w) tot += warp_tot[w];
+      s_base += tot;
+    }
+    __syncthreads();
+  }
+  const int n = min(s_base, GRP_MAX_EXPANDED);
+  // expansion index -> candidate row: recompute by a second scan pass is
+  // avoided by storing the row in a parallel array keyed by expansion index.
+  __shared__ int16_t row_of[GRP_MAX_EXPANDED];
+  // (fill row_of: re-walk the rows; each thread writes its own range)
+  if (tid == 0) s_base = 0;
+  __syncthreads();
+  for (int r0 = 0; r0 < k; r0 += GRP_THREADS) {
+    const int r = r0 + tid;
+    int cnt = 0;
+    if (r < k) {
+      const int64_t src = sources[(int64_t)b * k + r];
+      if (src >= 0 && src < num_sources) cnt = xfer_counts[src];
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int before = s_base;
+    for (int w = 0; w < warp; ++w) before += warp_tot[w];
+    for (int w = 0; w < cnt; ++w) {
+      const int e = before + incl - cnt + w;
+      if (e < GRP_MAX_EXPANDED) row_of[e] = (int16_t)r;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int tot = 0;
+      for (int w = 0; w < GRP_THREADS / 32; ++w) tot += warp_tot[w];
+      s_base += tot;
+    }
+    __syncthreads();
+  }
+  int size = 1;
+  while (size < n) size <<= 1;
+  for (int i = n + tid; i < size; i += GRP_THREADS) keys[i] = ~0ull;
+  __syncthreads();
+  for (int k2 = 2; k2 <= size; k2 <<= 1) {
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < size; i += GRP_THREADS) {
+        const int l = i ^ j;
+        if (l > i) {
+          const unsigned long long x = keys[i], y = keys[l];
+          const bool asc = (i & k2) == 0;
+          if (asc ? (x > y) : (x < y)) { keys[i] = y; keys[l] = x; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const int keep = min(n, cap);
+  for (int r = tid; r < cap; r += GRP_THREADS) {
+    const int64_t o = (int64_t)b * cap + r;
+    if (r < keep) {
+      const unsigned long long key = keys[r];
+      const int e = (int)(key & 0xfff);
+      const int x = (int)((key >> 12) & 0xffff);
+      const int delta = (int)(key >> 60) - 8;
+      sel_row[o] = b * k + row_of[e];
+      sel_xfer[o] = x;
+      sel_next[o] = (int32_t)(pgate + delta);
+    } else {
+      sel_row[o] = -1;
+      sel_xfer[o] = -1;
+      sel_next[o] = 0;
+    }
+  }
+  if (tid == 0) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(&metrics[0]), s_pred);
+    atomicAdd(reinterpret_cast<unsigned long long*>(&metrics[1]), s_elig);
+  }
+}
+
+__global__ void prop_grouped_key_kernel(const int32_t* __restrict__ sel_row,
+                                        const int32_t* __restrict__ sel_next,
+                                        const float* __restrict__ probs,
+                                        const int64_t* __restrict__ parent_gates, int k,
+                                        int64_t n, uint64_t* __restrict__ key,
+                                        int32_t* __restrict__ value, int32_t* __restrict__ status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int32_t row = sel_row[i];
+  if (row < 0) {
+    key[i] = PAD_KEY;
+  } else {
+    const int64_t pg = parent_gates[row / k];
+    const int32_t next = sel_next[i];
+    if (pg < -32768 || pg > 32767 || next < -32768 || next > 32767) set_status(status, GRS_ERR_SHAPE);
+    key[i] = ((uint64_t)(uint16_t)(next + 32768) << 48) |
+             ((uint64_t)desc_float_key(probs[row]) << 16) | (uint64_t)(uint16_t)(pg + 32768);
+  }
+  value[i] = (int32_t)i;
+}
+
+__global__ void prop_grouped_output_kernel(const uint64_t* __restrict__ sorted_key,
+                                           const int32_t* __restrict__ sorted_pos,
+                                           int64_t global_cap, const int32_t* __restrict__ sel_row,
+                                           const int32_t* __restrict__ sel_xfer,
+                                           const int32_t* __restrict__ sel_next, int64_t n,
+                                           int64_t* __restrict__ out_row,
+                                           int64_t* __restrict__ out_xfer,
+                                           int64_t* __restrict__ out_next,
+                                           int64_t* __restrict__ out_count) {
+  __shared__ int block_count;
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (threadIdx.x == 0) block_count = 0;
+  __syncthreads();
+  bool live = j < global_cap && j < n && sorted_key[j] != PAD_KEY;
+  if (j < global_cap) {
+    if (live) {
+      const int32_t pos = sorted_pos[j];
+      out_row[j] = sel_row[pos];
+      out_xfer[j] = sel_xfer[pos];
+      out_next[j] = sel_next[pos];
+    } else {
+      out_row[j] = -1;
+      out_xfer[j] = -1;
+      out_next[j] = 0;
+    }
+  }
+  if (live) atomicAdd(&block_count, 1);
+  __syncthreads();
+  if (threadIdx.x == 0 && block_count)
+    atomicAdd(reinterpret_cast<unsigned long long*>(out_count), (unsigned long long)block_count);
+}
+
+}  // namespace grs
+
+extern "C" int64_t grs_proposals_grouped_workspace_bytes(int64_t parents, int per_parent_cap) {
+  const int64_t n = parents * (int64_t)per_parent_cap;
+  size_t t = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, t, (uint64_t*)nullptr, (uint64_t*)nullptr,
+                                  (int32_t*)nullptr, (int32_t*)nullptr, (int)(n > 0 ? n : 1));
+  const size_t elems = (size_t)(n > 0 ? n : 1);
+  return (int64_t)(align_up(elems * 4) * 3 + align_up(elems * 8) * 2 + align_up(elems * 4) * 2 +
+                   align_up(t));
+}
+
+extern "C" int grs_proposals_rank_grouped(
+    const int64_t* sources, const float* probabilities, int64_t parents, int k,
+    const int64_t* parent_gate_counts, const int32_t* xfer_offsets, const int32_t* xfer_counts,
+    const int32_t* xfer_ids, const int32_t* gate_deltas, const int32_t* all_xfer_counts,
+    int num_sources, int per_parent_cap, int64_t global_cap, int64_t* out_row, int64_t* out_xfer,
+    int64_t* out_next_gate, int64_t* out_count, int64_t* out_metrics, void* workspace,
+    int64_t workspace_bytes, int32_t* status, void* stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  if (parents < 0 || k <= 0 || per_parent_cap <= 0 || global_cap < 0 ||
+      per_parent_cap > GRP_MAX_EXPANDED)
+    return GRS_ERR_SHAPE;
+  if (grs_proposals_grouped_workspace_bytes(parents, per_parent_cap) > workspace_bytes)
+    return GRS_ERR_WORKSPACE;
+  cudaMemsetAsync(out_metrics, 0, 2 * sizeof(int64_t), s);
+  cudaMemsetAsync(out_count, 0, sizeof(int64_t), s);
+  if (parents == 0) {
+    GRS_CUDA_CHECK_LAUNCH();
+    return GRS_OK;
+  }
+  const int64_t n = parents * per_parent_cap;
+  char* base = (char*)workspace;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { char* p = base + off; off += align_up(bytes); return p; };
+  int32_t* sel_row = (int32_t*)take(n * 4);
+  int32_t* sel_xfer = (int32_t*)take(n * 4);
+  int32_t* sel_next = (int32_t*)take(n * 4);
+  uint64_t* key_in = (uint64_t*)take(n * 8);
+  uint64_t* key_out = (uint64_t*)take(n * 8);
+  int32_t* val_in = (int32_t*)take(n * 4);
+  int32_t* val_out = (int32_t*)take(n * 4);
+  size_t tb = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, tb, key_in, key_out, val_in, val_out, (int)n);
+  void* cub_tmp = take(tb);
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(prop_grouped_parent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GRP_MAX_EXPANDED * 8);
+    attr[dev] = true;
+  }
+  prop_grouped_parent_kernel<<<(unsigned)parents, GRP_THREADS, GRP_MAX_EXPANDED * 8, s>>>(
+      sources, probabilities, k, parent_gate_counts, xfer_offsets, xfer_counts, xfer_ids,
+      gate_deltas, all_xfer_counts, num_sources, per_parent_cap, sel_row, sel_xfer, sel_next,
+      out_metrics, status);
+  prop_grouped_key_kernel<<<ceil_div(n, 256), 256, 0, s>>>(sel_row, sel_next, probabilities,
+                                                           parent_gate_counts, k, n, key_in,
+                                                           val_in, status);
+  cub::DeviceRadixSort::SortPairs(cub_tmp, tb, key_in, key_out, val_in, val_out, (int)n, 0, 64,
+                                  s);
+  if (global_cap > 0)
+    prop_grouped_output_kernel<<<ceil_div(global_cap, 256), 256, 0, s>>>(
+        key_out, val_out, global_cap, sel_row, sel_xfer, sel_next, n, out_row, out_xfer,
+        out_next_gate, out_count);
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}

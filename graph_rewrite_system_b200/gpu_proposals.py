@@ -152,3 +152,42 @@ def build_gpu_proposals(candidates: CandidateTensors, beam: list[BeamState],
     if profile_stages:
         timing["proposal_device_to_host_and_pack_seconds"] = time.perf_counter() - started
     return proposals, {"predicted_actions": int(predicted), "eligible_actions": int(eligible)}, timing
+
+
+def rank_proposals_grouped(sources: torch.Tensor, probabilities: torch.Tensor, k: int,
+                           parent_gate_counts: torch.Tensor, rule_index: GpuRuleIndex, *,
+                           per_parent_cap: int, global_cap: int,
+                           status: torch.Tensor | None = None) -> RankedProposals:
+    """Same result as ``rank_proposals_device`` for candidates laid out
+    [parents, k] (parent b owns rows b*k..b*k+k-1, absent rows have source
+    -1), with the per-parent cap taken per parent in shared memory."""
+    _lib.require_cuda(sources, probabilities, parent_gate_counts)
+    device = sources.device
+    parents = parent_gate_counts.numel()
+    if sources.numel() != parents * k:
+        raise ValueError("grouped candidates must be [parents * k]")
+    need = int(_lib.lib().grs_proposals_grouped_workspace_bytes(parents, per_parent_cap))
+    key = (str(device), "grouped")
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 1), device=device, dtype=torch.uint8)
+        _WORKSPACES[key] = ws
+    i64 = dict(device=device, dtype=torch.int64)
+    rows = torch.empty(max(global_cap, 0), **i64)
+    xfers = torch.empty_like(rows)
+    nexts = torch.empty_like(rows)
+    count = torch.empty(1, **i64)
+    metrics = torch.empty(2, **i64)
+    if status is None:
+        status = torch.zeros(1, device=device, dtype=torch.int32)
+    _lib.check(_lib.lib().grs_proposals_rank_grouped(
+        sources.to(torch.int64).contiguous().data_ptr(),
+        probabilities.to(torch.float32).contiguous().data_ptr(), parents, k,
+        parent_gate_counts.to(torch.int64).contiguous().data_ptr(),
+        rule_index.xfer_offsets.data_ptr(), rule_index.xfer_counts.data_ptr(),
+        rule_index.xfer_ids.data_ptr(), rule_index.gate_deltas.data_ptr(),
+        rule_index.all_xfer_counts.data_ptr(), rule_index.xfer_counts.numel(), per_parent_cap,
+        global_cap, rows.data_ptr(), xfers.data_ptr(), nexts.data_ptr(), count.data_ptr(),
+        metrics.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(),
+        torch.cuda.current_stream(device).cuda_stream), "rank_proposals_grouped")
+    return RankedProposals(rows, xfers, nexts, count, metrics, status)

@@ -81,7 +81,7 @@ def paged_attention(
         _lib.ptr(sk), _lib.ptr(sv), num_shared,
         output.data_ptr(), output.stride(0), output.stride(1), output.stride(2),
         batch, heads, query_length, head_width, key_cache.shape[1], block_table.shape[1],
-        _lib.stream_of(query),
+        key_cache.shape[0], _lib.stream_of(query),
     )
     _lib.check(status, "paged_attention")
     return output

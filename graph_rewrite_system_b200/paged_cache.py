@@ -72,6 +72,17 @@ class PagedKVCache:
             self._refcounts.data_ptr(), self._free.data_ptr(), self._free_count.data_ptr(),
             self._last_pos.data_ptr(), capacity, self._stream()), "PagedKVCache")
 
+    def reset(self) -> None:
+        """Return every page to the free list (the state of a new cache)."""
+        self._status.zero_()
+        _lib.check(_lib.lib().grs_cache_init(
+            self._refcounts.data_ptr(), self._free.data_ptr(), self._free_count.data_ptr(),
+            self._last_pos.data_ptr(), self.capacity, self._stream()), "PagedKVCache")
+
+    def status_tensor(self) -> torch.Tensor:
+        """The device status word (0 = ok) without synchronising."""
+        return self._status
+
     # ---- state views (device -> host) -------------------------------------
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
@@ -177,6 +188,8 @@ class PagedKVCache:
         for i, h in enumerate(handles):
             if (h.length + self.page_size - 1) // self.page_size != len(h.blocks):
                 raise RuntimeError("prefix handle length/block table mismatch")
+            if any(not 0 <= p < self.capacity for p in h.blocks):
+                raise ValueError("prefix handle names a page outside the cache")
             rows[i, : len(h.blocks)] = h.blocks
             lengths[i] = h.length
         table = torch.from_numpy(rows).to(self.device, non_blocking=True)

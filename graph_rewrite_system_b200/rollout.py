@@ -31,7 +31,7 @@ import torch
 
 from . import _lib
 from . import kernels as K
-from .gpu_proposals import GpuRuleIndex, rank_proposals_device
+from .gpu_proposals import GpuRuleIndex, rank_proposals_grouped
 from .paged_cache import PagedKVCache
 from .paged_model import PagedActionBindingModel
 from .synthetic import (Circuit, RolloutConfig, RuleMetadata, SELECT_ALL_THRESHOLDS)
@@ -144,6 +144,7 @@ class DeviceBeamSearch:
                  "edge_relation": (e[:, 2] * 4 + e[:, 3]).to(dev)}
         self.states, self.live, self.types = model.initialize_incremental(batch)
         self.topo = initial_topology(self.topology[0], nodes, edges, s)
+        self.cache.reset()
         self.current = 0
         self.block_table = torch.zeros(1, 1, device=dev, dtype=torch.int32)
         self.lengths = torch.zeros(1, device=dev, dtype=torch.int32)
@@ -175,9 +176,10 @@ class DeviceBeamSearch:
         # 3. proposals (effective parent cap of paged_rollout_benchmark.py:963-966)
         cap = max(cfg.per_parent_cap, math.ceil(cfg.beam_size / max(1, b)) * 2)
         self._mark("proposals")
-        ranked = rank_proposals_device(cand["batch_ids"], cand["sources"], cand["probabilities"],
-                                       topo.gate, self.rule_index, per_parent_cap=cap,
-                                       global_cap=cfg.global_cap, status=self.status)
+        k = cand["sources"].numel() // b
+        ranked = rank_proposals_grouped(cand["sources"], cand["probabilities"], k, topo.gate,
+                                        self.rule_index, per_parent_cap=cap,
+                                        global_cap=cfg.global_cap, status=self.status)
         # 4. plan + accept
         gcap = cfg.global_cap
         valid = torch.empty(gcap, device=dev, dtype=torch.uint8)
@@ -206,12 +208,15 @@ class DeviceBeamSearch:
         # one synchronisation per level
         self._mark("host_sync")
         host = torch.cat((self.summary, ranked.count, ranked.metrics,
-                          self.cache.allocated_pages_tensor().long(), self.status.long())).cpu()
+                          self.cache.allocated_pages_tensor().long(), self.status.long(),
+                          self.cache.status_tensor().long())).cpu()
         (accepted, attempted, invalid, dup, extent, best, proposals, predicted, eligible_n,
-         allocated, status) = host.tolist()
+         allocated, status, cache_status) = host.tolist()
         if status:
             self.status.zero_()
             _lib.check(int(status), "beam search step")
+        if cache_status:
+            self.cache.check_status()
         row = StepRow(depth + 1, b, accepted, best, predicted, eligible_n, proposals, attempted,
                       accepted, invalid, dup, allocated, 0, 0.0)
         if not accepted:

@@ -287,7 +287,7 @@ class RolloutConfig:
     depth: int = 64
     microbatch: int = 512
     page_size: int = 16
-    max_candidates_per_state: int = 80
+    max_candidates_per_state: int = 2048
     per_parent_cap: int = 16
     proposal_factor: int = 16
     max_gate_increase: int = 1

@@ -49,7 +49,8 @@ GRS_API const char* grs_version(void);
  * paged_attention.py:230-232); optional shared_key/value [num_shared,H,D]
  * contiguous, attended by every beam before its pages (not in the
  * reference; the shared-prefix decode microbenchmark).  Rows with no valid
- * key are written as zeros. */
+ * key are written as zeros.  Block-table entries outside [0, num_pages) are
+ * not read (such a token is treated as absent). */
 GRS_API int grs_paged_attention(int dtype, const void* query, int64_t q_sb, int64_t q_sh, int64_t q_sq,
                         const void* key_cache, const void* value_cache, int64_t kc_sp,
                         int64_t kc_st, int64_t kc_sh, const int32_t* block_table,
@@ -59,7 +60,7 @@ GRS_API int grs_paged_attention(int dtype, const void* query, int64_t q_sb, int6
                         const void* shared_value, int64_t num_shared, void* output,
                         int64_t o_sb, int64_t o_sh, int64_t o_sq, int batch, int heads,
                         int query_len, int head_width, int page_size, int max_blocks,
-                        void* stream);
+                        int num_pages, void* stream);
 
 /* ---- PagedKVCache device state: paged_cache.py:16-105 -------------------
  * refcounts int32 [capacity], free_list int32 [capacity] with its length in
@@ -122,6 +123,25 @@ GRS_API int grs_proposals_rank(const int64_t* batch_ids, const int64_t* sources,
                                int64_t* out_row, int64_t* out_xfer, int64_t* out_next_gate,
                                int64_t* out_count, int64_t* out_metrics, void* workspace,
                                int64_t workspace_bytes, int32_t* status, void* stream);
+
+/* Parent-grouped form of grs_proposals_rank (gpu_proposals.py:69-155 with the
+ * same ordering and tie rules) for candidates laid out [parents, k] with the
+ * rows of parent b at [b*k, (b+1)*k) and absent rows marked source < 0: the
+ * per-parent cap is taken per parent in shared memory (expansion of one
+ * parent <= 4096 actions, gate deltas in [-8, 7]) and one stable radix sort
+ * ranks the <= parents*cap survivors.  Outputs as grs_proposals_rank (rows
+ * index the [parents*k] candidate table); workspace from
+ * grs_proposals_grouped_workspace_bytes(parents, per_parent_cap). */
+GRS_API int64_t grs_proposals_grouped_workspace_bytes(int64_t parents, int per_parent_cap);
+GRS_API int grs_proposals_rank_grouped(const int64_t* sources, const float* probabilities,
+                                       int64_t parents, int k, const int64_t* parent_gate_counts,
+                                       const int32_t* xfer_offsets, const int32_t* xfer_counts,
+                                       const int32_t* xfer_ids, const int32_t* gate_deltas,
+                                       const int32_t* all_xfer_counts, int num_sources,
+                                       int per_parent_cap, int64_t global_cap, int64_t* out_row,
+                                       int64_t* out_xfer, int64_t* out_next_gate,
+                                       int64_t* out_count, int64_t* out_metrics, void* workspace,
+                                       int64_t workspace_bytes, int32_t* status, void* stream);
 
 /* Allocation-free variant of grs_proposals_rank (no counterpart in the
  * reference).  For callers that cannot allocate device memory when they rank

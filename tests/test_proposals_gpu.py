@@ -73,3 +73,36 @@ def test_random_vs_oracle(cuda_device, seed):
     np.testing.assert_array_equal(ranked.xfer_ids[:count].cpu().numpy(), sel["xfer"])
     np.testing.assert_array_equal(ranked.next_gate[:count].cpu().numpy(), sel["next_gate"])
     assert ranked.metrics.tolist() == [metrics["predicted_actions"], metrics["eligible_actions"]]
+
+
+@pytest.mark.parametrize("seed,k,cap", [(0, 80, 16), (1, 300, 5), (2, 2048, 16), (3, 7, 2000)])
+def test_grouped_matches_general(cuda_device, seed, k, cap):
+    """Padded parent-grouped layout: the shared-memory per-parent path equals
+    the general expansion + stable radix sort path, bit for bit."""
+    from graph_rewrite_system_b200.gpu_proposals import (GpuRuleIndex, rank_proposals_device,
+                                                         rank_proposals_grouped)
+    from graph_rewrite_system_b200.synthetic import synthetic_rules
+
+    rules = synthetic_rules()
+    rng = np.random.default_rng(seed)
+    parents = 120
+    n = parents * k
+    sources = rng.integers(0, rules.num_sources, n)
+    sources[rng.random(n) < 0.6] = -1                           # absent rows
+    probs = (1 / (1 + np.exp(-rng.integers(-20, 20, n) / 4.0))).astype(np.float32)  # ties
+    gates = rng.integers(250, 256, parents)
+    batch = np.repeat(np.arange(parents), k)
+    index = GpuRuleIndex.build(rules.source_to_xfers(), rules.gate_deltas(), rules.num_sources, 1,
+                               cuda_device)
+    d = lambda a: torch.from_numpy(np.asarray(a)).to(cuda_device)
+    general = rank_proposals_device(d(batch), d(sources), d(probs), d(gates), index,
+                                    per_parent_cap=cap, global_cap=1500)
+    grouped = rank_proposals_grouped(d(sources), d(probs), k, d(gates), index,
+                                     per_parent_cap=cap, global_cap=1500)
+    assert int(general.status.item()) == 0 and int(grouped.status.item()) == 0
+    c = int(general.count.item())
+    assert int(grouped.count.item()) == c
+    assert torch.equal(grouped.rows[:c], general.rows[:c])
+    assert torch.equal(grouped.xfer_ids[:c], general.xfer_ids[:c])
+    assert torch.equal(grouped.next_gate[:c], general.next_gate[:c])
+    assert torch.equal(grouped.metrics, general.metrics)
