@@ -465,10 +465,9 @@ __global__ void __launch_bounds__(GRP_THREADS) prop_grouped_parent_kernel(
     __syncthreads();
   }
   const int n = min(s_base, GRP_MAX_EXPANDED);
-  // expansion index -> candidate row: recompute by a second scan pass is
-  // avoided by storing the row in a parallel array keyed by expansion index.
+  // Expansion index -> candidate row, from a second walk over the rows.
   __shared__ int16_t row_of[GRP_MAX_EXPANDED];
-  // (fill row_of: re-walk the rows; each thread writes its own range)
+  __syncthreads();  // every thread has read s_base before it is reset
   if (tid == 0) s_base = 0;
   __syncthreads();
   for (int r0 = 0; r0 < k; r0 += GRP_THREADS) {

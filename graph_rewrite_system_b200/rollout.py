@@ -122,6 +122,37 @@ class DeviceBeamSearch:
         self.summary = torch.zeros(6, device=dev, dtype=torch.int64)
         self.rows: list[StepRow] = []
         self.timer: StageTimer | None = None
+        self.validate = False
+
+    def _check_range(self, stage: str, name: str, t: torch.Tensor, low: int, high: int,
+                     allow_negative_one: bool = False) -> None:
+        """Validation mode: every index a later kernel dereferences is in range."""
+        if not self.validate or t.numel() == 0:
+            return
+        torch.cuda.synchronize(self.device)
+        v = t.long()
+        if allow_negative_one:
+            v = v[v != -1]
+            if v.numel() == 0:
+                return
+        lo, hi = int(v.min().item()), int(v.max().item())
+        if lo < low or hi >= high:
+            raise RuntimeError(f"validation: {stage}: {name} in [{lo}, {hi}] outside "
+                               f"[{low}, {high}) at depth {self.depth}")
+
+    def _check_tables(self, stage: str, table: torch.Tensor, lengths: torch.Tensor) -> None:
+        if not self.validate:
+            return
+        torch.cuda.synchronize(self.device)
+        page = self.cfg.page_size
+        cols = table.shape[1]
+        need = (lengths.long() + page - 1) // page
+        if int(need.max().item()) > cols:
+            raise RuntimeError(f"validation: {stage}: lengths need {int(need.max())} blocks, "
+                               f"table has {cols}")
+        mask = torch.arange(cols, device=table.device).unsqueeze(0) < need.unsqueeze(1)
+        used = table[mask]
+        self._check_range(stage, "page id", used, 0, self.cache.capacity)
 
     def _mark(self, name: str) -> None:
         if self.timer is not None:
@@ -162,6 +193,10 @@ class DeviceBeamSearch:
         b, s, depth = self.beams, self.slots, self.depth
         topo = self.topo
         ports = topo.ports()
+        for name, t in zip(("in_node", "in_port", "out_node", "out_port"), ports):
+            self._check_range("step start", name, t, 0, s if "node" in name else 4,
+                              allow_negative_one=True)
+        self._check_tables("step start", self.block_table, self.lengths)
         # 1-2. readout and match logits
         self._mark("readout")
         readout, _, _ = model.readout_incremental(
@@ -173,6 +208,10 @@ class DeviceBeamSearch:
         self._mark("candidates")
         cand = select_candidates_device(model, self.types, self.live, ports, topo.distance, logits,
                                         eligible, self.thresholds, cfg.max_candidates_per_state)
+        self._check_range("candidates", "anchor", cand["anchors"], 0, s)
+        self._check_range("candidates", "source", cand["sources"], 0, self.rules.num_sources,
+                          allow_negative_one=True)
+        self._check_range("candidates", "binding", cand["bindings"], 0, s, allow_negative_one=True)
         # 3. proposals (effective parent cap of paged_rollout_benchmark.py:963-966)
         cap = max(cfg.per_parent_cap, math.ceil(cfg.beam_size / max(1, b)) * 2)
         self._mark("proposals")
@@ -180,6 +219,10 @@ class DeviceBeamSearch:
         ranked = rank_proposals_grouped(cand["sources"], cand["probabilities"], k, topo.gate,
                                         self.rule_index, per_parent_cap=cap,
                                         global_cap=cfg.global_cap, status=self.status)
+        self._check_range("proposals", "row", ranked.rows, 0, cand["sources"].numel(),
+                          allow_negative_one=True)
+        self._check_range("proposals", "xfer", ranked.xfer_ids, 0, self.rules.num_xfers,
+                          allow_negative_one=True)
         # 4. plan + accept
         gcap = cfg.global_cap
         valid = torch.empty(gcap, device=dev, dtype=torch.uint8)
@@ -246,6 +289,13 @@ class DeviceBeamSearch:
             a_parent.data_ptr(), a_xfer.data_ptr(), a_source.data_ptr(), a_src.data_ptr(),
             a_src.shape[1], a_dst.data_ptr(), a_dst_types.data_ptr(), a_dst.shape[1], depth,
             self.status.data_ptr(), stream), "topology_materialize")
+        self._check_range("materialize", "parent", a_parent, 0, b)
+        self._check_range("materialize", "source slot", a_src, 0, s, allow_negative_one=True)
+        self._check_range("materialize", "destination slot", a_dst, 0, s_new,
+                          allow_negative_one=True)
+        for name, t in zip(("in_node", "in_port", "out_node", "out_port"), nxt.ports()):
+            self._check_range("materialize", name, t, 0, s_new if "node" in name else 4,
+                              allow_negative_one=True)
         # 6. model advance of the children, cache append, release the parents
         self._mark("advance")
         w = model.width
@@ -259,6 +309,7 @@ class DeviceBeamSearch:
         K.gather_beams(self.block_table, a_parent, table_par)
         lengths_par = torch.empty(accepted, device=dev, dtype=torch.int32)
         K.gather_beams(self.lengths, a_parent, lengths_par)
+        self._check_tables("advance", table_par, lengths_par)
         states, live, types, new_k, new_v, action = model.advance_device(
             states_par, live_par, types_par, a_xfer, a_source, a_src, a_dst, a_dst_types,
             self.cache.keys, self.cache.values, table_par, lengths_par)
@@ -267,6 +318,7 @@ class DeviceBeamSearch:
         child_cols = -(-(depth + 1) // cfg.page_size)
         child_table, child_lengths = self.cache.append_device(
             table_par, lengths_par, new_k, new_v, action, rk, rv, child_cols=child_cols)
+        self._check_tables("append", child_table, child_lengths)
         self.cache.release_device(self.block_table, self.lengths)
         self.states, self.live, self.types = states, live, types
         self.block_table, self.lengths = child_table, child_lengths
