@@ -71,6 +71,20 @@ def paged_attention(
         sk = shared_key.to(query.dtype).contiguous()
         sv = shared_value.to(query.dtype).contiguous()
         num_shared = sk.shape[0]
+    if (shared_key is not None and query.dtype == torch.bfloat16 and query_length == 1
+            and head_width == 32 and heads <= 8 and query.stride(3) == 1
+            and key_cache.stride(3) == 1 and value_cache.stride() == key_cache.stride()):
+        status = _lib.lib().grs_decode_attention_shared(
+            query.data_ptr(), query.stride(0), query.stride(1), key_cache.data_ptr(),
+            value_cache.data_ptr(), key_cache.stride(0), key_cache.stride(1),
+            key_cache.stride(2), block_table.data_ptr(), block_table.stride(0),
+            block_table.shape[1], lengths.data_ptr(), key_cache.shape[0], _lib.ptr(ck),
+            _lib.ptr(cv), ck_sb, ck_sh,
+            _lib.ptr(valid), sk.data_ptr(), sv.data_ptr(), num_shared, output.data_ptr(),
+            output.stride(0), output.stride(1), batch, heads, key_cache.shape[1],
+            _lib.stream_of(query))
+        if status == 0:
+            return output
     status = _lib.lib().grs_paged_attention(
         _lib.DTYPE_CODES[query.dtype],
         query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),

@@ -28,6 +28,17 @@ class DecodeAttentionWorkload:
     distinct_pages: int
 
     @property
+    def logical_bytes(self) -> int:
+        """Q + O + shared K/V once + every beam's history K/V counted per beam
+        (pages shared through the prefix tree counted once per beam that
+        reads them) + block table + lengths."""
+        e = self.query.element_size()
+        b, h, q, d = self.query.shape
+        history = int(self.lengths.sum().item()) * h * d * e * 2
+        return (2 * b * h * q * d * e + 2 * self.shared_key.numel() * e + history
+                + self.block_table.numel() * 4 + self.lengths.numel() * 4)
+
+    @property
     def unique_bytes(self) -> int:
         """Algorithmic HBM bytes of one launch: Q + O + shared K/V once +
         every distinct referenced page (K and V) + block table + lengths."""

@@ -62,6 +62,26 @@ GRS_API int grs_paged_attention(int dtype, const void* query, int64_t q_sb, int6
                         int query_len, int head_width, int page_size, int max_blocks,
                         int num_pages, void* stream);
 
+/* Shared-prefix decode (bf16, head width 32, one query, heads <= 8): the
+ * same semantics as grs_paged_attention with query_len 1 (token order:
+ * shared prefix, pages, current token), in one launch of 8-CTA clusters of
+ * 16 beams; the shared keys are split across the cluster and combined
+ * through distributed shared memory.  block_table rows hold max_blocks
+ * entries.  Requires 16-byte aligned query, cache
+ * and current tensors and strides that are multiples of 8 elements; returns
+ * GRS_ERR_SHAPE otherwise (the caller then uses grs_paged_attention). */
+GRS_API int grs_decode_attention_shared(const void* query, int64_t q_sb, int64_t q_sh,
+                                        const void* key_cache, const void* value_cache,
+                                        int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
+                                        const int32_t* block_table, int64_t bt_stride,
+                                        int max_blocks, const int32_t* lengths, int num_pages,
+                                        const void* current_key, const void* current_value,
+                                        int64_t ck_sb, int64_t ck_sh,
+                                        const uint8_t* current_valid, const void* shared_key,
+                                        const void* shared_value, int num_shared, void* output,
+                                        int64_t o_sb, int64_t o_sh, int batch, int heads,
+                                        int page_size, void* stream);
+
 /* ---- PagedKVCache device state: paged_cache.py:16-105 -------------------
  * refcounts int32 [capacity], free_list int32 [capacity] with its length in
  * free_count (device int32), last_pos int32 [capacity] release scratch.

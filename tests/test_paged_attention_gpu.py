@@ -116,3 +116,12 @@ def test_partial_current_triple_rejected(cuda_device):
         paged_attention(q, kc, kc, torch.zeros(1, 1, dtype=torch.int32, device=cuda_device),
                         torch.zeros(1, dtype=torch.int32, device=cuda_device),
                         current_key=torch.zeros(1, 1, 32, device=cuda_device))
+
+
+@pytest.mark.parametrize("batch,shared,current", [(37, 381, False), (16, 381, True),
+                                                  (5, 17, True), (48, 0, False)])
+def test_cluster_decode_shared_prefix(cuda_device, batch, shared, current):
+    """The 8-CTA cluster decode (shared prefix split across the cluster) vs the oracle."""
+    out, exp = _random_case(7 + batch, batch, 8, 32, 16, 200, 1, 64, torch.bfloat16, cuda_device,
+                            shared=shared, current=current)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
