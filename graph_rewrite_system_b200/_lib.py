@@ -25,6 +25,7 @@ ERRORS = {
     -7: (RuntimeError, "prefix handle length/block table mismatch"),
     -8: (RuntimeError, "workspace too small"),
     -9: (ValueError, "inputs exceed the library's fixed scratch capacity"),
+    -10: (RuntimeError, "an in-kernel wait timed out"),
 }
 
 DTYPE_CODES = {torch.bfloat16: 0, torch.float32: 1}

@@ -1,21 +1,42 @@
 // Shared-prefix paged decode attention in one launch of 8-CTA clusters
-// (bf16, head width 32, one query per beam and head).
+// (bf16, head width 32, one query per beam and head, page size a multiple
+// of 16).
 //
-// Every beam attends to the same `num_shared` s0 node keys/values and to its
-// own block-table pages (+ an optional current token).  A cluster owns 16
-// beams.  Phase 1: CTA r of the cluster computes, for all 16 beams and every
-// head, the softmax partial (max, sum, P.V) over its 1/8 slice of the shared
-// keys with mma.m16n8k16 tiles (the 16 beams are the M dimension), so the
-// shared prefix is read from L2 once per CTA instead of once per beam.
-// The slice is staged into shared memory with cp.async first, and phase 2
-// runs while it lands: CTA r computes the partial over the pages of its two
-// beams, one warp per (beam, head), a quad of lanes per key, 16-byte loads,
-// eight keys in flight per lane.  Each CTA pushes the phase-1 partials of
-// every beam into the shared memory of the beam's owner (CTA beam/2); phase
-// 3, after one cluster barrier, merges the eight pushed partials with the
-// owner's page partial from local shared memory and writes the output.  Keys
-// whose page id is outside the cache are skipped.
+// Every beam attends to the same `num_shared` s0 node keys/values, to its own
+// block-table pages and to an optional current token.  A cluster owns 16
+// beams (the M dimension of mma.m16n8k16) and splits their keys into units
+// of 16 rows:
+//
+//   shared units   16 consecutive shared keys
+//   page units     16 rows of a page that one or more of the 16 beams hold
+//                  in the same block-table column (deduplicated, so a page
+//                  the beams share through copy-on-write is read once per
+//                  cluster, not once per beam)
+//   current unit   the 16 beams' current tokens
+//
+// Each CTA of the cluster takes every eighth shared unit and every eighth
+// page/current unit.  Warp 8 of the CTA is the producer: per unit it issues
+// TMA tile loads (cp.async.bulk.tensor, 16 rows x 128 bytes, 128-byte
+// swizzle, no multicast) of the K and V rows of all heads into a ring of
+// five stages, completion counted on the stage's "full" mbarrier.  The shared
+// units go out at kernel entry, before the block tables are read.  Warps 0-7
+// are the consumers, one per head: each waits for a stage, computes the
+// masked online-softmax partial (max, sum, P.V) of its head for all 16 beams
+// with ldmatrix-fed mma tiles, and releases the stage on its "empty"
+// mbarrier.  Each CTA then pushes its partials into the shared memory of the
+// beams' owners (CTA beam/2); after one cluster barrier the owners merge the
+// eight partials and write the output.
+//
+// Every mbarrier wait is bounded: a wait that runs out records
+// GRS_ERR_TIMEOUT in the caller's status word and the kernel finishes
+// without the missing data.  Keys whose page id is outside the cache are
+// skipped.
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
 
 #include "grs_common.cuh"
 
@@ -25,406 +46,513 @@ namespace grs {
 
 constexpr int DC_CLUSTER = 8;
 constexpr int DC_BEAMS = 16;          // beams per cluster (mma M)
-constexpr int DC_WARPS = 8;
+constexpr int DC_CONSUMERS = 8;       // warps 0-7, one per head
+constexpr int DC_PRODUCER = DC_CONSUMERS;
+constexpr int DC_THREADS = (DC_CONSUMERS + 1) * 32;
 constexpr int DC_D = 32;
-constexpr int DC_MAXH = DC_WARPS;  // heads <= warps
-constexpr int DC_MAX_CHUNK = 64;      // shared keys per CTA
+constexpr int DC_UNIT = 16;           // rows per unit / stage (one mma tile of keys)
+constexpr int DC_NBUF = 5;            // stages in the ring
+constexpr int DC_BOX_BYTES = DC_UNIT * 128;              // one TMA tile: 16 rows x 128 B
+constexpr int DC_STAGE_BYTES = 2 * 4 * DC_BOX_BYTES;     // K and V, up to 4 tiles each
+constexpr int DC_MAX_COLS = 32;       // block-table columns
+constexpr int DC_MAX_UNITS = 64;      // page/current units per CTA
+constexpr int DC_SPIN_LIMIT = 1 << 22;   // mbarrier polls before a wait gives up
 
 struct DecodeArgs {
   const __nv_bfloat16* q; int64_t q_sb, q_sh;
-  const __nv_bfloat16* kc; const __nv_bfloat16* vc; int64_t kc_sp, kc_st, kc_sh;
   const int32_t* bt; int64_t bt_s; int max_blocks; const int32_t* lengths; int num_pages;
-  const __nv_bfloat16* ck; const __nv_bfloat16* cv; int64_t ck_sb, ck_sh; const uint8_t* cvalid;
-  const __nv_bfloat16* sk; const __nv_bfloat16* sv; int num_shared; int chunk;
+  const uint8_t* cvalid; int has_current;
+  int num_shared;
   __nv_bfloat16* out; int64_t o_sb, o_sh;
+  int32_t* status;
   int B, H, page; float scale_log2;
 };
 
 struct Partial { float m, l, acc[DC_D]; };
 
-// Shared-key slice staged in shared memory: [key][head][32] rows padded to
-// H*32+8 elements so the eight fragment rows of an mma tile hit distinct banks.
-__device__ __forceinline__ int stage_stride(int H) { return H * DC_D + 8; }
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
-  const unsigned saddr = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(gmem),
-               "r"(src_bytes)
+// ---- mbarrier and TMA primitives (PTX ISA 8.x) ---------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// bounded wait for the phase with the given parity to complete
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  for (int i = 0; i < DC_SPIN_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+// TMA tile loads into this CTA's shared memory (no multicast)
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
 }
 
-__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], const uint32_t b[2]) {
+__device__ __forceinline__ void ldmatrix_x4(uint32_t r[4], unsigned addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t r[4], unsigned addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0,
+                                         uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
-__device__ __forceinline__ uint32_t pack2raw(__nv_bfloat16 lo, __nv_bfloat16 hi) {
-  __nv_bfloat162 v; v.x = lo; v.y = hi;
-  return *reinterpret_cast<uint32_t*>(&v);
+
+// Address of the 16-byte chunk `chunk` (0-7) of row `row` in a 16 x 128-byte
+// tile written by TMA with 128-byte swizzle (tile base 1024-byte aligned).
+__device__ __forceinline__ unsigned swz(unsigned tile, int row, int chunk) {
+  return tile + row * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
-__device__ __forceinline__ void unpack8(const uint4 x, float out[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f = __bfloat1622float2(h[j]);
-    out[2 * j] = f.x;
-    out[2 * j + 1] = f.y;
-  }
+// barrier among the consumer warps only (the producer keeps streaming)
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;\n" ::"n"(DC_CONSUMERS * 32) : "memory");
+}
+// the consumers publish the page units (arrive); the producer waits for them
+__device__ __forceinline__ void units_ready_arrive() {
+  asm volatile("bar.arrive 2, %0;\n" ::"n"(DC_THREADS) : "memory");
+}
+__device__ __forceinline__ void units_ready_wait() {
+  asm volatile("bar.sync 2, %0;\n" ::"n"(DC_THREADS) : "memory");
 }
 
-__device__ __forceinline__ float dot8(const uint4 x, const float q[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
-  float d = 0.f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f = __bfloat1622float2(h[j]);
-    d += q[2 * j] * f.x + q[2 * j + 1] * f.y;
-  }
-  return d;
-}
+__global__ void __cluster_dims__(DC_CLUSTER, 1, 1) __launch_bounds__(DC_THREADS, 2)
+decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
+                      const __grid_constant__ CUtensorMap tm_sv,
+                      const __grid_constant__ CUtensorMap tm_kc,
+                      const __grid_constant__ CUtensorMap tm_vc,
+                      const __grid_constant__ CUtensorMap tm_ck,
+                      const __grid_constant__ CUtensorMap tm_cv) {
+  // inbox[slot][head][r]: CTA r's partial for local beam `slot` of this CTA,
+  // written by CTA r into this CTA's shared memory
+  __shared__ Partial inbox[2][DC_CONSUMERS][DC_CLUSTER];
+  __shared__ __align__(8) uint64_t full_bar[DC_NBUF], empty_bar[DC_NBUF];
+  __shared__ int s_len[DC_BEAMS], s_cur[DC_BEAMS];
+  __shared__ int s_bt[DC_MAX_COLS][DC_BEAMS];
+  // distinct (column, page) entries: page id, column << 16 | beam mask
+  __shared__ int s_entry_page[DC_BEAMS * DC_MAX_COLS];
+  __shared__ int s_entry_cm[DC_BEAMS * DC_MAX_COLS];
+  __shared__ int s_entries, s_nunits;
+  // this CTA's page/current units: page id (-1: the current unit), first row
+  // in the page, beam mask, position of the first row, rows that are keys
+  __shared__ int4 s_unit[DC_MAX_UNITS];
+  extern __shared__ __align__(1024) unsigned char dyn[];
 
-__device__ __forceinline__ void axpy8(const uint4 x, float p, float acc[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f = __bfloat1622float2(h[j]);
-    acc[2 * j] += p * f.x;
-    acc[2 * j + 1] += p * f.y;
-  }
-}
-
-__global__ void __cluster_dims__(DC_CLUSTER, 1, 1) __launch_bounds__(DC_WARPS * 32, 2)
-decode_cluster_kernel(DecodeArgs a) {
-  // inbox[slot][head][r]: CTA r's shared-key partial for local beam slot
-  // `slot` of this CTA, written by CTA r into this CTA's shared memory
-  __shared__ Partial inbox[2][DC_MAXH][DC_CLUSTER];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
-  const int cluster_id = blockIdx.x / DC_CLUSTER;
-  const int beam0 = cluster_id * DC_BEAMS;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int beam0 = (blockIdx.x / DC_CLUSTER) * DC_BEAMS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tig = lane & 3;
   // every CTA of the cluster must be running before another writes into its
   // shared memory: arrive now, wait just before the first remote store
   asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
 
-  // ---- stage this CTA's shared-key slice (asynchronous, zero-filled) --------
-  extern __shared__ __align__(16) unsigned char dyn[];
-  __nv_bfloat16* ks_s = reinterpret_cast<__nv_bfloat16*>(dyn);
-  const int sstride = stage_stride(a.H);
-  __nv_bfloat16* vs_s = ks_s + (size_t)a.chunk * sstride;
-  const int k0 = rank * a.chunk;
-  const int kn = max(0, min(a.chunk, a.num_shared - k0));
-  {
-    const int vec_per_key = a.H * DC_D / 8;              // 16-byte vectors per key row
-    const int total = a.chunk * vec_per_key;
-    for (int i = threadIdx.x; i < total; i += DC_WARPS * 32) {
-      const int key = i / vec_per_key, v = i % vec_per_key;
-      const int h = v / (DC_D / 8), part = v % (DC_D / 8);
-      const bool ok = key < kn;
-      const int64_t goff = ((int64_t)(k0 + (ok ? key : 0)) * a.H + h) * DC_D + part * 8;
-      const size_t soff = (size_t)key * sstride + h * DC_D + part * 8;
-      cp_async16(ks_s + soff, a.sk + (ok ? goff : 0), ok ? 16 : 0);
-      cp_async16(vs_s + soff, a.sv + (ok ? goff : 0), ok ? 16 : 0);
-    }
-  }
+  // the ring, 1024-byte aligned for the 128-byte swizzle
+  const unsigned ring = (smem_addr(dyn) + 1023u) & ~1023u;
+  const int tiles = (a.H * DC_D + 63) / 64;              // 128-byte tiles per key row
+  const unsigned stage_bytes = 2u * tiles * DC_BOX_BYTES;
+  const int ns = a.num_shared;
+  const int sh_units = (ns + DC_UNIT - 1) / DC_UNIT;
+  // this CTA's shared units: rank, rank + 8, ...
+  const int my_sh = sh_units > rank ? (sh_units - rank + DC_CLUSTER - 1) / DC_CLUSTER : 0;
 
-  // ---- phase 2: the pages of this CTA's two beams ---------------------------
-  // warp task t = warp + 8*slot: local beam 2*rank + t / H, head t % H.  A key
-  // row (64 bytes of one head) is split over a quad of lanes, 16 bytes each;
-  // quad g takes keys g, g+8, ..., g+56 of a 64-key block, so every lane has
-  // eight K loads (to registers) and eight V copies (cp.async to a per-warp
-  // shared buffer) in flight before it uses one.  The lengths,
-  // validity flags and the first block's page ids of both slots are
-  // loaded up front (page ids speculatively, clamped to the table width), so
-  // each slot costs one dependent round trip to memory: its query and
-  // current token are loaded with its keys, and the current token is folded
-  // in after the pages.  Lane (g, t) ends holding dimension t*8 + g of the
-  // partial, which goes to shared memory for phase 3.
-  const int tasks = 2 * a.H;
-  __nv_bfloat16* vbuf = vs_s + (size_t)a.chunk * sstride + warp * 64 * DC_D;
-  // per warp and slot: history length, current-token flag, the first
-  // block's page ids (at most 64) and, after the pages, the partial
-  __shared__ int first_pages[DC_WARPS][2][64];
-  __shared__ int slot_len[DC_WARPS][2], slot_cur[DC_WARPS][2];
-  __shared__ Partial page_part[DC_WARPS][2];
-#pragma unroll
-  for (int slot = 0; slot < 2; ++slot) {
-    const int t = warp + slot * DC_WARPS;
-    const int b = t < tasks ? beam0 + 2 * rank + t / a.H : a.B;
-    const bool live = b < a.B;
-    const int past = live ? __ldg(a.lengths + b) : 0;
-    const int cur = live && a.ck != nullptr && __ldg(a.cvalid + b) != 0;
-    if (lane == 0) {
-      slot_len[warp][slot] = past;
-      slot_cur[warp][slot] = cur;
+  if (tid == 0) {
+    for (int i = 0; i < DC_NBUF; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], DC_CONSUMERS);
     }
-    const int first_blocks = min((64 + a.page - 1) / a.page, a.max_blocks);
-#pragma unroll
-    for (int j = lane; j < 64; j += 32)
-      if (live && j < first_blocks)
-        first_pages[warp][slot][j] = __ldg(a.bt + (int64_t)b * a.bt_s + j);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  __syncwarp();
-#pragma unroll 1
-  for (int slot = 0; slot < 2; ++slot) {
-    const int t = warp + slot * DC_WARPS;
-    const int b = t < tasks ? beam0 + 2 * rank + t / a.H : a.B, h = t % a.H;
-    float m = -INFINITY, l = 0.f, acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    // the query is not needed to address the keys: load it with them
-    const uint4 qpk = b < a.B ? __ldg(reinterpret_cast<const uint4*>(
-                                    a.q + (int64_t)b * a.q_sb + (int64_t)h * a.q_sh + tig * 8))
-                              : make_uint4(0, 0, 0, 0);
-    const int past = slot_len[warp][slot];
-    const bool cur = slot_cur[warp][slot] != 0;
-    uint4 ckr = make_uint4(0, 0, 0, 0), cvr = ckr;
-    if (cur) {
-      const int64_t off = (int64_t)b * a.ck_sb + (int64_t)h * a.ck_sh + tig * 8;
-      ckr = __ldg(reinterpret_cast<const uint4*>(a.ck + off));
-      cvr = __ldg(reinterpret_cast<const uint4*>(a.cv + off));
-    }
-    for (int base = 0; base < past; base += 64) {
-      // K rows to registers; V rows to this warp's shared buffer (each lane
-      // reads back only the 16-byte pieces it copied itself)
-      uint4 kr[8];
-      bool ok[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int tk = base + g + 8 * u;
-        ok[u] = false;
-        kr[u] = make_uint4(0, 0, 0, 0);
-        if (tk < past) {
-          const int pg = base == 0 ? first_pages[warp][slot][tk / a.page]
-                                   : __ldg(a.bt + (int64_t)b * a.bt_s + tk / a.page);
-          if (pg >= 0 && pg < a.num_pages) {
-            const int64_t off = (int64_t)pg * a.kc_sp + (int64_t)(tk % a.page) * a.kc_st +
-                                (int64_t)h * a.kc_sh + tig * 8;
-            kr[u] = __ldg(reinterpret_cast<const uint4*>(a.kc + off));
-            cp_async16(vbuf + (u * 8 + g) * DC_D + tig * 8, a.vc + off, 16);
-            ok[u] = true;
+  __syncthreads();
+
+  if (warp == DC_PRODUCER) {
+    // ---- producer: lane 0 issues the loads, the warp waits together ----
+    bool ok = true;
+    auto produce = [&](int st, int unit_page, int y0) {
+      const int buf = st % DC_NBUF;
+      if (st >= DC_NBUF)
+        ok = __all_sync(0xffffffffu, mbar_wait(&empty_bar[buf], (unsigned)((st / DC_NBUF - 1) & 1)));
+      if (ok && lane == 0) {
+        mbar_arrive_expect_tx(&full_bar[buf], stage_bytes);
+        unsigned char* kdst = dyn + (ring - smem_addr(dyn)) + buf * DC_STAGE_BYTES;
+        unsigned char* vdst = kdst + 4 * DC_BOX_BYTES;
+        for (int t = 0; t < tiles; ++t) {
+          if (unit_page == -2) {            // shared unit: rows y0..y0+15 of [N, H*32]
+            tma_load_2d(kdst + t * DC_BOX_BYTES, &tm_sk, t * 64, y0, &full_bar[buf]);
+            tma_load_2d(vdst + t * DC_BOX_BYTES, &tm_sv, t * 64, y0, &full_bar[buf]);
+          } else if (unit_page >= 0) {      // page unit: rows y0.. of [pages, page, H*32]
+            tma_load_3d(kdst + t * DC_BOX_BYTES, &tm_kc, t * 64, y0, unit_page, &full_bar[buf]);
+            tma_load_3d(vdst + t * DC_BOX_BYTES, &tm_vc, t * 64, y0, unit_page, &full_bar[buf]);
+          } else {                          // current unit: the beams' rows of [B, H*32]
+            tma_load_2d(kdst + t * DC_BOX_BYTES, &tm_ck, t * 64, beam0, &full_bar[buf]);
+            tma_load_2d(vdst + t * DC_BOX_BYTES, &tm_cv, t * 64, beam0, &full_bar[buf]);
           }
         }
       }
-      float qv[8];
-      unpack8(qpk, qv);
-      float sc[8];
-      float cm = -INFINITY;
+      __syncwarp();
+    };
+    // the shared units need no block table
+    for (int i = 0; i < my_sh && ok; ++i) produce(i, -2, (rank + i * DC_CLUSTER) * DC_UNIT);
+    // page/current units once the consumers have published them
+    __syncwarp();
+    units_ready_wait();
+    const int nu = s_nunits;
+    for (int i = 0; i < nu && ok; ++i) {
+      const int4 u = s_unit[i];
+      produce(my_sh + i, u.x, u.y);
+    }
+    if (!ok && lane == 0 && a.status) atomicCAS(a.status, 0, GRS_ERR_TIMEOUT);
+    __syncwarp();
+  } else {
+    // ---- consumers: metadata, then the stages ----------------------------
+    // 1. lengths, current-token flags, block-table columns (one round trip)
+    const int cols = a.max_blocks;   // <= DC_MAX_COLS (host-checked)
+    if (tid < DC_BEAMS) {
+      const int b = beam0 + tid;
+      s_len[tid] = b < a.B ? a.lengths[b] : 0;
+      s_cur[tid] = (b < a.B && a.has_current) ? (a.cvalid[b] != 0) : 0;
+    }
+    for (int i = tid; i < cols * DC_BEAMS; i += DC_CONSUMERS * 32) {
+      const int c = i >> 4, j = i & 15, b = beam0 + j;
+      s_bt[c][j] = b < a.B ? a.bt[(int64_t)b * a.bt_s + c] : -1;
+    }
+    // query fragments of head `warp` for the 16 beams (A operand, rows = beams)
+    uint32_t qa[2][4] = {};
+    if (warp < a.H) {
+      const int r0 = beam0 + g, r1 = beam0 + g + 8;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float d = dot8(kr[u], qv);
-        d += __shfl_xor_sync(0xffffffffu, d, 1);
-        d += __shfl_xor_sync(0xffffffffu, d, 2);
-        sc[u] = ok[u] ? d * a.scale_log2 : -INFINITY;
-        cm = fmaxf(cm, sc[u]);
-      }
-      cm = warp_max(cm);
-      const float nm = fmaxf(m, cm);
-      const float corr = (m == -INFINITY || nm == -INFINITY) ? 0.f : exp2f(m - nm);
-      l *= corr;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] *= corr;
-      cp_async_wait_all();
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (ok[u]) {
-          const float p = exp2f(sc[u] - nm);
-          l += p;
-          axpy8(*reinterpret_cast<const uint4*>(vbuf + (u * 8 + g) * DC_D + tig * 8), p, acc);
+      for (int ks = 0; ks < 2; ++ks) {
+        const int c = ks * 16 + tig * 2;
+        const __nv_bfloat16* p0 = a.q + (int64_t)r0 * a.q_sb + (int64_t)warp * a.q_sh + c;
+        const __nv_bfloat16* p1 = a.q + (int64_t)r1 * a.q_sb + (int64_t)warp * a.q_sh + c;
+        if (r0 < a.B) {
+          qa[ks][0] = *reinterpret_cast<const uint32_t*>(p0);
+          qa[ks][2] = *reinterpret_cast<const uint32_t*>(p0 + 8);
+        }
+        if (r1 < a.B) {
+          qa[ks][1] = *reinterpret_cast<const uint32_t*>(p1);
+          qa[ks][3] = *reinterpret_cast<const uint32_t*>(p1 + 8);
         }
       }
-      m = nm;
     }
-    // the current token: every quad scores it, quad 0 alone accumulates it
-    float qv[8];
-    unpack8(qpk, qv);
-    float d = dot8(ckr, qv);
-    d += __shfl_xor_sync(0xffffffffu, d, 1);
-    d += __shfl_xor_sync(0xffffffffu, d, 2);
-    if (cur) {
-      const float sc = d * a.scale_log2;
-      const float nm = fmaxf(m, sc);
-      const float corr = m == -INFINITY ? 0.f : exp2f(m - nm);
-      const float p = g == 0 ? exp2f(sc - nm) : 0.f;
-      l = l * corr + p;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] *= corr;
-      axpy8(cvr, p, acc);
-      m = nm;
+    consumers_sync();
+
+    // 2. distinct pages per column: lanes 0-15 column c, 16-31 column c+1
+    if (warp == 0) {
+      int count = 0;
+      for (int c0 = 0; c0 < cols; c0 += 2) {
+        const int c = c0 + (lane >> 4), j = lane & 15;
+        int p = -1;
+        if (c < cols && c * a.page < s_len[j]) {
+          p = s_bt[c][j];
+          if (p >= a.num_pages) p = -1;
+        }
+        const unsigned long long key =
+            p >= 0 ? (((unsigned long long)(unsigned)p << 1) | (unsigned)(lane >> 4))
+                   : ((1ull << 63) | (unsigned)lane);
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        const bool lead = p >= 0 && __ffs(peers) - 1 == lane;
+        const unsigned leads = __ballot_sync(0xffffffffu, lead);
+        if (lead) {
+          const int e = count + __popc(leads & ((1u << lane) - 1u));
+          s_entry_page[e] = p;
+          s_entry_cm[e] = (c << 16) | ((peers >> (lane & 16)) & 0xFFFF);
+        }
+        count += __popc(leads);
+      }
+      if (lane == 0) s_entries = count;
     }
-    // sum over the eight quads; the halving exchange leaves lane (g, t)
-    // with element g of its quad slice, i.e. dimension t*8 + g
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-#pragma unroll
-    for (int half = 16, n = 4; half >= 4; half >>= 1, n >>= 1) {
-      const bool upper = (lane & half) != 0;
-#pragma unroll
-      for (int e = 0; e < n; ++e) {
-        const float send = upper ? acc[e] : acc[e + n];
-        const float keep = upper ? acc[e + n] : acc[e];
-        acc[e] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+    consumers_sync();
+
+    // 3. this CTA's page/current units: global unit u = entry * (page/16) +
+    //    sub-block, the current unit last; CTA r takes u = r, r + 8, ...
+    const int per_page = a.page / DC_UNIT;
+    const int page_units = s_entries * per_page;
+    const int all_units = page_units + (a.has_current ? 1 : 0);
+    const int nu = all_units > rank ? (all_units - rank + DC_CLUSTER - 1) / DC_CLUSTER : 0;
+    for (int i = tid; i < nu; i += DC_CONSUMERS * 32) {
+      const int u = rank + i * DC_CLUSTER;
+      if (u < page_units) {
+        const int e = u / per_page, sub = u - e * per_page;
+        const int cm = s_entry_cm[e];
+        s_unit[i] = make_int4(s_entry_page[e], sub * DC_UNIT, cm & 0xFFFF,
+                              (cm >> 16) * a.page + sub * DC_UNIT);
+      } else {
+        int mask = 0;
+        for (int j = 0; j < DC_BEAMS; ++j) mask |= s_cur[j] ? (1 << j) : 0;
+        s_unit[i] = make_int4(-1, 0, mask, -1);
       }
     }
-    page_part[warp][slot].acc[tig * 8 + g] = acc[0];
-    if (lane == 0) {
-      page_part[warp][slot].m = m;
-      page_part[warp][slot].l = l;
-    }
-  }
+    if (tid == 0) s_nunits = nu;
+    consumers_sync();
+    units_ready_arrive();
+    const int stages = my_sh + nu;
 
-  // ---- phase 1: shared-key slice, all 16 beams, mma tiles from shared memory
-  cp_async_wait_all();
-  __syncthreads();
-  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
-  for (int h = warp; h < a.H; h += DC_WARPS) {
-    uint32_t qa[2][4];
-    const int r0 = beam0 + g, r1 = beam0 + g + 8;
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      const int c = ks * 16 + tig * 2;
-      const __nv_bfloat16* p0 = a.q + (int64_t)r0 * a.q_sb + (int64_t)h * a.q_sh + c;
-      const __nv_bfloat16* p1 = a.q + (int64_t)r1 * a.q_sb + (int64_t)h * a.q_sh + c;
-      qa[ks][0] = r0 < a.B ? *reinterpret_cast<const uint32_t*>(p0) : 0u;
-      qa[ks][1] = r1 < a.B ? *reinterpret_cast<const uint32_t*>(p1) : 0u;
-      qa[ks][2] = r0 < a.B ? *reinterpret_cast<const uint32_t*>(p0 + 8) : 0u;
-      qa[ks][3] = r1 < a.B ? *reinterpret_cast<const uint32_t*>(p1 + 8) : 0u;
-    }
+    // 4. consume the ring
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float o[4][4] = {};
-    for (int base = 0; base < kn; base += 16) {
-      float s[2][4];
+    const int h = warp;
+    const int len0 = s_len[g], len1 = s_len[g + 8];
+    bool ok = true;
+    for (int st = 0; st < stages; ++st) {
+      const int buf = st % DC_NBUF;
+      if (ok) ok = mbar_wait(&full_bar[buf], (unsigned)((st / DC_NBUF) & 1));
+      if (ok && h < a.H) {
+        // visibility of the stage's 16 rows for beams g (v0) and g + 8 (v1)
+        int kind, mask = 0xFFFF, pos0 = -1, rows = DC_UNIT;
+        if (st < my_sh) {
+          kind = 0;
+          rows = min(DC_UNIT, ns - (rank + st * DC_CLUSTER) * DC_UNIT);
+        } else {
+          const int4 u = s_unit[st - my_sh];
+          kind = u.x >= 0 ? 1 : 2;
+          mask = u.z;
+          pos0 = u.w;
+        }
+        const bool see0 = (mask >> g) & 1, see1 = (mask >> (g + 8)) & 1;
+        const unsigned kt = ring + buf * DC_STAGE_BYTES + (h >> 1) * DC_BOX_BYTES;
+        const unsigned vt = kt + 4 * DC_BOX_BYTES;
+        const int hc = (h & 1) * 4;                    // chunk of this head in the tile row
+        float s[2][4] = {};
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-        const __nv_bfloat16* kr = ks_s + (size_t)(base + nt * 8 + g) * sstride + h * DC_D;
+        for (int nt = 0; nt < 2; ++nt) {
+          uint32_t kf[4];
+          ldmatrix_x4(kf, swz(kt, nt * 8 + (lane & 7), hc + (lane >> 3)));
+          mma16816(s[nt], qa[0], kf[0], kf[1]);
+          mma16816(s[nt], qa[1], kf[2], kf[3]);
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          uint32_t bf[2];
-          bf[0] = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + tig * 2);
-          bf[1] = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + tig * 2 + 8);
-          mma16816(s[nt], qa[ks], bf);
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int r = nt * 8 + tig * 2 + c;
+            bool v0, v1;
+            if (kind == 0) {
+              v0 = v1 = r < rows;
+            } else if (kind == 1) {
+              v0 = see0 && pos0 + r < len0;
+              v1 = see1 && pos0 + r < len1;
+            } else {                                   // row r is beam r's current token
+              v0 = see0 && r == g;
+              v1 = see1 && r == g + 8;
+            }
+            s[nt][c] = v0 ? s[nt][c] * a.scale_log2 : -INFINITY;
+            s[nt][2 + c] = v1 ? s[nt][2 + c] * a.scale_log2 : -INFINITY;
+            mx0 = fmaxf(mx0, s[nt][c]);
+            mx1 = fmaxf(mx1, s[nt][2 + c]);
+          }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+        const float c0 = m0 == -INFINITY ? 0.f : exp2f(m0 - n0);
+        const float c1 = m1 == -INFINITY ? 0.f : exp2f(m1 - n1);
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            s[nt][c] = s[nt][c] == -INFINITY ? 0.f : exp2f(s[nt][c] - n0);
+            s[nt][2 + c] = s[nt][2 + c] == -INFINITY ? 0.f : exp2f(s[nt][2 + c] - n1);
+            sum0 += s[nt][c];
+            sum1 += s[nt][2 + c];
+          }
+        // per-lane partial row sums; the quad reduction happens once at the end
+        l0 = l0 * c0 + sum0;
+        l1 = l1 * c1 + sum1;
+        m0 = n0;
+        m1 = n1;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          o[nt][0] *= c0; o[nt][1] *= c0; o[nt][2] *= c1; o[nt][3] *= c1;
+        }
+        uint32_t pa[4];
+        pa[0] = pack2(s[0][0], s[0][1]);
+        pa[1] = pack2(s[0][2], s[0][3]);
+        pa[2] = pack2(s[1][0], s[1][1]);
+        pa[3] = pack2(s[1][2], s[1][3]);
+#pragma unroll
+        for (int dp = 0; dp < 2; ++dp) {
+          // four 8x8 tiles: keys 0-7 / 8-15 x dims dp*16 + 0-7 / 8-15
+          uint32_t vf[4];
+          ldmatrix_x4_trans(vf, swz(vt, (lane & 7) + ((lane >> 3) & 1) * 8,
+                                    hc + dp * 2 + (lane >> 4)));
+          mma16816(o[2 * dp], pa, vf[0], vf[1]);
+          mma16816(o[2 * dp + 1], pa, vf[2], vf[3]);
         }
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const bool ok = base + nt * 8 + tig * 2 + c < kn;
-          s[nt][c] = ok ? s[nt][c] * a.scale_log2 : -INFINITY;
-          s[nt][2 + c] = ok ? s[nt][2 + c] * a.scale_log2 : -INFINITY;
-          mx0 = fmaxf(mx0, s[nt][c]);
-          mx1 = fmaxf(mx1, s[nt][2 + c]);
-        }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-      const float c0 = m0 == -INFINITY ? 0.f : exp2f(m0 - n0);
-      const float c1 = m1 == -INFINITY ? 0.f : exp2f(m1 - n1);
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          s[nt][c] = s[nt][c] == -INFINITY ? 0.f : exp2f(s[nt][c] - n0);
-          s[nt][2 + c] = s[nt][2 + c] == -INFINITY ? 0.f : exp2f(s[nt][2 + c] - n1);
-          sum0 += s[nt][c];
-          sum1 += s[nt][2 + c];
-        }
-      sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
-      sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
-      sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
-      sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
-      l0 = l0 * c0 + sum0;
-      l1 = l1 * c1 + sum1;
-      m0 = n0;
-      m1 = n1;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[buf]);
+    }
+    if (!ok && lane == 0 && a.status) atomicCAS(a.status, 0, GRS_ERR_TIMEOUT);
+
+    // 5. push the partials of beams g and g+8 to their owners
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+    if (h < a.H) {
+      Partial* d0 = cluster.map_shared_rank(&inbox[g & 1][h][rank], g >> 1);
+      Partial* d1 = cluster.map_shared_rank(&inbox[g & 1][h][rank], (g >> 1) + 4);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        o[nt][0] *= c0; o[nt][1] *= c0; o[nt][2] *= c1; o[nt][3] *= c1;
+        const int d = nt * 8 + tig * 2;
+        *reinterpret_cast<float2*>(&d0->acc[d]) = make_float2(o[nt][0], o[nt][1]);
+        *reinterpret_cast<float2*>(&d1->acc[d]) = make_float2(o[nt][2], o[nt][3]);
       }
-      uint32_t pa[4];
-      pa[0] = pack2(s[0][0], s[0][1]);
-      pa[1] = pack2(s[0][2], s[0][3]);
-      pa[2] = pack2(s[1][0], s[1][1]);
-      pa[3] = pack2(s[1][2], s[1][3]);
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const int dim = h * DC_D + nt * 8 + g;
-        const int kr0 = base + tig * 2, kr1 = base + tig * 2 + 8;
-        uint32_t bf[2];
-        bf[0] = pack2raw(vs_s[(size_t)kr0 * sstride + dim], vs_s[(size_t)(kr0 + 1) * sstride + dim]);
-        bf[1] = pack2raw(vs_s[(size_t)kr1 * sstride + dim], vs_s[(size_t)(kr1 + 1) * sstride + dim]);
-        mma16816(o[nt], pa, bf);
+      if (tig == 0) {
+        d0->m = m0; d0->l = l0;
+        d1->m = m1; d1->l = l1;
       }
-    }
-    // push the partials of beams g and g+8 to their owners (CTA beam/2)
-    Partial* d0 = cluster.map_shared_rank(&inbox[g & 1][h][rank], g >> 1);
-    Partial* d1 = cluster.map_shared_rank(&inbox[g & 1][h][rank], (g >> 1) + 4);
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int d = nt * 8 + tig * 2;
-      *reinterpret_cast<float2*>(&d0->acc[d]) = make_float2(o[nt][0], o[nt][1]);
-      *reinterpret_cast<float2*>(&d1->acc[d]) = make_float2(o[nt][2], o[nt][3]);
-    }
-    if (tig == 0) {
-      d0->m = m0; d0->l = l0;
-      d1->m = m1; d1->l = l1;
     }
   }
+  if (warp == DC_PRODUCER) asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
 
-  // ---- phase 3: merge with the eight prefix partials ------------------------
-  // One cluster barrier makes every pushed partial visible; after it no CTA
-  // touches another's shared memory, so none has to wait for the others.
+  // ---- 6. merge: one cluster barrier makes every pushed partial visible;
+  // after it no CTA touches another's shared memory
   cluster.sync();
-#pragma unroll
-  for (int slot = 0; slot < 2; ++slot) {
-    const int t = warp + slot * DC_WARPS;
-    if (t >= tasks) continue;
-    const int ls = t / a.H, h = t % a.H;
-    const int b = beam0 + 2 * rank + ls;
-    // lane (g, t) holds dimension t*8 + g of the page partial
-    const int dim = tig * 8 + g;
-    float mr[DC_CLUSTER], lr[DC_CLUSTER], ar[DC_CLUSTER];
+  if (warp < a.H) {
+    const int h = warp, slot = lane >> 4, d = (lane & 15) * 2;
+    const int b = beam0 + 2 * rank + slot;
+    float mr[DC_CLUSTER], lr[DC_CLUSTER], ar[DC_CLUSTER], br[DC_CLUSTER];
 #pragma unroll
     for (int r = 0; r < DC_CLUSTER; ++r) {
-      const Partial& p = inbox[ls][h][r];
+      const Partial& p = inbox[slot][h][r];
       mr[r] = p.m;
       lr[r] = p.l;
-      ar[r] = p.acc[dim];
+      const float2 v = *reinterpret_cast<const float2*>(&p.acc[d]);
+      ar[r] = v.x;
+      br[r] = v.y;
     }
-    const Partial& pp = page_part[warp][slot];
-    const float m = pp.m;
-    float M = m;
+    float M = -INFINITY;
 #pragma unroll
     for (int r = 0; r < DC_CLUSTER; ++r) M = fmaxf(M, mr[r]);
-    const float wp = m == -INFINITY ? 0.f : exp2f(m - M);
-    float L = pp.l * wp, O = pp.acc[dim] * wp;
+    float L = 0.f, O0 = 0.f, O1 = 0.f;
 #pragma unroll
     for (int r = 0; r < DC_CLUSTER; ++r) {
       const float w = mr[r] == -INFINITY ? 0.f : exp2f(mr[r] - M);
       L += lr[r] * w;
-      O += ar[r] * w;
+      O0 += ar[r] * w;
+      O1 += br[r] * w;
     }
-    if (b < a.B)
-      a.out[(int64_t)b * a.o_sb + (int64_t)h * a.o_sh + dim] =
-          __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+    if (b < a.B) {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      *reinterpret_cast<__nv_bfloat162*>(a.out + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + d) =
+          __floats2bfloat162_rn(O0 * inv, O1 * inv);
+    }
   }
+}
+
+// ---- host: tensor maps ----------------------------------------------------
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// libcuda link), with a small cache keyed by every encoded field.
+struct MapKey {
+  const void* base; int rank; uint64_t dims[3]; uint64_t strides[2];
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor of `rank` (2 or 3) dims, innermost first; tiles of 64 x 16 (x 1)
+static bool tile_map(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes) {
+  constexpr int kCache = 32;
+  static MapKey keys[kCache];
+  static CUtensorMap maps[kCache];
+  static int used = 0, next = 0;
+  static std::mutex mu;
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));
+  k.base = base;
+  k.rank = rank;
+  for (int i = 0; i < rank; ++i) k.dims[i] = dims[i];
+  for (int i = 0; i < rank - 1; ++i) k.strides[i] = strides_bytes[i];
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (keys[i] == k) {
+      *out = maps[i];
+      return true;
+    }
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t gdim[3], gstr[2];
+  cuuint32_t box[3] = {64, DC_UNIT, 1}, estr[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) gdim[i] = dims[i];
+  for (int i = 0; i < rank - 1; ++i) gstr[i] = strides_bytes[i];
+  CUtensorMap m;
+  if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), gdim,
+         gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  keys[next] = k;
+  maps[next] = m;
+  next = (next + 1) % kCache;
+  used = used < kCache ? used + 1 : kCache;
+  *out = m;
+  return true;
 }
 
 }  // namespace grs
@@ -435,47 +563,69 @@ extern "C" int grs_decode_attention_shared(
     const void* query, int64_t q_sb, int64_t q_sh, const void* key_cache,
     const void* value_cache, int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
     const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* lengths,
-    int num_pages,
-    const void* current_key, const void* current_value, int64_t ck_sb, int64_t ck_sh,
-    const uint8_t* current_valid, const void* shared_key, const void* shared_value,
-    int num_shared, void* output, int64_t o_sb, int64_t o_sh, int batch, int heads,
-    int page_size, void* stream) {
+    int num_pages, const void* current_key, const void* current_value, int64_t ck_sb,
+    int64_t ck_sh, const uint8_t* current_valid, const void* shared_key,
+    const void* shared_value, int num_shared, void* output, int64_t o_sb, int64_t o_sh,
+    int batch, int heads, int page_size, int32_t* status, void* stream) {
   if (batch <= 0) return GRS_OK;
-  // two (beam, head) page tasks per warp: heads <= DC_WARPS
-  if (heads <= 0 || heads > DC_WARPS || page_size <= 0 || num_shared < 0 || max_blocks <= 0)
+  if (heads <= 0 || heads > DC_CONSUMERS || page_size <= 0 || page_size % DC_UNIT ||
+      num_shared < 0 || num_pages <= 0 || max_blocks <= 0 || max_blocks > DC_MAX_COLS)
     return GRS_ERR_SHAPE;
-  int chunk = (num_shared + DC_CLUSTER - 1) / DC_CLUSTER;
-  chunk = (chunk + 15) / 16 * 16;
-  if (chunk > DC_MAX_CHUNK) return GRS_ERR_SHAPE;
+  // page/current units of one CTA: at most 16 distinct pages per column
+  const int64_t max_units =
+      (int64_t)DC_BEAMS * max_blocks * (page_size / DC_UNIT) + (current_key ? 1 : 0);
+  if ((max_units + DC_CLUSTER - 1) / DC_CLUSTER > DC_MAX_UNITS) return GRS_ERR_SHAPE;
   if ((current_key == nullptr) != (current_value == nullptr) ||
       (current_key == nullptr) != (current_valid == nullptr))
     return GRS_ERR_SHAPE;
+  // key rows (all heads of one token) are loaded as tiles: heads adjacent
+  // (head stride 32), rows 16-byte aligned
+  if (kc_sh != DC_D || (current_key && ck_sh != DC_D)) return GRS_ERR_SHAPE;
   if (((uintptr_t)query | (uintptr_t)key_cache | (uintptr_t)value_cache) & 15) return GRS_ERR_SHAPE;
   if (num_shared > 0 && ((uintptr_t)shared_key | (uintptr_t)shared_value) & 15) return GRS_ERR_SHAPE;
-  if ((q_sb | q_sh | kc_sp | kc_st | kc_sh) % 8) return GRS_ERR_SHAPE;
-  if (current_key && (((uintptr_t)current_key | (uintptr_t)current_value) & 15 || (ck_sb | ck_sh) % 8))
+  if ((q_sb | q_sh | kc_sp | kc_st) % 8) return GRS_ERR_SHAPE;
+  if (current_key && (((uintptr_t)current_key | (uintptr_t)current_value) & 15 || ck_sb % 8))
     return GRS_ERR_SHAPE;
-  DecodeArgs a{(const __nv_bfloat16*)query, q_sb, q_sh, (const __nv_bfloat16*)key_cache,
-               (const __nv_bfloat16*)value_cache, kc_sp, kc_st, kc_sh, block_table, bt_stride,
-               max_blocks, lengths, num_pages, (const __nv_bfloat16*)current_key,
-               (const __nv_bfloat16*)current_value, ck_sb, ck_sh, current_valid,
-               (const __nv_bfloat16*)shared_key, (const __nv_bfloat16*)shared_value, num_shared,
-               chunk, (__nv_bfloat16*)output, o_sb, o_sh, batch, heads, page_size,
+  if (((uintptr_t)output & 3) || (o_sb | o_sh) % 2) return GRS_ERR_SHAPE;
+
+  const uint64_t row = (uint64_t)heads * DC_D;           // elements per key row
+  CUtensorMap tm_kc, tm_vc, tm_sk, tm_sv, tm_ck, tm_cv;
+  {
+    const uint64_t dims[3] = {row, (uint64_t)page_size, (uint64_t)num_pages};
+    const uint64_t str[2] = {(uint64_t)kc_st * 2, (uint64_t)kc_sp * 2};
+    if (!tile_map(&tm_kc, key_cache, 3, dims, str) || !tile_map(&tm_vc, value_cache, 3, dims, str))
+      return GRS_ERR_SHAPE;
+  }
+  tm_sk = tm_sv = tm_ck = tm_cv = tm_kc;                 // placeholders for absent inputs
+  if (num_shared > 0) {
+    const uint64_t dims[2] = {row, (uint64_t)num_shared};
+    const uint64_t str[1] = {row * 2};
+    if (!tile_map(&tm_sk, shared_key, 2, dims, str) || !tile_map(&tm_sv, shared_value, 2, dims, str))
+      return GRS_ERR_SHAPE;
+  }
+  if (current_key) {
+    const uint64_t dims[2] = {row, (uint64_t)batch};
+    const uint64_t str[1] = {(uint64_t)ck_sb * 2};
+    if (!tile_map(&tm_ck, current_key, 2, dims, str) || !tile_map(&tm_cv, current_value, 2, dims, str))
+      return GRS_ERR_SHAPE;
+  }
+  DecodeArgs a{(const __nv_bfloat16*)query, q_sb, q_sh, block_table, bt_stride, max_blocks,
+               lengths, num_pages, current_valid, current_key != nullptr, num_shared,
+               (__nv_bfloat16*)output, o_sb, o_sh, status, batch, heads, page_size,
                1.4426950408889634f / sqrtf(32.f)};
   const int clusters = (batch + DC_BEAMS - 1) / DC_BEAMS;
-  // staged shared-key slice (K and V) + one 64-key V buffer per warp
-  const size_t smem = ((size_t)2 * chunk * (heads * DC_D + 8) + DC_WARPS * 64 * DC_D) *
-                      sizeof(__nv_bfloat16);
-  if (smem > 96 * 1024) return GRS_ERR_SHAPE;
+  // the ring plus up to 1 KB to align it to 1024 bytes
+  const size_t smem = (size_t)DC_NBUF * DC_STAGE_BYTES + 1024;
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr[dev]) {
     cudaFuncSetAttribute(decode_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         96 * 1024);
+                         (int)smem);
     attr[dev] = true;
   }
-  decode_cluster_kernel<<<clusters * DC_CLUSTER, DC_WARPS * 32, smem, (cudaStream_t)stream>>>(a);
+  decode_cluster_kernel<<<clusters * DC_CLUSTER, DC_THREADS, smem, (cudaStream_t)stream>>>(
+      a, tm_sk, tm_sv, tm_kc, tm_vc, tm_ck, tm_cv);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }

@@ -17,6 +17,29 @@ import torch
 from . import _lib
 
 
+_STATUS: dict[torch.device, torch.Tensor] = {}
+
+
+def _status_word(device: torch.device) -> torch.Tensor:
+    """Device int32 that the shared-prefix decode kernel sets to a negative
+    status when one of its bounded in-kernel waits gives up."""
+    if device not in _STATUS:
+        _STATUS[device] = torch.zeros(1, dtype=torch.int32, device=device)
+    return _STATUS[device]
+
+
+def check_decode_status(device: torch.device | str = "cuda") -> None:
+    """Raise if a shared-prefix decode launch on `device` reported an error
+    (reads the device status word: one synchronisation), then clear it."""
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device(device.type, torch.cuda.current_device())
+    word = _status_word(device)
+    code = int(word.item())
+    word.zero_()
+    _lib.check(code, "shared-prefix decode attention")
+
+
 def paged_attention(
     query: torch.Tensor,
     key_cache: torch.Tensor,
@@ -45,6 +68,17 @@ def paged_attention(
         raise ValueError("cache must be [pages, page, heads, head_width]")
     if key_cache.stride() != value_cache.stride() or key_cache.stride(3) != 1:
         raise ValueError("key/value caches must share a layout with contiguous head_width")
+    if shared_key is not None and (shared_key.dim() != 3
+                                   or shared_key.shape[1:] != (heads, head_width)
+                                   or shared_value.shape != shared_key.shape):
+        raise ValueError("shared key/value must be [num_shared, heads, head_width]")
+    if has_current and (current_key.shape != (batch, heads, head_width)
+                        or current_value.shape != current_key.shape
+                        or current_valid.shape != (batch,)):
+        raise ValueError("current key/value must be [batch, heads, head_width], valid [batch]")
+    if out is not None and (out.shape != query.shape or out.dtype != query.dtype
+                            or out.stride(3) != 1):
+        raise ValueError("out must match the query's shape and dtype with contiguous head_width")
     if query.stride(3) != 1:
         query = query.contiguous()
     block_table = block_table.to(torch.int32)
@@ -82,7 +116,7 @@ def paged_attention(
             _lib.ptr(cv), ck_sb, ck_sh,
             _lib.ptr(valid), sk.data_ptr(), sv.data_ptr(), num_shared, output.data_ptr(),
             output.stride(0), output.stride(1), batch, heads, key_cache.shape[1],
-            _lib.stream_of(query))
+            _status_word(query.device).data_ptr(), _lib.stream_of(query))
         if status == 0:
             return output
     status = _lib.lib().grs_paged_attention(

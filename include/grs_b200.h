@@ -33,7 +33,8 @@ typedef enum {
   GRS_ERR_CORRUPT = -6,      /* "free-list corruption" (paged_cache.py:90) */
   GRS_ERR_LENGTH = -7,       /* "prefix handle length/block table mismatch" (paged_cache.py:228) */
   GRS_ERR_WORKSPACE = -8,    /* caller workspace too small */
-  GRS_ERR_TOO_LARGE = -9     /* inputs exceed a fixed internal scratch capacity */
+  GRS_ERR_TOO_LARGE = -9,    /* inputs exceed a fixed internal scratch capacity */
+  GRS_ERR_TIMEOUT = -10      /* a bounded in-kernel wait ran out (device status word) */
 } grs_status;
 
 enum { GRS_DTYPE_BF16 = 0, GRS_DTYPE_F32 = 1 };
@@ -65,11 +66,15 @@ GRS_API int grs_paged_attention(int dtype, const void* query, int64_t q_sb, int6
 /* Shared-prefix decode (bf16, head width 32, one query, heads <= 8): the
  * same semantics as grs_paged_attention with query_len 1 (token order:
  * shared prefix, pages, current token), in one launch of 8-CTA clusters of
- * 16 beams; the shared keys are split across the cluster and combined
- * through distributed shared memory.  block_table rows hold max_blocks
- * entries.  Requires 16-byte aligned query, cache
- * and current tensors and strides that are multiples of 8 elements; returns
- * GRS_ERR_SHAPE otherwise (the caller then uses grs_paged_attention). */
+ * 16 beams.  Each cluster reads every distinct page of its beams once;
+ * shared and page keys are split across the cluster and the partials are
+ * combined through distributed shared memory.  block_table rows hold
+ * max_blocks (<= 32) entries.  Requires 16-byte aligned query, cache,
+ * current and shared tensors, heads adjacent in the cache and current rows
+ * (head stride 32) and strides that are multiples of 8 elements; returns
+ * GRS_ERR_SHAPE otherwise (the caller then uses grs_paged_attention).
+ * `status` (device int32, may be null) receives GRS_ERR_TIMEOUT if an
+ * in-kernel wait gives up; it is left untouched otherwise. */
 GRS_API int grs_decode_attention_shared(const void* query, int64_t q_sb, int64_t q_sh,
                                         const void* key_cache, const void* value_cache,
                                         int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
@@ -80,7 +85,7 @@ GRS_API int grs_decode_attention_shared(const void* query, int64_t q_sb, int64_t
                                         const uint8_t* current_valid, const void* shared_key,
                                         const void* shared_value, int num_shared, void* output,
                                         int64_t o_sb, int64_t o_sh, int batch, int heads,
-                                        int page_size, void* stream);
+                                        int page_size, int32_t* status, void* stream);
 
 /* ---- PagedKVCache device state: paged_cache.py:16-105 -------------------
  * refcounts int32 [capacity], free_list int32 [capacity] with its length in

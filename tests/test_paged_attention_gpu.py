@@ -122,6 +122,39 @@ def test_partial_current_triple_rejected(cuda_device):
                                                   (5, 17, True), (48, 0, False)])
 def test_cluster_decode_shared_prefix(cuda_device, batch, shared, current):
     """The 8-CTA cluster decode (shared prefix split across the cluster) vs the oracle."""
+    from graph_rewrite_system_b200.paged_attention import check_decode_status
+
     out, exp = _random_case(7 + batch, batch, 8, 32, 16, 200, 1, 64, torch.bfloat16, cuda_device,
                             shared=shared, current=current)
     np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+    check_decode_status(cuda_device)
+
+
+@pytest.mark.parametrize("batch,heads,cap,max_len,page", [(40, 6, 6, 64, 16), (33, 8, 3, 96, 32),
+                                                          (24, 5, 9, 61, 16), (70, 8, 400, 64, 16),
+                                                          (33, 8, 3, 50, 8), (16, 4, 12, 17, 4)])
+def test_cluster_decode_shared_pages(cuda_device, batch, heads, cap, max_len, page):
+    """Heavily shared pages (small arenas) exercise the per-column page dedup
+    of the cluster decode; ragged lengths, odd head counts, pages of 32 rows
+    and partial clusters included (page sizes 8 and 4 take the rows kernel)."""
+    from graph_rewrite_system_b200.paged_attention import check_decode_status
+
+    out, exp = _random_case(100 + batch, batch, heads, 32, page, cap, 1, max_len, torch.bfloat16,
+                            cuda_device, shared=50, current=True)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+    check_decode_status(cuda_device)
+
+
+def test_cluster_decode_prefix_tree(cuda_device):
+    """The decode microbenchmark's own prefix-tree tables at a small size."""
+    from graph_rewrite_system_b200.paged_attention import paged_attention
+    from graph_rewrite_system_b200.workloads import decode_attention_workload
+
+    w = decode_attention_workload(cuda_device, beams=48, num_shared=381, seed=5)
+    got = paged_attention(w.query, w.key_cache, w.value_cache, w.block_table, w.lengths,
+                          shared_key=w.shared_key, shared_value=w.shared_value)
+    f = lambda t: t.float().cpu()
+    exp = oracle.paged_attention(f(w.query), f(w.key_cache), f(w.value_cache),
+                                 w.block_table.cpu(), w.lengths.cpu(), shared_key=f(w.shared_key),
+                                 shared_value=f(w.shared_value))
+    np.testing.assert_allclose(got.float().cpu().numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
