@@ -39,12 +39,18 @@ import sys
 import tempfile
 import time
 
-import torch
+# grow the caching allocator's segments in place: the beam state tensors grow
+# with the slot count level by level, and fresh cudaMalloc calls for them
+# stall whole levels
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
+import torch  # noqa: E402
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "beam-state decode steps/s at B=1000,T=64; paged-attn HBM GB/s vs peak"
+PROBE_LEAD_CYCLES = 40_000             # ~20 us at 1.965 GHz
 DECODE_INPUT_COPIES = 16              # 16 x ~11.2 MB = 180 MB > 126 MB L2
 
 
@@ -64,6 +70,74 @@ def measured_peaks() -> dict:
                 "bf16_tflops_sustained": data.get("bf16_tflops_sustained"), "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
             "source": "fallback"}
+
+
+class KernelProbe:
+    """Times every call of one kernel wrapper of graph_rewrite_system_b200.kernels
+    with CUDA events on the launching stream while active, and adds up the
+    wrapper's algorithmic bytes."""
+
+    def __init__(self, name: str, bytes_fn):
+        self.name, self.bytes_fn = name, bytes_fn
+        self.events, self.bytes, self.rows = [], 0, 0
+
+    def __enter__(self):
+        from graph_rewrite_system_b200 import kernels
+
+        self.module, self.original = kernels, getattr(kernels, self.name)
+
+        def timed(*a, **kw):
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            # keep the device busy while the host issues the launch, so the
+            # events bracket the kernel and not the host call (~20 us)
+            torch.cuda._sleep(PROBE_LEAD_CYCLES)
+            start.record()
+            out = self.original(*a, **kw)
+            end.record()
+            self.events.append((start, end))
+            nbytes, rows = self.bytes_fn(*a, **kw)
+            self.bytes += nbytes
+            self.rows += rows
+            return out
+
+        setattr(kernels, self.name, timed)
+        return self
+
+    def __exit__(self, *exc):
+        setattr(self.module, self.name, self.original)
+
+    def roofline(self, peaks: dict, kernel: str, traffic_ratio) -> dict | None:
+        """`traffic_ratio`: DRAM bytes / algorithmic bytes of this kernel from
+        a committed ncu capture (None when absent)."""
+        if not self.events:
+            return None
+        torch.cuda.synchronize()
+        n = len(self.events)
+        ms = sum(s.elapsed_time(e) for s, e in self.events) / n
+        per_launch = self.bytes / n
+        achieved = per_launch / (ms * 1e-3) / 1e9
+        traffic = traffic_ratio * per_launch if traffic_ratio else None
+        return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                "kernel": kernel, "launches": n, "avg_launch_ms": ms,
+                "algorithmic_bytes_per_launch": per_launch,
+                "peak_source": f"{peaks['source']} hbm_gbs"}
+
+
+def bias_gelu_bytes(y, bias, gelu=True):
+    """In-place bias + GELU over y [rows, cols]: read and write y, read the bias."""
+    nbytes = 2 * y.numel() * y.element_size()
+    if bias is not None:
+        nbytes += bias.numel() * bias.element_size()
+    return nbytes, y.shape[0]
+
+
+def launch_count() -> int:
+    """Kernels launched so far by libgrs_b200.so (its own launch counter)."""
+    from graph_rewrite_system_b200 import _lib
+
+    return int(_lib.lib().grs_launch_count())
 
 
 def profiled_traffic(kernel: str) -> float | None:
@@ -193,10 +267,12 @@ def run_decode_attention(args, world, rank, device):
         # hold the device while the host enqueues the timed launches, so the
         # events bracket device time and not the Python call overhead
         torch.cuda._sleep(queue_ahead_cycles(args.steps))
+        launches0 = launch_count()
         start.record(stream)
         for i in range(args.steps):
             step(i)
         end.record(stream)
+        launches = launch_count() - launches0
         torch.cuda.synchronize(device)
     barrier(world, device)
     kernel_ms = start.elapsed_time(end) / args.steps
@@ -268,7 +344,7 @@ def run_decode_attention(args, world, rank, device):
                    "parallelism": f"replicas x{world}"},
         "e2e": {"value": world * 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
+        "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "traffic": profiled_traffic("decode_attention"),
@@ -343,7 +419,7 @@ def run_rollout(args, world, rank, device):
     from graph_rewrite_system_b200.rollout import StageTimer
 
     depth = args.warmup + args.steps
-    search, rc = build_rollout(device, depth=depth, seed=0)
+    search, rc = build_rollout(device, beam_size=args.beam, depth=depth, seed=0)
     stream = torch.cuda.current_stream(device)
     # one full untimed search first (module load, allocator warm-up)
     search.run(min(depth, args.warmup + 2))
@@ -358,7 +434,9 @@ def run_rollout(args, world, rank, device):
     barrier(world, device)
     torch.cuda.synchronize(device)
     done = 0
-    with ClockSampler(device.index) as clocks:
+    launches0 = launch_count()
+    probe = KernelProbe("bias_gelu", bias_gelu_bytes)
+    with ClockSampler(device.index) as clocks, probe:
         for i in range(args.steps):
             starts[i].record(stream)
             row = search.step()
@@ -367,6 +445,7 @@ def run_rollout(args, world, rank, device):
             if row is None:
                 break
         torch.cuda.synchronize(device)
+    launches = launch_count() - launches0
     timer.collect()
     search.timer = None
     barrier(world, device)
@@ -395,8 +474,8 @@ def run_rollout(args, world, rank, device):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "full rollout step: synthetic 6-qubit 259-gate circuit, "
                                "d_model 256, 8 heads, 4 causal + 4 message-passing layers, "
-                               "random init, beam 1000, depth 64, page 16, 80 candidates -> "
-                               "16 per parent -> 16000 proposals",
+                               "random init, beam 1000, depth 64, page 16, up to 2048 "
+                               "candidates per state -> 16 per parent -> 16000 proposals",
                    "beam": rc.beam_size, "depth": depth, "timed_levels": f"{args.warmup + 1}"
                    f"..{args.warmup + done}", "page_size": rc.page_size,
                    "l2": "inputs larger than L2 (beam state ~0.2 GB bf16 per activation)",
@@ -404,6 +483,9 @@ def run_rollout(args, world, rank, device):
         "e2e": {"value": world * depth * 1e3 / e2e_ms, "unit": "steps/s",
                 "h2d_bytes_per_step": h2d // depth, "d2h_bytes_per_step": d2h,
                 "scope": "DeviceBeamSearch.run(): s0 upload, all levels, beam summary download"},
+        "gpu_launches": launches,
+        "roofline": probe.roofline(measured_peaks(), "bias_gelu_kernel",
+                                   profiled_traffic("bias_gelu_traffic_ratio")),
         "search": {"last_level": {k: getattr(last, k) for k in (
                        "input_states", "output_states", "best_speculative_gate_count",
                        "predicted_actions", "eligible_actions_before_parent_cap",
@@ -510,6 +592,10 @@ def main() -> None:
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--workload", choices=("rollout", "decode-attention"), default="rollout")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--beam", type=int, default=1000,
+                        help="rollout beam size (1000 is the benchmark configuration)")
+    parser.add_argument("--no-attention", action="store_true",
+                        help="rollout only: skip the paged-attention sub-benchmark")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -525,10 +611,11 @@ def main() -> None:
     torch.cuda.set_device(device)
     if args.workload == "rollout":
         line = run_rollout(args, world, rank, device)
-        attn_args = argparse.Namespace(steps=20, warmup=5, no_cpu_baseline=True)
-        attention = run_decode_attention(attn_args, world, rank, device)
-        line["paged_attention"] = {k: attention[k] for k in ("value", "unit", "ms_per_step",
-                                                             "roofline", "config")}
+        if not args.no_attention:
+            attn_args = argparse.Namespace(steps=20, warmup=5, no_cpu_baseline=True)
+            attention = run_decode_attention(attn_args, world, rank, device)
+            line["paged_attention"] = {k: attention[k] for k in (
+                "value", "unit", "ms_per_step", "roofline", "config")}
     else:
         line = run_decode_attention(args, world, rank, device)
     if rank == 0:

@@ -240,7 +240,7 @@ extern "C" int grs_select_candidates(const float* logits, const uint8_t* eligibl
   SelectArgs a{logits, eligible, distance, slots, num_sources, k, near_scale, near_bias,
                near_thr, far_scale, far_bias, far_thr, out_batch, out_source, out_anchor,
                out_prob, out_score};
-  select_candidates_kernel<<<batch, SEL_THREADS, 0, (cudaStream_t)stream>>>(a);
+  select_candidates_kernel<<<batch, SEL_THREADS, 0, grs::counted((cudaStream_t)stream)>>>(a);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
@@ -259,7 +259,7 @@ extern "C" int grs_structural_decode(
                source_lengths, child, parent, parent_port, child_port, direction, pattern_edges,
                max_edges, max_pattern, batch_ids, sources, anchors, count, bindings, valid,
                clear_invalid};
-  structural_decode_kernel<<<ceil_div(count, 128), 128, 0, (cudaStream_t)stream>>>(a);
+  structural_decode_kernel<<<ceil_div(count, 128), 128, 0, grs::counted((cudaStream_t)stream)>>>(a);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }

@@ -1,6 +1,6 @@
 // Shared-prefix paged decode attention in one launch of 8-CTA clusters
-// (bf16, head width 32, one query per beam and head, page size a multiple
-// of 16).
+// (bf16, head width 32, one query per beam and head, an even number of
+// heads <= 8, page size a multiple of 16).
 //
 // Every beam attends to the same `num_shared` s0 node keys/values, to its own
 // block-table pages and to an optional current token.  A cluster owns 16
@@ -16,9 +16,12 @@
 //
 // Each CTA of the cluster takes every eighth shared unit and every eighth
 // page/current unit.  Warp 8 of the CTA is the producer: per unit it issues
-// TMA tile loads (cp.async.bulk.tensor, 16 rows x 128 bytes, 128-byte
-// swizzle, no multicast) of the K and V rows of all heads into a ring of
-// five stages, completion counted on the stage's "full" mbarrier.  The shared
+// two TMA tile loads (cp.async.bulk.tensor, no multicast), one for the K and
+// one for the V rows of all heads, into a ring of five stages, completion
+// counted on the stage's "full" mbarrier.  The tensor maps view a key row
+// (H*32 bf16) as H/2 chunks of 128 bytes and make the chunk the outermost
+// box dimension, so one 8 KB load lands as H/2 tiles of 16 rows x 128 bytes
+// with the 128-byte swizzle (conflict-free ldmatrix).  The shared
 // units go out at kernel entry, before the block tables are read.  Warps 0-7
 // are the consumers, one per head: each waits for a stage, computes the
 // masked online-softmax partial (max, sum, P.V) of its head for all 16 beams
@@ -52,7 +55,7 @@ constexpr int DC_THREADS = (DC_CONSUMERS + 1) * 32;
 constexpr int DC_D = 32;
 constexpr int DC_UNIT = 16;           // rows per unit / stage (one mma tile of keys)
 constexpr int DC_NBUF = 5;            // stages in the ring
-constexpr int DC_BOX_BYTES = DC_UNIT * 128;              // one TMA tile: 16 rows x 128 B
+constexpr int DC_BOX_BYTES = DC_UNIT * 128;              // one tile: 16 rows x 128 B
 constexpr int DC_STAGE_BYTES = 2 * 4 * DC_BOX_BYTES;     // K and V, up to 4 tiles each
 constexpr int DC_MAX_COLS = 32;       // block-table columns
 constexpr int DC_MAX_UNITS = 64;      // page/current units per CTA
@@ -103,21 +106,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
-// TMA tile loads into this CTA's shared memory (no multicast)
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+// TMA tile loads into this CTA's shared memory (no multicast); the
+// innermost coordinate is always 0 (a whole 128-byte chunk)
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int y, int z,
                                             uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
-                                            int z, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int y, int z,
+                                            int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z), "r"(w),
+      "r"(smem_addr(bar))
       : "memory");
 }
 
@@ -139,6 +144,14 @@ __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 2^x with the hardware approximation (ex2.approx.ftz: relative error about
+// 2^-22, subnormal results flushed to zero); 2^-inf = 0
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
@@ -224,17 +237,15 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
         mbar_arrive_expect_tx(&full_bar[buf], stage_bytes);
         unsigned char* kdst = dyn + (ring - smem_addr(dyn)) + buf * DC_STAGE_BYTES;
         unsigned char* vdst = kdst + 4 * DC_BOX_BYTES;
-        for (int t = 0; t < tiles; ++t) {
-          if (unit_page == -2) {            // shared unit: rows y0..y0+15 of [N, H*32]
-            tma_load_2d(kdst + t * DC_BOX_BYTES, &tm_sk, t * 64, y0, &full_bar[buf]);
-            tma_load_2d(vdst + t * DC_BOX_BYTES, &tm_sv, t * 64, y0, &full_bar[buf]);
-          } else if (unit_page >= 0) {      // page unit: rows y0.. of [pages, page, H*32]
-            tma_load_3d(kdst + t * DC_BOX_BYTES, &tm_kc, t * 64, y0, unit_page, &full_bar[buf]);
-            tma_load_3d(vdst + t * DC_BOX_BYTES, &tm_vc, t * 64, y0, unit_page, &full_bar[buf]);
-          } else {                          // current unit: the beams' rows of [B, H*32]
-            tma_load_2d(kdst + t * DC_BOX_BYTES, &tm_ck, t * 64, beam0, &full_bar[buf]);
-            tma_load_2d(vdst + t * DC_BOX_BYTES, &tm_cv, t * 64, beam0, &full_bar[buf]);
-          }
+        if (unit_page == -2) {              // shared unit: rows y0..y0+15 of [N, chunks, 64]
+          tma_load_3d(kdst, &tm_sk, y0, 0, &full_bar[buf]);
+          tma_load_3d(vdst, &tm_sv, y0, 0, &full_bar[buf]);
+        } else if (unit_page >= 0) {        // page unit: rows y0.. of [pages, page, chunks, 64]
+          tma_load_4d(kdst, &tm_kc, y0, 0, unit_page, &full_bar[buf]);
+          tma_load_4d(vdst, &tm_vc, y0, 0, unit_page, &full_bar[buf]);
+        } else {                            // current unit: the beams' rows of [B, chunks, 64]
+          tma_load_3d(kdst, &tm_ck, beam0, 0, &full_bar[buf]);
+          tma_load_3d(vdst, &tm_cv, beam0, 0, &full_bar[buf]);
         }
       }
       __syncwarp();
@@ -394,16 +405,18 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        // running maxima; a row that has seen no key yet keeps -inf and is
+        // exponentiated against 0 instead, so every term is 2^-inf = 0
         const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-        const float c0 = m0 == -INFINITY ? 0.f : exp2f(m0 - n0);
-        const float c1 = m1 == -INFINITY ? 0.f : exp2f(m1 - n1);
+        const float e0 = n0 == -INFINITY ? 0.f : n0, e1 = n1 == -INFINITY ? 0.f : n1;
+        const float c0 = fast_exp2(m0 - e0), c1 = fast_exp2(m1 - e1);
         float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            s[nt][c] = s[nt][c] == -INFINITY ? 0.f : exp2f(s[nt][c] - n0);
-            s[nt][2 + c] = s[nt][2 + c] == -INFINITY ? 0.f : exp2f(s[nt][2 + c] - n1);
+            s[nt][c] = fast_exp2(s[nt][c] - e0);
+            s[nt][2 + c] = fast_exp2(s[nt][2 + c] - e1);
             sum0 += s[nt][c];
             sum1 += s[nt][2 + c];
           }
@@ -481,7 +494,7 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
     float L = 0.f, O0 = 0.f, O1 = 0.f;
 #pragma unroll
     for (int r = 0; r < DC_CLUSTER; ++r) {
-      const float w = mr[r] == -INFINITY ? 0.f : exp2f(mr[r] - M);
+      const float w = fast_exp2(mr[r] - (M == -INFINITY ? 0.f : M));
       L += lr[r] * w;
       O0 += ar[r] * w;
       O1 += br[r] * w;
@@ -498,7 +511,7 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no
 // libcuda link), with a small cache keyed by every encoded field.
 struct MapKey {
-  const void* base; int rank; uint64_t dims[3]; uint64_t strides[2];
+  const void* base; int rank; uint64_t dims[4]; uint64_t strides[3];
   bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
 };
 
@@ -516,7 +529,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// bf16 tensor of `rank` (2 or 3) dims, innermost first; tiles of 64 x 16 (x 1)
+// bf16 tensor of `rank` (3 or 4) dims, innermost first: 64-element chunk,
+// row, chunk index, [page]; boxes of one chunk x 16 rows x all chunks (x 1)
 static bool tile_map(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes) {
   constexpr int kCache = 32;
@@ -538,8 +552,8 @@ static bool tile_map(CUtensorMap* out, const void* base, int rank, const uint64_
     }
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t gdim[3], gstr[2];
-  cuuint32_t box[3] = {64, DC_UNIT, 1}, estr[3] = {1, 1, 1};
+  cuuint64_t gdim[4], gstr[3];
+  cuuint32_t box[4] = {64, DC_UNIT, (cuuint32_t)dims[2], 1}, estr[4] = {1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) gdim[i] = dims[i];
   for (int i = 0; i < rank - 1; ++i) gstr[i] = strides_bytes[i];
   CUtensorMap m;
@@ -568,7 +582,7 @@ extern "C" int grs_decode_attention_shared(
     const void* shared_value, int num_shared, void* output, int64_t o_sb, int64_t o_sh,
     int batch, int heads, int page_size, int32_t* status, void* stream) {
   if (batch <= 0) return GRS_OK;
-  if (heads <= 0 || heads > DC_CONSUMERS || page_size <= 0 || page_size % DC_UNIT ||
+  if (heads <= 0 || heads > DC_CONSUMERS || heads % 2 || page_size <= 0 || page_size % DC_UNIT ||
       num_shared < 0 || num_pages <= 0 || max_blocks <= 0 || max_blocks > DC_MAX_COLS)
     return GRS_ERR_SHAPE;
   // page/current units of one CTA: at most 16 distinct pages per column
@@ -588,25 +602,26 @@ extern "C" int grs_decode_attention_shared(
     return GRS_ERR_SHAPE;
   if (((uintptr_t)output & 3) || (o_sb | o_sh) % 2) return GRS_ERR_SHAPE;
 
-  const uint64_t row = (uint64_t)heads * DC_D;           // elements per key row
+  // a key row of H*32 elements as H/2 chunks of 64 (128 bytes)
+  const uint64_t chunks = (uint64_t)heads / 2;
   CUtensorMap tm_kc, tm_vc, tm_sk, tm_sv, tm_ck, tm_cv;
   {
-    const uint64_t dims[3] = {row, (uint64_t)page_size, (uint64_t)num_pages};
-    const uint64_t str[2] = {(uint64_t)kc_st * 2, (uint64_t)kc_sp * 2};
-    if (!tile_map(&tm_kc, key_cache, 3, dims, str) || !tile_map(&tm_vc, value_cache, 3, dims, str))
+    const uint64_t dims[4] = {64, (uint64_t)page_size, chunks, (uint64_t)num_pages};
+    const uint64_t str[3] = {(uint64_t)kc_st * 2, 128, (uint64_t)kc_sp * 2};
+    if (!tile_map(&tm_kc, key_cache, 4, dims, str) || !tile_map(&tm_vc, value_cache, 4, dims, str))
       return GRS_ERR_SHAPE;
   }
   tm_sk = tm_sv = tm_ck = tm_cv = tm_kc;                 // placeholders for absent inputs
   if (num_shared > 0) {
-    const uint64_t dims[2] = {row, (uint64_t)num_shared};
-    const uint64_t str[1] = {row * 2};
-    if (!tile_map(&tm_sk, shared_key, 2, dims, str) || !tile_map(&tm_sv, shared_value, 2, dims, str))
+    const uint64_t dims[3] = {64, (uint64_t)num_shared, chunks};
+    const uint64_t str[2] = {(uint64_t)heads * DC_D * 2, 128};
+    if (!tile_map(&tm_sk, shared_key, 3, dims, str) || !tile_map(&tm_sv, shared_value, 3, dims, str))
       return GRS_ERR_SHAPE;
   }
   if (current_key) {
-    const uint64_t dims[2] = {row, (uint64_t)batch};
-    const uint64_t str[1] = {(uint64_t)ck_sb * 2};
-    if (!tile_map(&tm_ck, current_key, 2, dims, str) || !tile_map(&tm_cv, current_value, 2, dims, str))
+    const uint64_t dims[3] = {64, (uint64_t)batch, chunks};
+    const uint64_t str[2] = {(uint64_t)ck_sb * 2, 128};
+    if (!tile_map(&tm_ck, current_key, 3, dims, str) || !tile_map(&tm_cv, current_value, 3, dims, str))
       return GRS_ERR_SHAPE;
   }
   DecodeArgs a{(const __nv_bfloat16*)query, q_sb, q_sh, block_table, bt_stride, max_blocks,
@@ -624,7 +639,7 @@ extern "C" int grs_decode_attention_shared(
                          (int)smem);
     attr[dev] = true;
   }
-  decode_cluster_kernel<<<clusters * DC_CLUSTER, DC_THREADS, smem, (cudaStream_t)stream>>>(
+  decode_cluster_kernel<<<clusters * DC_CLUSTER, DC_THREADS, smem, grs::counted((cudaStream_t)stream)>>>(
       a, tm_sk, tm_sv, tm_kc, tm_vc, tm_ck, tm_cv);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;

@@ -15,6 +15,14 @@
 
 namespace grs {
 
+// Every kernel launch of the library passes its stream through counted(),
+// which bumps the process-wide launch counter read by grs_launch_count().
+void note_launch();
+inline cudaStream_t counted(cudaStream_t stream) {
+  note_launch();
+  return stream;
+}
+
 // Element loads/stores for the two arena dtypes: bf16 (device arenas) and
 // fp32 (the CPU-equivalence configuration run on the GPU).
 __device__ __forceinline__ float to_float(float v) { return v; }

@@ -96,17 +96,61 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) add_ln_kernel(AddLnArgs a) {
   }
 }
 
-// In place: y[r, c] = GELU(y[r, c] + bias[c]) (bias optional).
+// Eight consecutive elements as fp32, loaded/stored with 16-byte (bf16) or
+// 2 x 16-byte (fp32) accesses; the pointer must be aligned to that width.
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float v[8]) {
+  const uint4 x = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float v[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float v[8]) {
+  uint4 x;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&x);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+  *reinterpret_cast<uint4*>(p) = x;
+}
+__device__ __forceinline__ void store8(float* p, const float v[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// In place: y[r, c] = GELU(y[r, c] + bias[c]) (bias optional).  Each thread
+// handles groups of 8 consecutive columns (cols % 8 == 0, 16-byte aligned
+// rows), grid-strided.
 template <typename T>
 __global__ void bias_gelu_kernel(T* y, int64_t rows, int cols, int64_t stride,
                                  const float* bias, int apply_gelu) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= rows * cols) return;
-  const int64_t r = idx / cols;
-  const int c = (int)(idx % cols);
-  T* p = y + r * stride + c;
-  float v = to_float(*p) + (bias ? bias[c] : 0.f);
-  *p = from_float<T>(apply_gelu ? gelu_exact(v) : v);
+  const int groups = cols >> 3;
+  const int64_t n = rows * groups;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = g / groups;
+    const int c = (int)(g - r * groups) << 3;
+    T* p = y + r * stride + c;
+    float v[8];
+    load8(p, v);
+    if (bias) {
+      float b[8];
+      load8(bias + c, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += b[j];
+    }
+    if (apply_gelu) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = gelu_exact(v[j]);
+    }
+    store8(p, v);
+  }
 }
 
 // states[b, s] = (gate_embedding[max(type, 0)] + marker) * (type >= 0)
@@ -438,7 +482,7 @@ extern "C" int grs_add_layernorm(int dtype, const void* x, int64_t x_stride, con
               rows_per_beam, width, eps, zero_before};
   const int grid = ceil_div(rows, ROW_WARPS);
   GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
-      add_ln_kernel<T, V><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(a)))
+      add_ln_kernel<T, V><<<grid, ROW_WARPS * 32, 0, grs::counted((cudaStream_t)stream)>>>(a)))
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
@@ -446,8 +490,11 @@ extern "C" int grs_add_layernorm(int dtype, const void* x, int64_t x_stride, con
 extern "C" int grs_bias_gelu(int dtype, void* y, int64_t rows, int cols, int64_t stride,
                              const float* bias, int apply_gelu, void* stream) {
   if (rows <= 0) return GRS_OK;
-  const int64_t n = rows * cols;
-  GRS_DTYPE_SWITCH(T, dtype, bias_gelu_kernel<T><<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+  // 8-column groups with 16-byte (bf16) / 32-byte (fp32) aligned accesses
+  if (cols % 8 || stride % 8 || ((uintptr_t)y & 15) || ((uintptr_t)bias & 15)) return GRS_ERR_SHAPE;
+  const int64_t groups = rows * (cols / 8);
+  const int grid = (int)(groups < 148 * 16 * 256 ? ceil_div(groups, 256) : 148 * 16);
+  GRS_DTYPE_SWITCH(T, dtype, bias_gelu_kernel<T><<<grid, 256, 0, grs::counted((cudaStream_t)stream)>>>(
       (T*)y, rows, cols, stride, bias, apply_gelu))
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
@@ -458,7 +505,7 @@ extern "C" int grs_embed_initial(int dtype, const int64_t* types, int64_t rows, 
                                  int64_t stride, uint8_t* live, void* stream) {
   if (rows <= 0) return GRS_OK;
   GRS_DTYPE_SWITCH(T, dtype, embed_initial_kernel<T><<<ceil_div(rows, ROW_WARPS), ROW_WARPS * 32, 0,
-                                                       (cudaStream_t)stream>>>(
+                                                       grs::counted((cudaStream_t)stream)>>>(
       types, rows, width, gate_emb, marker, (T*)states, stride, live))
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
@@ -473,7 +520,7 @@ extern "C" int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride,
   if (slots <= 0 || port_slots < slots) return GRS_ERR_SHAPE;
   const int grid = ceil_div(rows, ROW_WARPS);
   GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
-      graph_aggregate_kernel<T, V><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(
+      graph_aggregate_kernel<T, V><<<grid, ROW_WARPS * 32, 0, grs::counted((cudaStream_t)stream)>>>(
           (const T*)fb, fb_stride, rel, in_node, in_port, out_node, out_port, rows, slots,
           port_slots, width, (T*)agg, agg_stride)))
   GRS_CUDA_CHECK_LAUNCH();
@@ -488,7 +535,7 @@ extern "C" int grs_action_inputs(int dtype, const void* states, int64_t state_st
                                  void* stream) {
   if (batch <= 0) return GRS_OK;
   if (pattern > 32) return GRS_ERR_SHAPE;
-  GRS_DTYPE_SWITCH(T, dtype, action_inputs_kernel<T><<<batch, 128, 0, (cudaStream_t)stream>>>(
+  GRS_DTYPE_SWITCH(T, dtype, action_inputs_kernel<T><<<batch, 128, 0, grs::counted((cudaStream_t)stream)>>>(
       (const T*)states, state_stride, slots, xfer_ids, source_ids, source_slots, pattern, width,
       xfer_emb, source_reps, (T*)bound, (T*)ctx_in, source_mask, active, batch))
   GRS_CUDA_CHECK_LAUNCH();
@@ -500,7 +547,7 @@ extern "C" int grs_position_token(int dtype, const void* raw, const float* posit
                                   int batch, int width, void* stream) {
   if (batch <= 0) return GRS_OK;
   const int64_t n = (int64_t)batch * width;
-  GRS_DTYPE_SWITCH(T, dtype, position_token_kernel<T><<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+  GRS_DTYPE_SWITCH(T, dtype, position_token_kernel<T><<<ceil_div(n, 256), 256, 0, grs::counted((cudaStream_t)stream)>>>(
       (const T*)raw, position, lengths, active, (T*)token, batch, width))
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
@@ -518,8 +565,8 @@ extern "C" int grs_update_live_hidden(int dtype, const void* qxa, int64_t qxa_st
   if (vq < 0 || vh < 0) return GRS_ERR_SHAPE;
 #define GRS_ULH(VQ, VH)                                                                        \
   if (vq == VQ && vh == VH) {                                                                  \
-    GRS_DTYPE_SWITCH(T, dtype, update_live_hidden_kernel<T, VQ, VH><<<grid, ROW_WARPS * 32, 0, \
-                                                                     (cudaStream_t)stream>>>(  \
+    GRS_DTYPE_SWITCH(T, dtype, update_live_hidden_kernel<T, VQ, VH><<<grid, ROW_WARPS * 32, 0, grs::counted(\
+                                                                     (cudaStream_t)stream)>>>(  \
         (const T*)qxa, qxa_stride, (const T*)keys, (const T*)vw, (const T*)cvec, source_mask,  \
         pattern, rows, slots, width, (T*)hidden, hidden_stride, affinity))                      \
     GRS_CUDA_CHECK_LAUNCH();                                                                   \
@@ -538,7 +585,7 @@ extern "C" int grs_destination_hidden(int dtype, const void* r, const float* typ
                                       void* stream) {
   const int64_t n = (int64_t)batch * pattern * hidden_width;
   if (n <= 0) return GRS_OK;
-  GRS_DTYPE_SWITCH(T, dtype, destination_hidden_kernel<T><<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+  GRS_DTYPE_SWITCH(T, dtype, destination_hidden_kernel<T><<<ceil_div(n, 256), 256, 0, grs::counted((cudaStream_t)stream)>>>(
       (const T*)r, type_table, pos_table, dest_slots, dest_types, active, pattern, batch,
       hidden_width, (T*)hidden))
   GRS_CUDA_CHECK_LAUNCH();
@@ -551,7 +598,7 @@ extern "C" int grs_apply_slots(int dtype, void* states, int64_t state_stride, ui
                                const int64_t* dest_types, const uint8_t* active, int dpattern,
                                const void* created, int width, int batch, void* stream) {
   if (batch <= 0) return GRS_OK;
-  GRS_DTYPE_SWITCH(T, dtype, apply_slots_kernel<T><<<batch, 128, 0, (cudaStream_t)stream>>>(
+  GRS_DTYPE_SWITCH(T, dtype, apply_slots_kernel<T><<<batch, 128, 0, grs::counted((cudaStream_t)stream)>>>(
       (T*)states, state_stride, live, types, slots, source_slots, source_mask, spattern,
       dest_slots, dest_types, active, dpattern, (const T*)created, width, batch))
   GRS_CUDA_CHECK_LAUNCH();
@@ -565,7 +612,7 @@ extern "C" int grs_match_logits(int dtype, const void* acc, int64_t acc_stride,
                                 uint8_t* eligible, void* stream) {
   const int64_t n = rows * num_sources;
   if (n <= 0) return GRS_OK;
-  GRS_DTYPE_SWITCH(T, dtype, match_logits_kernel<T><<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+  GRS_DTYPE_SWITCH(T, dtype, match_logits_kernel<T><<<ceil_div(n, 256), 256, 0, grs::counted((cudaStream_t)stream)>>>(
       (const T*)acc, acc_stride, source_bias, first_types, live, types, rows, num_sources,
       inv_sqrt_r, logits, eligible))
   GRS_CUDA_CHECK_LAUNCH();
@@ -577,7 +624,7 @@ extern "C" int grs_gather_beams(const void* in, void* out, const int64_t* index,
                                 void* stream) {
   if (rows <= 0) return GRS_OK;
   if (in_bytes < 0 || out_bytes < 0) return GRS_ERR_SHAPE;
-  gather_beams_kernel<<<(unsigned)rows, 256, 0, (cudaStream_t)stream>>>(
+  gather_beams_kernel<<<(unsigned)rows, 256, 0, grs::counted((cudaStream_t)stream)>>>(
       (const char*)in, (char*)out, index, rows, in_bytes, out_bytes, fill_byte);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
@@ -588,7 +635,7 @@ extern "C" int grs_edges_to_ports(const int64_t* eb, const int64_t* es, const in
                                   int32_t* out_port, int32_t* in_node, int32_t* in_port,
                                   void* stream) {
   if (edges <= 0) return GRS_OK;
-  edges_to_ports_kernel<<<ceil_div(edges, 256), 256, 0, (cudaStream_t)stream>>>(
+  edges_to_ports_kernel<<<ceil_div(edges, 256), 256, 0, grs::counted((cudaStream_t)stream)>>>(
       eb, es, ed, er, edges, slots, out_node, out_port, in_node, in_port);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;

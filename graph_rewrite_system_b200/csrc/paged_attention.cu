@@ -347,7 +347,7 @@ int launch_rows(const RowsArgs<T, D>& a, cudaStream_t stream) {
   const long long rows = (long long)a.B * a.H * a.Q;
   if (rows == 0) return GRS_OK;
   const int warps = 8;
-  paged_attention_rows_kernel<T, D><<<ceil_div(rows, warps), warps * 32, 0, stream>>>(a);
+  paged_attention_rows_kernel<T, D><<<ceil_div(rows, warps), warps * 32, 0, grs::counted(stream)>>>(a);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
@@ -423,9 +423,9 @@ extern "C" int grs_paged_attention(
       attr_set[dev] = true;
     }
     if ((int64_t)max_blocks * page_size <= RO_TILE)
-      readout_single_tile_kernel<<<batch, RO_WARPS * 32, smem, stream>>>(a);
+      readout_single_tile_kernel<<<batch, RO_WARPS * 32, smem, grs::counted(stream)>>>(a);
     else
-      readout_multi_tile_kernel<4><<<batch, RO_WARPS * 32, smem, stream>>>(a);
+      readout_multi_tile_kernel<4><<<batch, RO_WARPS * 32, smem, grs::counted(stream)>>>(a);
     GRS_CUDA_CHECK_LAUNCH();
     return GRS_OK;
   }

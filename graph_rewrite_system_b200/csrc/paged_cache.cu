@@ -259,7 +259,7 @@ using namespace grs;
 extern "C" int grs_cache_init(int32_t* refcounts, int32_t* free_list, int32_t* free_count,
                               int32_t* last_pos, int capacity, void* stream) {
   if (capacity <= 0) return GRS_ERR_SHAPE;
-  cache_init_kernel<<<ceil_div(capacity, 256), 256, 0, (cudaStream_t)stream>>>(
+  cache_init_kernel<<<ceil_div(capacity, 256), 256, 0, grs::counted((cudaStream_t)stream)>>>(
       refcounts, free_list, free_count, last_pos, capacity);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
@@ -281,14 +281,14 @@ extern "C" int grs_cache_append(int elem_bytes, int32_t* refcounts, int32_t* fre
     return GRS_ERR_SHAPE;
   if ((new_readout_keys == nullptr) != (new_readout_values == nullptr)) return GRS_ERR_SHAPE;
   if (n == 0) return GRS_OK;
-  cache_fork_kernel<<<ceil_div(n, 128), 128, 0, s>>>(refcounts, free_list, free_count, capacity,
+  cache_fork_kernel<<<ceil_div(n, 128), 128, 0, grs::counted(s)>>>(refcounts, free_list, free_count, capacity,
                                                       parent_table, parent_stride, parent_lengths,
                                                       n, page_size, child_table, child_stride,
                                                       child_lengths, child_cols, status);
   GRS_CUDA_CHECK_LAUNCH();
   CacheArenas ar{keys, values, actions, readout_keys, readout_values, layers, capacity,
                  page_size, heads_x_width, model_width, elem_bytes};
-  cache_write_kernel<<<n, 128, 0, s>>>(ar, parent_table, parent_stride, parent_lengths,
+  cache_write_kernel<<<n, 128, 0, grs::counted(s)>>>(ar, parent_table, parent_stride, parent_lengths,
                                        child_table, child_stride, n, (const char*)new_keys,
                                        (const char*)new_values, (const char*)new_actions,
                                        (const char*)new_readout_keys,
@@ -305,10 +305,10 @@ extern "C" int grs_cache_release(int32_t* refcounts, int32_t* free_list, int32_t
   if (n < 0 || cols <= 0 || page_size <= 0) return GRS_ERR_SHAPE;
   if (n == 0) return GRS_OK;
   const long long total = (long long)n * cols;
-  cache_release_decrement_kernel<<<ceil_div(total, 256), 256, 0, s>>>(
+  cache_release_decrement_kernel<<<ceil_div(total, 256), 256, 0, grs::counted(s)>>>(
       refcounts, last_pos, capacity, table, stride, lengths, n, cols, page_size, status);
   GRS_CUDA_CHECK_LAUNCH();
-  cache_release_collect_kernel<<<1, REL_THREADS, 0, s>>>(refcounts, last_pos, free_list,
+  cache_release_collect_kernel<<<1, REL_THREADS, 0, grs::counted(s)>>>(refcounts, last_pos, free_list,
                                                          free_count, capacity, table, stride,
                                                          lengths, n, cols, page_size);
   GRS_CUDA_CHECK_LAUNCH();
@@ -318,7 +318,7 @@ extern "C" int grs_cache_release(int32_t* refcounts, int32_t* free_list, int32_t
 extern "C" int grs_cache_check_lengths(const int32_t* nblocks, const int32_t* lengths, int n,
                                        int page_size, int32_t* status, void* stream) {
   if (n <= 0) return GRS_OK;
-  cache_check_lengths_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+  cache_check_lengths_kernel<<<ceil_div(n, 256), 256, 0, grs::counted((cudaStream_t)stream)>>>(
       nblocks, lengths, n, page_size, status);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;

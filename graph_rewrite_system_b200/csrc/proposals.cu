@@ -274,33 +274,33 @@ extern "C" int grs_proposals_rank(
     return GRS_OK;
   }
   const int T = 256;
-  prop_count_kernel<<<ceil_div(c, T), T, 0, s>>>(sources, c, xfer_counts, all_xfer_counts,
+  prop_count_kernel<<<ceil_div(c, T), T, 0, grs::counted(s)>>>(sources, c, xfer_counts, all_xfer_counts,
                                                  num_sources, w.counts, out_metrics, status);
   size_t tb = w.cub_bytes;
   cub::DeviceScan::ExclusiveSum(w.cub_tmp, tb, w.counts, w.offsets, (int)c, s);
-  prop_total_kernel<<<1, 1, 0, s>>>(w.counts, w.offsets, c, w.total);
-  prop_expand_kernel<<<ceil_div(c, T), T, 0, s>>>(
+  prop_total_kernel<<<1, 1, 0, grs::counted(s)>>>(w.counts, w.offsets, c, w.total);
+  prop_expand_kernel<<<ceil_div(c, T), T, 0, grs::counted(s)>>>(
       batch_ids, sources, probabilities, c, w.counts, w.offsets, xfer_offsets, xfer_ids,
       gate_deltas, parent_gate_counts, num_parents, w.e_row, w.e_xfer, w.e_next, w.e_parent,
       w.key_in, w.val_in, n, status);
-  prop_pad_kernel<<<ceil_div(n, T), T, 0, s>>>(w.total, n, w.key_in, w.val_in);
+  prop_pad_kernel<<<ceil_div(n, T), T, 0, grs::counted(s)>>>(w.total, n, w.key_in, w.val_in);
   // (next_gate, prob desc, xfer) then stable by parent.
   tb = w.cub_bytes;
   cub::DeviceRadixSort::SortPairs(w.cub_tmp, tb, w.key_in, w.key_out, w.val_in, w.val_out,
                                   (int)n, 0, 64, s);
-  prop_parent_key_kernel<<<ceil_div(n, T), T, 0, s>>>(w.val_out, n, w.total, w.e_parent,
+  prop_parent_key_kernel<<<ceil_div(n, T), T, 0, grs::counted(s)>>>(w.val_out, n, w.total, w.e_parent,
                                                       w.pkey_in);
   tb = w.cub_bytes;
   cub::DeviceRadixSort::SortPairs(w.cub_tmp, tb, w.pkey_in, w.pkey_out, w.val_out, w.val_in,
                                   (int)n, 0, 32, s);
-  prop_segment_start_kernel<<<ceil_div(n, T), T, 0, s>>>(w.pkey_out, n, w.seg_start);
+  prop_segment_start_kernel<<<ceil_div(n, T), T, 0, grs::counted(s)>>>(w.pkey_out, n, w.seg_start);
   tb = w.cub_bytes;
   cub::DeviceScan::InclusiveScan(w.cub_tmp, tb, w.seg_start, w.val_out, cub::Max(), (int)n, s);
-  prop_flag_kernel<<<ceil_div(n, T), T, 0, s>>>(w.pkey_out, w.val_out, n, per_parent_cap,
+  prop_flag_kernel<<<ceil_div(n, T), T, 0, grs::counted(s)>>>(w.pkey_out, w.val_out, n, per_parent_cap,
                                                 w.flags);
   tb = w.cub_bytes;
   cub::DeviceSelect::Flagged(w.cub_tmp, tb, w.val_in, w.flags, w.kept, w.num_kept, (int)n, s);
-  prop_global_key_kernel<<<ceil_div(n, T), T, 0, s>>>(w.kept, w.num_kept, n, w.e_next, w.e_row,
+  prop_global_key_kernel<<<ceil_div(n, T), T, 0, grs::counted(s)>>>(w.kept, w.num_kept, n, w.e_next, w.e_row,
                                                       w.e_parent, probabilities,
                                                       parent_gate_counts, w.key_in, w.val_in,
                                                       status);
@@ -308,7 +308,7 @@ extern "C" int grs_proposals_rank(
   cub::DeviceRadixSort::SortPairs(w.cub_tmp, tb, w.key_in, w.key_out, w.val_in, w.val_out,
                                   (int)n, 0, 64, s);
   if (global_cap > 0)
-    prop_output_kernel<<<ceil_div(global_cap, T), T, 0, s>>>(
+    prop_output_kernel<<<ceil_div(global_cap, T), T, 0, grs::counted(s)>>>(
         w.val_out, w.num_kept, global_cap, w.e_row, w.e_xfer, w.e_next, out_row, out_xfer,
         out_next_gate, out_count);
   else
@@ -645,17 +645,17 @@ extern "C" int grs_proposals_rank_grouped(
                          GRP_MAX_EXPANDED * 8);
     attr[dev] = true;
   }
-  prop_grouped_parent_kernel<<<(unsigned)parents, GRP_THREADS, GRP_MAX_EXPANDED * 8, s>>>(
+  prop_grouped_parent_kernel<<<(unsigned)parents, GRP_THREADS, GRP_MAX_EXPANDED * 8, grs::counted(s)>>>(
       sources, probabilities, k, parent_gate_counts, xfer_offsets, xfer_counts, xfer_ids,
       gate_deltas, all_xfer_counts, num_sources, per_parent_cap, sel_row, sel_xfer, sel_next,
       out_metrics, status);
-  prop_grouped_key_kernel<<<ceil_div(n, 256), 256, 0, s>>>(sel_row, sel_next, probabilities,
+  prop_grouped_key_kernel<<<ceil_div(n, 256), 256, 0, grs::counted(s)>>>(sel_row, sel_next, probabilities,
                                                            parent_gate_counts, k, n, key_in,
                                                            val_in, status);
   cub::DeviceRadixSort::SortPairs(cub_tmp, tb, key_in, key_out, val_in, val_out, (int)n, 0, 64,
                                   s);
   if (global_cap > 0)
-    prop_grouped_output_kernel<<<ceil_div(global_cap, 256), 256, 0, s>>>(
+    prop_grouped_output_kernel<<<ceil_div(global_cap, 256), 256, 0, grs::counted(s)>>>(
         key_out, val_out, global_cap, sel_row, sel_xfer, sel_next, n, out_row, out_xfer,
         out_next_gate, out_count);
   GRS_CUDA_CHECK_LAUNCH();

@@ -526,7 +526,7 @@ extern "C" int grs_topology_plan(int64_t count_cap, const int64_t* count, const 
   PlanArgs a{count_cap, count, rows, xfers, next_gate, cand_batch, cand_bindings, cand_pattern,
              table, types, Ports{out_node, out_port, in_node, in_port}, slots, next_slot,
              fingerprint, valid, fp_out, status};
-  topology_plan_kernel<<<ceil_div(count_cap, 128), 128, 0, (cudaStream_t)stream>>>(a);
+  topology_plan_kernel<<<ceil_div(count_cap, 128), 128, 0, grs::counted((cudaStream_t)stream)>>>(a);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
@@ -549,9 +549,9 @@ extern "C" int grs_topology_accept(int64_t count_cap, const int64_t* count, cons
   if (smem > 200 * 1024) return GRS_ERR_SHAPE;
   cudaMemsetAsync(step_keys, 0, step_capacity * sizeof(uint64_t), s);
   cudaMemsetAsync(step_first, 0x7f, step_capacity * sizeof(int32_t), s);
-  topology_first_kernel<<<ceil_div(count_cap, 256), 256, 0, s>>>(valid, fp, count_cap, step_keys,
+  topology_first_kernel<<<ceil_div(count_cap, 256), 256, 0, grs::counted(s)>>>(valid, fp, count_cap, step_keys,
                                                                 step_first, step_capacity, status);
-  topology_classify_kernel<<<ceil_div(count_cap, 256), 256, 0, s>>>(
+  topology_classify_kernel<<<ceil_div(count_cap, 256), 256, 0, grs::counted(s)>>>(
       valid, fp, count_cap, step_keys, step_first, step_capacity, seen, seen_capacity, classes);
   static bool attr[64] = {};
   int dev = 0;
@@ -561,10 +561,10 @@ extern "C" int grs_topology_accept(int64_t count_cap, const int64_t* count, cons
                          200 * 1024);
     attr[dev] = true;
   }
-  topology_accept_kernel<<<1, ACC_THREADS, smem, s>>>(classes, count, count_cap, fp, next_gate,
+  topology_accept_kernel<<<1, ACC_THREADS, smem, grs::counted(s)>>>(classes, count, count_cap, fp, next_gate,
                                                       beam_size, seen, seen_capacity,
                                                       child_proposal, summary, status);
-  topology_extent_kernel<<<1, 256, 0, s>>>(child_proposal, summary, rows, xfers, cand_batch,
+  topology_extent_kernel<<<1, 256, 0, grs::counted(s)>>>(child_proposal, summary, rows, xfers, cand_batch,
                                            table, next_slot, summary + 4);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
@@ -607,7 +607,7 @@ extern "C" int grs_topology_materialize(
                          cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
     attr[dev] = true;
   }
-  topology_materialize_kernel<<<max_children, MAT_THREADS, smem, (cudaStream_t)stream>>>(a);
+  topology_materialize_kernel<<<max_children, MAT_THREADS, smem, grs::counted((cudaStream_t)stream)>>>(a);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
@@ -617,7 +617,7 @@ extern "C" int grs_topology_fingerprint(const int64_t* types, const int32_t* out
                                         const int32_t* in_port, int batch, int slots,
                                         uint64_t* fp, void* stream) {
   if (batch <= 0) return GRS_OK;
-  topology_fingerprint_kernel<<<batch, 256, 0, (cudaStream_t)stream>>>(
+  topology_fingerprint_kernel<<<batch, 256, 0, grs::counted((cudaStream_t)stream)>>>(
       types, Ports{const_cast<int32_t*>(out_node), const_cast<int32_t*>(out_port),
                    const_cast<int32_t*>(in_node), const_cast<int32_t*>(in_port)},
       slots, fp);
@@ -643,7 +643,7 @@ extern "C" int grs_topology_seen_insert(const uint64_t* fp, int64_t n, uint64_t*
                                         int64_t seen_capacity, int32_t* status, void* stream) {
   if (n <= 0) return GRS_OK;
   if (seen_capacity & (seen_capacity - 1)) return GRS_ERR_SHAPE;
-  seen_insert_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(fp, n, seen,
+  seen_insert_kernel<<<ceil_div(n, 256), 256, 0, grs::counted((cudaStream_t)stream)>>>(fp, n, seen,
                                                                          seen_capacity, status);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;

@@ -21,7 +21,12 @@ def dtype_code(t: torch.Tensor) -> int:
 
 
 def stream() -> int:
-    return torch.cuda.current_stream().cuda_stream
+    """Raw handle of the stream the wrappers launch on: the stream pinned by
+    an enclosing ``pinned_stream()`` block, else torch's current stream."""
+    return _lib.current_stream()
+
+
+pinned_stream = _lib.pinned_stream
 
 
 def _p(t):

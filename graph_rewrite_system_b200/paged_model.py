@@ -189,8 +189,19 @@ class PagedActionBindingModel(nn.Module):
         self._w: dict[str, torch.Tensor] = {}
 
     # ---- weight preparation ---------------------------------------------------
+    def _apply(self, fn, *args, **kwargs):
+        # .to()/.cuda()/.float() may swap parameter storage: list them afresh
+        self._param_list = None
+        return super()._apply(fn, *args, **kwargs)
+
     def _version_key(self):
-        return tuple((p.data_ptr(), p._version) for p in self.parameters()) + (self.compute_dtype,)
+        """Storage pointer and in-place version of every parameter: changes
+        whenever a parameter is replaced or written (load_state_dict, an
+        optimizer step), so the prepared weights are rebuilt."""
+        params = getattr(self, "_param_list", None)
+        if params is None:
+            params = self._param_list = list(self.parameters())
+        return tuple((p.data_ptr(), p._version) for p in params) + (self.compute_dtype,)
 
     @torch.no_grad()
     def prepare(self) -> dict[str, torch.Tensor]:

@@ -189,6 +189,10 @@ class DeviceBeamSearch:
     # ---- one level --------------------------------------------------------------
     @torch.no_grad()
     def step(self) -> StepRow | None:
+        with K.pinned_stream():
+            return self._step()
+
+    def _step(self) -> StepRow | None:
         cfg, model, dev = self.cfg, self.model, self.device
         b, s, depth = self.beams, self.slots, self.depth
         topo = self.topo

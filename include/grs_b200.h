@@ -42,6 +42,10 @@ enum { GRS_DTYPE_BF16 = 0, GRS_DTYPE_F32 = 1 };
 /* Library version string. */
 GRS_API const char* grs_version(void);
 
+/* Number of kernels this library has launched in the process so far (every
+ * launch site counts itself; library kernels such as CUB sorts do not). */
+GRS_API int64_t grs_launch_count(void);
+
 /* ---- paged attention: paged_attention.py:217-306 (paged_attention) ------
  * query [B,H,Q,D] (strides q_sb,q_sh,q_sq; D contiguous); key/value cache
  * [pages,page,H,D] (strides kc_sp,kc_st,kc_sh; D contiguous); block_table

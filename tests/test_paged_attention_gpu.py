@@ -158,3 +158,31 @@ def test_cluster_decode_prefix_tree(cuda_device):
                                  w.block_table.cpu(), w.lengths.cpu(), shared_key=f(w.shared_key),
                                  shared_value=f(w.shared_value))
     np.testing.assert_allclose(got.float().cpu().numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+
+
+def test_cluster_decode_takes_the_cluster_kernel(cuda_device):
+    """The decode workload's layout is accepted by the cluster kernel itself
+    (a non-zero return would mean the rows-kernel fallback ran instead)."""
+    from graph_rewrite_system_b200 import _lib
+    from graph_rewrite_system_b200.paged_attention import check_decode_status
+    from graph_rewrite_system_b200.workloads import decode_attention_workload
+
+    w = decode_attention_workload(cuda_device, beams=40, num_shared=381, seed=9)
+    out = torch.empty_like(w.query)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    q, kc = w.query, w.key_cache
+    rc = _lib.lib().grs_decode_attention_shared(
+        q.data_ptr(), q.stride(0), q.stride(1), kc.data_ptr(), w.value_cache.data_ptr(),
+        kc.stride(0), kc.stride(1), kc.stride(2), w.block_table.data_ptr(),
+        w.block_table.stride(0), w.block_table.shape[1], w.lengths.data_ptr(), kc.shape[0],
+        None, None, 0, 0, None, w.shared_key.data_ptr(), w.shared_value.data_ptr(),
+        w.shared_key.shape[0], out.data_ptr(), out.stride(0), out.stride(1), q.shape[0],
+        q.shape[1], kc.shape[1], status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    assert int(status.item()) == 0
+    f = lambda t: t.float().cpu()
+    exp = oracle.paged_attention(f(w.query), f(w.key_cache), f(w.value_cache),
+                                 w.block_table.cpu(), w.lengths.cpu(), shared_key=f(w.shared_key),
+                                 shared_value=f(w.shared_value))
+    np.testing.assert_allclose(out.float().cpu().numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+    check_decode_status(cuda_device)
