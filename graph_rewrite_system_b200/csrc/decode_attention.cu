@@ -16,7 +16,7 @@
 //
 // Each CTA of the cluster takes every eighth shared unit and every eighth
 // page/current unit.  Warp 8 of the CTA is the producer: per unit it issues
-// two TMA tile loads (cp.async.bulk.tensor, no multicast), one for the K and
+// two TMA tile loads (cp.async.bulk.tensor into its own shared memory only), one for the K and
 // one for the V rows of all heads, into a ring of five stages, completion
 // counted on the stage's "full" mbarrier.  The tensor maps view a key row
 // (H*32 bf16) as H/2 chunks of 128 bytes and make the chunk the outermost
@@ -106,7 +106,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
-// TMA tile loads into this CTA's shared memory (no multicast); the
+// TMA tile loads into this CTA's own shared memory; the
 // innermost coordinate is always 0 (a whole 128-byte chunk)
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int y, int z,
                                             uint64_t* bar) {

@@ -252,9 +252,48 @@ __global__ void cache_check_lengths_kernel(const int32_t* __restrict__ nblocks,
   if (i < n && blocks_for(lengths[i], page) != nblocks[i]) set_status(status, GRS_ERR_LENGTH);
 }
 
+// Pop n pages from the top of the free list (request i takes
+// free_list[fc - 1 - i], the order the fork kernel uses), give each
+// refcount 1 and shrink the free count.  One CTA: the count is read before
+// any thread writes it.
+__global__ void cache_alloc_kernel(int32_t* __restrict__ refcounts,
+                                   const int32_t* __restrict__ free_list,
+                                   int32_t* __restrict__ free_count, int capacity, int n,
+                                   int32_t* __restrict__ out_pages, int32_t* __restrict__ status) {
+  const int fc = *free_count;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int page_id = 0;
+    if (i >= fc) {
+      set_status(status, GRS_ERR_EXHAUSTED);
+    } else {
+      const int candidate = free_list[fc - 1 - i];
+      if (candidate < 0 || candidate >= capacity || refcounts[candidate] != 0) {
+        set_status(status, GRS_ERR_CORRUPT);
+      } else {
+        page_id = candidate;
+        refcounts[page_id] = 1;
+      }
+    }
+    out_pages[i] = page_id;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *free_count = fc - min(n, fc);
+}
+
 }  // namespace grs
 
 using namespace grs;
+
+extern "C" int grs_cache_alloc(int32_t* refcounts, const int32_t* free_list,
+                               int32_t* free_count, int capacity, int n, int32_t* out_pages,
+                               int32_t* status, void* stream) {
+  if (n <= 0) return GRS_OK;
+  if (capacity <= 0) return GRS_ERR_SHAPE;
+  cache_alloc_kernel<<<1, 256, 0, grs::counted((cudaStream_t)stream)>>>(
+      refcounts, free_list, free_count, capacity, n, out_pages, status);
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
 
 extern "C" int grs_cache_init(int32_t* refcounts, int32_t* free_list, int32_t* free_count,
                               int32_t* last_pos, int capacity, void* stream) {

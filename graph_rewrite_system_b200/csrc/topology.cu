@@ -564,8 +564,12 @@ extern "C" int grs_topology_accept(int64_t count_cap, const int64_t* count, cons
   topology_accept_kernel<<<1, ACC_THREADS, smem, grs::counted(s)>>>(classes, count, count_cap, fp, next_gate,
                                                       beam_size, seen, seen_capacity,
                                                       child_proposal, summary, status);
-  topology_extent_kernel<<<1, 256, 0, grs::counted(s)>>>(child_proposal, summary, rows, xfers, cand_batch,
-                                           table, next_slot, summary + 4);
+  if (rows != nullptr)
+    topology_extent_kernel<<<1, 256, 0, grs::counted(s)>>>(child_proposal, summary, rows, xfers,
+                                                           cand_batch, table, next_slot,
+                                                           summary + 4);
+  else
+    cudaMemsetAsync(summary + 4, 0, sizeof(int64_t), s);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }

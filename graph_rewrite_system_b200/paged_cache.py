@@ -180,6 +180,52 @@ class PagedKVCache:
             lengths.data_ptr(), n, table.shape[1], self.page_size, self._status.data_ptr(),
             self._stream()), "release")
 
+    # ---- moving rows between caches (sharded beam search) -------------------
+    def _arenas(self) -> list[torch.Tensor]:
+        """Every arena as a [capacity, page elements] view (page-major), per
+        layer for the K/V arenas."""
+        cap = self.capacity
+        return ([self.keys[l].view(cap, -1) for l in range(self.layers)]
+                + [self.values[l].view(cap, -1) for l in range(self.layers)]
+                + [self.actions.view(cap, -1), self.readout_keys.view(cap, -1),
+                   self.readout_values.view(cap, -1)])
+
+    @property
+    def page_bytes(self) -> int:
+        """Bytes one page holds across all arenas (the export row size)."""
+        return sum(a.shape[1] * a.element_size() for a in self._arenas())
+
+    def export_pages(self, pages: torch.Tensor) -> torch.Tensor:
+        """Contents of the given pages (device int ids), one uint8 row of
+        ``page_bytes`` each, arenas in a fixed order."""
+        if pages.numel() == 0:
+            return torch.empty(0, self.page_bytes, device=self.device, dtype=torch.uint8)
+        idx = pages.long()
+        return torch.cat([a.index_select(0, idx).view(torch.uint8) for a in self._arenas()],
+                         dim=1)
+
+    def import_pages(self, data: torch.Tensor) -> torch.Tensor:
+        """Allocate ``len(data)`` pages (refcount 1, free-list order) and fill
+        them with rows produced by ``export_pages`` of a cache of the same
+        shape; returns the new page ids (device int32)."""
+        n = data.shape[0]
+        pages = torch.empty(n, device=self.device, dtype=torch.int32)
+        if n == 0:
+            return pages
+        if data.shape[1] != self.page_bytes:
+            raise ValueError("page rows do not match this cache's page layout")
+        _lib.check(_lib.lib().grs_cache_alloc(
+            self._refcounts.data_ptr(), self._free.data_ptr(), self._free_count.data_ptr(),
+            self.capacity, n, pages.data_ptr(), self._status.data_ptr(), self._stream()),
+            "import_pages")
+        idx = pages.long()
+        offset = 0
+        for arena in self._arenas():
+            width = arena.shape[1] * arena.element_size()
+            arena.index_copy_(0, idx, data[:, offset:offset + width].contiguous().view(arena.dtype))
+            offset += width
+        return pages
+
     # ---- reference API ----------------------------------------------------
     def _handle_rows(self, handles: list[PrefixHandle], min_cols: int = 1):
         cols = max([len(h.blocks) for h in handles] + [min_cols])

@@ -31,7 +31,7 @@ import torch
 
 from . import _lib
 from . import kernels as K
-from .gpu_proposals import GpuRuleIndex, rank_proposals_grouped
+from .gpu_proposals import GpuRuleIndex, RankedProposals, rank_proposals_grouped
 from .paged_cache import PagedKVCache
 from .paged_model import PagedActionBindingModel
 from .synthetic import (Circuit, RolloutConfig, RuleMetadata, SELECT_ALL_THRESHOLDS)
@@ -65,6 +65,17 @@ class StepRow:
     allocated_cache_pages: int
     logical_cache_pages: int
     page_sharing_ratio: float
+
+
+@dataclass
+class Proposed:
+    """Ranked and planned proposals of one GPU's beams at one level."""
+
+    ranked: "RankedProposals"
+    cand: dict
+    valid: torch.Tensor          # uint8 [global_cap] structurally valid
+    fp: torch.Tensor             # int64 [global_cap] child fingerprint
+    k: int                       # candidate rows per parent
 
 
 class StageTimer:
@@ -193,8 +204,51 @@ class DeviceBeamSearch:
             return self._step()
 
     def _step(self) -> StepRow | None:
-        cfg, model, dev = self.cfg, self.model, self.device
+        cfg, dev = self.cfg, self.device
         b, s, depth = self.beams, self.slots, self.depth
+        prop = self._propose()
+        # 4. accept (first occurrence of unseen valid fingerprints, in rank order)
+        gcap = cfg.global_cap
+        classes = torch.empty(gcap, device=dev, dtype=torch.uint8)
+        child_proposal = torch.empty(cfg.beam_size, device=dev, dtype=torch.int64)
+        self._mark("accept")
+        _lib.check(_lib.lib().grs_topology_accept(
+            gcap, prop.ranked.count.data_ptr(), prop.valid.data_ptr(), prop.fp.data_ptr(),
+            prop.ranked.next_gate.data_ptr(), cfg.beam_size, self.step_keys.data_ptr(),
+            self.step_first.data_ptr(), self.step_capacity, self.seen.data_ptr(),
+            self.seen_capacity, classes.data_ptr(), child_proposal.data_ptr(),
+            self.summary.data_ptr(), prop.ranked.rows.data_ptr(), prop.ranked.xfer_ids.data_ptr(),
+            prop.cand["batch_ids"].data_ptr(), self.table.data_ptr(),
+            self.topo.next_slot.data_ptr(), self.status.data_ptr(), K.stream()),
+            "topology_accept")
+        # one synchronisation per level
+        self._mark("host_sync")
+        host = torch.cat((self.summary, prop.ranked.count, prop.ranked.metrics,
+                          self.cache.allocated_pages_tensor().long(), self.status.long(),
+                          self.cache.status_tensor().long())).cpu()
+        (accepted, attempted, invalid, dup, extent, best, proposals, predicted, eligible_n,
+         allocated, status, cache_status) = host.tolist()
+        if status:
+            self.status.zero_()
+            _lib.check(int(status), "beam search step")
+        if cache_status:
+            self.cache.check_status()
+        row = StepRow(depth + 1, b, accepted, best, predicted, eligible_n, proposals, attempted,
+                      accepted, invalid, dup, allocated, 0, 0.0)
+        if not accepted:
+            self.rows.append(row)
+            return None
+        s_new = max(s, _round_up(int(extent), 8))
+        self._children(prop, child_proposal, self.summary, accepted, s_new)
+        row.logical_cache_pages = accepted * self.block_table.shape[1]
+        self._mark("end")
+        self.rows.append(row)
+        return row
+
+    def _propose(self) -> "Proposed":
+        """Stages 1-3 and the rewrite plan for the current beams."""
+        cfg, model, dev = self.cfg, self.model, self.device
+        b, s = self.beams, self.slots
         topo = self.topo
         ports = topo.ports()
         for name, t in zip(("in_node", "in_port", "out_node", "out_port"), ports):
@@ -217,7 +271,7 @@ class DeviceBeamSearch:
                           allow_negative_one=True)
         self._check_range("candidates", "binding", cand["bindings"], 0, s, allow_negative_one=True)
         # 3. proposals (effective parent cap of paged_rollout_benchmark.py:963-966)
-        cap = max(cfg.per_parent_cap, math.ceil(cfg.beam_size / max(1, b)) * 2)
+        cap = max(cfg.per_parent_cap, math.ceil(cfg.beam_size / max(1, self.global_beams())) * 2)
         self._mark("proposals")
         k = cand["sources"].numel() // b
         ranked = rank_proposals_grouped(cand["sources"], cand["probabilities"], k, topo.gate,
@@ -227,49 +281,35 @@ class DeviceBeamSearch:
                           allow_negative_one=True)
         self._check_range("proposals", "xfer", ranked.xfer_ids, 0, self.rules.num_xfers,
                           allow_negative_one=True)
-        # 4. plan + accept
+        # 4a. rewrite plan: validity and child fingerprint of every ranked proposal
         gcap = cfg.global_cap
         valid = torch.empty(gcap, device=dev, dtype=torch.uint8)
         fp = torch.empty(gcap, device=dev, dtype=torch.int64)
-        classes = torch.empty(gcap, device=dev, dtype=torch.uint8)
-        child_proposal = torch.empty(cfg.beam_size, device=dev, dtype=torch.int64)
         cb = cand["bindings"]
-        stream = K.stream()
-        lib = _lib.lib()
-        self._mark("plan_accept")
-        _lib.check(lib.grs_topology_plan(
+        self._mark("plan")
+        _lib.check(_lib.lib().grs_topology_plan(
             gcap, ranked.count.data_ptr(), ranked.rows.data_ptr(), ranked.xfer_ids.data_ptr(),
             ranked.next_gate.data_ptr(), cand["batch_ids"].data_ptr(), cb.data_ptr(), cb.shape[1],
             self.table.data_ptr(), topo.types.data_ptr(), topo.out_node.data_ptr(),
             topo.out_port.data_ptr(), topo.in_node.data_ptr(), topo.in_port.data_ptr(), s,
             topo.next_slot.data_ptr(), topo.fingerprint.data_ptr(), valid.data_ptr(), fp.data_ptr(),
-            self.status.data_ptr(), stream), "topology_plan")
-        _lib.check(lib.grs_topology_accept(
-            gcap, ranked.count.data_ptr(), valid.data_ptr(), fp.data_ptr(),
-            ranked.next_gate.data_ptr(), cfg.beam_size, self.step_keys.data_ptr(),
-            self.step_first.data_ptr(), self.step_capacity, self.seen.data_ptr(),
-            self.seen_capacity, classes.data_ptr(), child_proposal.data_ptr(),
-            self.summary.data_ptr(), ranked.rows.data_ptr(), ranked.xfer_ids.data_ptr(),
-            cand["batch_ids"].data_ptr(), self.table.data_ptr(), topo.next_slot.data_ptr(),
-            self.status.data_ptr(), stream), "topology_accept")
-        # one synchronisation per level
-        self._mark("host_sync")
-        host = torch.cat((self.summary, ranked.count, ranked.metrics,
-                          self.cache.allocated_pages_tensor().long(), self.status.long(),
-                          self.cache.status_tensor().long())).cpu()
-        (accepted, attempted, invalid, dup, extent, best, proposals, predicted, eligible_n,
-         allocated, status, cache_status) = host.tolist()
-        if status:
-            self.status.zero_()
-            _lib.check(int(status), "beam search step")
-        if cache_status:
-            self.cache.check_status()
-        row = StepRow(depth + 1, b, accepted, best, predicted, eligible_n, proposals, attempted,
-                      accepted, invalid, dup, allocated, 0, 0.0)
-        if not accepted:
-            self.rows.append(row)
-            return None
-        s_new = max(s, _round_up(int(extent), 8))
+            self.status.data_ptr(), K.stream()), "topology_plan")
+        return Proposed(ranked, cand, valid, fp, k)
+
+    def global_beams(self) -> int:
+        """Beams of the whole search at this level (this GPU's beams here)."""
+        return self.beams
+
+    def _children(self, prop: "Proposed", child_proposal: torch.Tensor, summary: torch.Tensor,
+                  accepted: int, s_new: int) -> None:
+        """Stages 5-6 for `accepted` children given as indices into the ranked
+        proposals of this GPU: child topology, model advance, cache append,
+        release of the parents.  Replaces the beam state."""
+        cfg, model, dev = self.cfg, self.model, self.device
+        b, s, depth = self.beams, self.slots, self.depth
+        topo, ranked, cand, fp = self.topo, prop.ranked, prop.cand, prop.fp
+        cb = cand["bindings"]
+        stream = K.stream()
         # 5. child topology
         self._mark("materialize")
         nxt = self.topology[1 - self.current].state(accepted, s_new)
@@ -278,8 +318,8 @@ class DeviceBeamSearch:
         a_src = torch.empty(accepted, self.max_src, **i64)
         a_dst = torch.empty(accepted, max(self.max_dst, 1), **i64)
         a_dst_types = torch.empty_like(a_dst)
-        _lib.check(lib.grs_topology_materialize(
-            accepted, child_proposal.data_ptr(), self.summary.data_ptr(), ranked.rows.data_ptr(),
+        _lib.check(_lib.lib().grs_topology_materialize(
+            accepted, child_proposal.data_ptr(), summary.data_ptr(), ranked.rows.data_ptr(),
             ranked.xfer_ids.data_ptr(), ranked.next_gate.data_ptr(), fp.data_ptr(),
             cand["batch_ids"].data_ptr(), cand["anchors"].data_ptr(), cb.data_ptr(), cb.shape[1],
             self.table.data_ptr(), self.xfer_to_source.data_ptr(), s, s_new,
@@ -329,10 +369,6 @@ class DeviceBeamSearch:
         self.topo, self.current = nxt, 1 - self.current
         self.last_actions = (a_parent, a_xfer, a_src)
         self.beams, self.slots, self.depth = accepted, s_new, depth + 1
-        row.logical_cache_pages = accepted * child_cols
-        self._mark("end")
-        self.rows.append(row)
-        return row
 
     def check(self) -> None:
         code = int(self.status.item())

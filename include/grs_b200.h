@@ -99,6 +99,14 @@ GRS_API int grs_decode_attention_shared(const void* query, int64_t q_sb, int64_t
 GRS_API int grs_cache_init(int32_t* refcounts, int32_t* free_list, int32_t* free_count,
                            int32_t* last_pos, int capacity, void* stream);
 
+/* Allocate n pages for rows copied in from another cache (a beam moved
+ * between GPUs of a sharded search): pop them from the top of the free list
+ * as the append path does, refcount 1 each, page ids into out_pages int32 [n].
+ * GRS_ERR_EXHAUSTED in status when the free list is too short. */
+GRS_API int grs_cache_alloc(int32_t* refcounts, const int32_t* free_list, int32_t* free_count,
+                            int capacity, int n, int32_t* out_pages, int32_t* status,
+                            void* stream);
+
 /* paged_cache.py:107-208 (PagedKVCache.append_batch): for each of n parents
  * (block-table rows + lengths) retain the shared pages, allocate the child
  * page from the top of the free list (parent order), COW-copy the valid rows
@@ -332,7 +340,9 @@ GRS_API int grs_topology_plan(int64_t count_cap, const int64_t* count, const int
  * the first beam_size are accepted, inserted into the seen set and stably
  * sorted by next gate count into child_proposal.  summary int64 [6] =
  * accepted, attempted, invalid, duplicates, max child next slot, best
- * (smallest) child gate count.  Hash
+ * (smallest) child gate count; with rows == NULL the next-slot extent is not
+ * computed (summary[4] = 0: a sharded search ranks records from several GPUs
+ * and takes the extent from the gathered records instead).  Hash
  * tables are power-of-two open-addressing arrays (uint64 keys, 0 = empty). */
 GRS_API int grs_topology_accept(int64_t count_cap, const int64_t* count, const uint8_t* valid,
                                 const uint64_t* fp, const int64_t* next_gate, int beam_size,
