@@ -16,16 +16,18 @@
 //
 // Each CTA of the cluster takes every eighth shared unit and every eighth
 // page/current unit.  Warp 8 of the CTA is the producer: per unit it issues
-// two TMA tile loads (cp.async.bulk.tensor into its own shared memory only), one for the K and
-// one for the V rows of all heads, into a ring of five stages, completion
-// counted on the stage's "full" mbarrier.  The tensor maps view a key row
-// (H*32 bf16) as H/2 chunks of 128 bytes and make the chunk the outermost
-// box dimension, so one 8 KB load lands as H/2 tiles of 16 rows x 128 bytes
-// with the 128-byte swizzle (conflict-free ldmatrix).  The shared
-// units go out at kernel entry, before the block tables are read.  Warps 0-7
-// are the consumers, one per head: each waits for a stage, computes the
-// masked online-softmax partial (max, sum, P.V) of its head for all 16 beams
-// with ldmatrix-fed mma tiles, and releases the stage on its "empty"
+// two TMA tile loads (cp.async.bulk.tensor into its own shared memory only),
+// one for the K and one for the V rows of all heads, into a ring of five
+// stages, completion counted on the stage's "full" mbarrier.  The tensor maps
+// view a key row (H*32 bf16) as H/2 chunks of 128 bytes and make the chunk
+// the outermost box dimension, so one 8 KB load lands as H/2 tiles of 16 rows
+// x 128 bytes with the 128-byte swizzle (conflict-free ldmatrix).  The shared
+// units go out at kernel entry; while they land the producer reads the block
+// tables, deduplicates the pages per column and publishes this CTA's page
+// units (and the beams' lengths) on a "units" mbarrier.  Warps 0-7 are the
+// consumers, one per head: they start on the shared units at once, take two
+// stages per online-softmax step (masked partial max, sum and P.V for all 16
+// beams with ldmatrix-fed mma tiles) and release each stage on its "empty"
 // mbarrier.  Each CTA then pushes its partials into the shared memory of the
 // beams' owners (CTA beam/2); after one cluster barrier the owners merge the
 // eight partials and write the output.
@@ -165,18 +167,6 @@ __device__ __forceinline__ unsigned swz(unsigned tile, int row, int chunk) {
   return tile + row * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
-// barrier among the consumer warps only (the producer keeps streaming)
-__device__ __forceinline__ void consumers_sync() {
-  asm volatile("bar.sync 1, %0;\n" ::"n"(DC_CONSUMERS * 32) : "memory");
-}
-// the consumers publish the page units (arrive); the producer waits for them
-__device__ __forceinline__ void units_ready_arrive() {
-  asm volatile("bar.arrive 2, %0;\n" ::"n"(DC_THREADS) : "memory");
-}
-__device__ __forceinline__ void units_ready_wait() {
-  asm volatile("bar.sync 2, %0;\n" ::"n"(DC_THREADS) : "memory");
-}
-
 __global__ void __cluster_dims__(DC_CLUSTER, 1, 1) __launch_bounds__(DC_THREADS, 2)
 decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
                       const __grid_constant__ CUtensorMap tm_sv,
@@ -187,13 +177,13 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
   // inbox[slot][head][r]: CTA r's partial for local beam `slot` of this CTA,
   // written by CTA r into this CTA's shared memory
   __shared__ Partial inbox[2][DC_CONSUMERS][DC_CLUSTER];
-  __shared__ __align__(8) uint64_t full_bar[DC_NBUF], empty_bar[DC_NBUF];
+  __shared__ __align__(8) uint64_t full_bar[DC_NBUF], empty_bar[DC_NBUF], units_bar;
   __shared__ int s_len[DC_BEAMS], s_cur[DC_BEAMS];
   __shared__ int s_bt[DC_MAX_COLS][DC_BEAMS];
   // distinct (column, page) entries: page id, column << 16 | beam mask
   __shared__ int s_entry_page[DC_BEAMS * DC_MAX_COLS];
   __shared__ int s_entry_cm[DC_BEAMS * DC_MAX_COLS];
-  __shared__ int s_entries, s_nunits;
+  __shared__ int s_nunits;
   // this CTA's page/current units: page id (-1: the current unit), first row
   // in the page, beam mask, position of the first row, rows that are keys
   __shared__ int4 s_unit[DC_MAX_UNITS];
@@ -222,12 +212,14 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], DC_CONSUMERS);
     }
+    mbar_init(&units_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncthreads();
 
   if (warp == DC_PRODUCER) {
-    // ---- producer: lane 0 issues the loads, the warp waits together ----
+    // ---- producer warp: shared stages first, then the block tables, the
+    // per-column page dedup and this CTA's page units, then the page stages
     bool ok = true;
     auto produce = [&](int st, int unit_page, int y0) {
       const int buf = st % DC_NBUF;
@@ -250,12 +242,68 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
       }
       __syncwarp();
     };
-    // the shared units need no block table
-    for (int i = 0; i < my_sh && ok; ++i) produce(i, -2, (rank + i * DC_CLUSTER) * DC_UNIT);
-    // page/current units once the consumers have published them
+    const int first = min(my_sh, DC_NBUF);          // the ring's first round needs no waits
+    for (int i = 0; i < first; ++i) produce(i, -2, (rank + i * DC_CLUSTER) * DC_UNIT);
+
+    // lengths, current-token flags and block-table columns of the 16 beams
+    const int cols = a.max_blocks;   // <= DC_MAX_COLS (host-checked)
+    if (lane < DC_BEAMS) {
+      const int b = beam0 + lane;
+      s_len[lane] = b < a.B ? a.lengths[b] : 0;
+      s_cur[lane] = (b < a.B && a.has_current) ? (a.cvalid[b] != 0) : 0;
+    }
+    for (int i = lane; i < cols * DC_BEAMS; i += 32) {
+      const int c = i >> 4, j = i & 15, b = beam0 + j;
+      s_bt[c][j] = b < a.B ? a.bt[(int64_t)b * a.bt_s + c] : -1;
+    }
     __syncwarp();
-    units_ready_wait();
-    const int nu = s_nunits;
+    // distinct pages per column: lanes 0-15 column c, 16-31 column c+1
+    int count = 0;
+    for (int c0 = 0; c0 < cols; c0 += 2) {
+      const int c = c0 + (lane >> 4), j = lane & 15;
+      int p = -1;
+      if (c < cols && c * a.page < s_len[j]) {
+        p = s_bt[c][j];
+        if (p >= a.num_pages) p = -1;
+      }
+      const unsigned long long key =
+          p >= 0 ? (((unsigned long long)(unsigned)p << 1) | (unsigned)(lane >> 4))
+                 : ((1ull << 63) | (unsigned)lane);
+      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      const bool lead = p >= 0 && __ffs(peers) - 1 == lane;
+      const unsigned leads = __ballot_sync(0xffffffffu, lead);
+      if (lead) {
+        const int e = count + __popc(leads & ((1u << lane) - 1u));
+        s_entry_page[e] = p;
+        s_entry_cm[e] = (c << 16) | ((peers >> (lane & 16)) & 0xFFFF);
+      }
+      count += __popc(leads);
+    }
+    __syncwarp();
+    // this CTA's page/current units: global unit u = entry * (page/16) +
+    // sub-block, the current unit last; CTA r takes u = r, r + 8, ...
+    const int per_page = a.page / DC_UNIT;
+    const int page_units = count * per_page;
+    const int all_units = page_units + (a.has_current ? 1 : 0);
+    const int nu = all_units > rank ? (all_units - rank + DC_CLUSTER - 1) / DC_CLUSTER : 0;
+    int cur_mask = 0;
+    for (int j = 0; j < DC_BEAMS; ++j) cur_mask |= s_cur[j] ? (1 << j) : 0;
+    for (int i = lane; i < nu; i += 32) {
+      const int u = rank + i * DC_CLUSTER;
+      if (u < page_units) {
+        const int e = u / per_page, sub = u - e * per_page;
+        const int cm = s_entry_cm[e];
+        s_unit[i] = make_int4(s_entry_page[e], sub * DC_UNIT, cm & 0xFFFF,
+                              (cm >> 16) * a.page + sub * DC_UNIT);
+      } else {
+        s_unit[i] = make_int4(-1, 0, cur_mask, -1);
+      }
+    }
+    if (lane == 0) s_nunits = nu;
+    __syncwarp();
+    // publish lengths and units to the consumers (release on arrive)
+    if (lane == 0) mbar_arrive(&units_bar);
+    for (int i = first; i < my_sh && ok; ++i) produce(i, -2, (rank + i * DC_CLUSTER) * DC_UNIT);
     for (int i = 0; i < nu && ok; ++i) {
       const int4 u = s_unit[i];
       produce(my_sh + i, u.x, u.y);
@@ -263,18 +311,7 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
     if (!ok && lane == 0 && a.status) atomicCAS(a.status, 0, GRS_ERR_TIMEOUT);
     __syncwarp();
   } else {
-    // ---- consumers: metadata, then the stages ----------------------------
-    // 1. lengths, current-token flags, block-table columns (one round trip)
-    const int cols = a.max_blocks;   // <= DC_MAX_COLS (host-checked)
-    if (tid < DC_BEAMS) {
-      const int b = beam0 + tid;
-      s_len[tid] = b < a.B ? a.lengths[b] : 0;
-      s_cur[tid] = (b < a.B && a.has_current) ? (a.cvalid[b] != 0) : 0;
-    }
-    for (int i = tid; i < cols * DC_BEAMS; i += DC_CONSUMERS * 32) {
-      const int c = i >> 4, j = i & 15, b = beam0 + j;
-      s_bt[c][j] = b < a.B ? a.bt[(int64_t)b * a.bt_s + c] : -1;
-    }
+    // ---- consumers: one warp per head ------------------------------------
     // query fragments of head `warp` for the 16 beams (A operand, rows = beams)
     uint32_t qa[2][4] = {};
     if (warp < a.H) {
@@ -294,113 +331,70 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
         }
       }
     }
-    consumers_sync();
-
-    // 2. distinct pages per column: lanes 0-15 column c, 16-31 column c+1
-    if (warp == 0) {
-      int count = 0;
-      for (int c0 = 0; c0 < cols; c0 += 2) {
-        const int c = c0 + (lane >> 4), j = lane & 15;
-        int p = -1;
-        if (c < cols && c * a.page < s_len[j]) {
-          p = s_bt[c][j];
-          if (p >= a.num_pages) p = -1;
-        }
-        const unsigned long long key =
-            p >= 0 ? (((unsigned long long)(unsigned)p << 1) | (unsigned)(lane >> 4))
-                   : ((1ull << 63) | (unsigned)lane);
-        const unsigned peers = __match_any_sync(0xffffffffu, key);
-        const bool lead = p >= 0 && __ffs(peers) - 1 == lane;
-        const unsigned leads = __ballot_sync(0xffffffffu, lead);
-        if (lead) {
-          const int e = count + __popc(leads & ((1u << lane) - 1u));
-          s_entry_page[e] = p;
-          s_entry_cm[e] = (c << 16) | ((peers >> (lane & 16)) & 0xFFFF);
-        }
-        count += __popc(leads);
-      }
-      if (lane == 0) s_entries = count;
-    }
-    consumers_sync();
-
-    // 3. this CTA's page/current units: global unit u = entry * (page/16) +
-    //    sub-block, the current unit last; CTA r takes u = r, r + 8, ...
-    const int per_page = a.page / DC_UNIT;
-    const int page_units = s_entries * per_page;
-    const int all_units = page_units + (a.has_current ? 1 : 0);
-    const int nu = all_units > rank ? (all_units - rank + DC_CLUSTER - 1) / DC_CLUSTER : 0;
-    for (int i = tid; i < nu; i += DC_CONSUMERS * 32) {
-      const int u = rank + i * DC_CLUSTER;
-      if (u < page_units) {
-        const int e = u / per_page, sub = u - e * per_page;
-        const int cm = s_entry_cm[e];
-        s_unit[i] = make_int4(s_entry_page[e], sub * DC_UNIT, cm & 0xFFFF,
-                              (cm >> 16) * a.page + sub * DC_UNIT);
-      } else {
-        int mask = 0;
-        for (int j = 0; j < DC_BEAMS; ++j) mask |= s_cur[j] ? (1 << j) : 0;
-        s_unit[i] = make_int4(-1, 0, mask, -1);
-      }
-    }
-    if (tid == 0) s_nunits = nu;
-    consumers_sync();
-    units_ready_arrive();
-    const int stages = my_sh + nu;
-
-    // 4. consume the ring
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float o[4][4] = {};
     const int h = warp;
-    const int len0 = s_len[g], len1 = s_len[g + 8];
     bool ok = true;
-    for (int st = 0; st < stages; ++st) {
-      const int buf = st % DC_NBUF;
-      if (ok) ok = mbar_wait(&full_bar[buf], (unsigned)((st / DC_NBUF) & 1));
+    int len0 = 0, len1 = 0, nu = 0;
+
+    // consume n (1 or 2) consecutive stages from `st` as one softmax step
+    auto consume = [&](int st, int n) {
+      int buf[2] = {st % DC_NBUF, (st + 1) % DC_NBUF};
+      for (int k = 0; k < n; ++k)
+        if (ok) ok = mbar_wait(&full_bar[buf[k]], (unsigned)(((st + k) / DC_NBUF) & 1));
       if (ok && h < a.H) {
-        // visibility of the stage's 16 rows for beams g (v0) and g + 8 (v1)
-        int kind, mask = 0xFFFF, pos0 = -1, rows = DC_UNIT;
-        if (st < my_sh) {
-          kind = 0;
-          rows = min(DC_UNIT, ns - (rank + st * DC_CLUSTER) * DC_UNIT);
-        } else {
-          const int4 u = s_unit[st - my_sh];
-          kind = u.x >= 0 ? 1 : 2;
-          mask = u.z;
-          pos0 = u.w;
-        }
-        const bool see0 = (mask >> g) & 1, see1 = (mask >> (g + 8)) & 1;
-        const unsigned kt = ring + buf * DC_STAGE_BYTES + (h >> 1) * DC_BOX_BYTES;
-        const unsigned vt = kt + 4 * DC_BOX_BYTES;
-        const int hc = (h & 1) * 4;                    // chunk of this head in the tile row
-        float s[2][4] = {};
+        float s[2][2][4] = {};
+        const int hc = (h & 1) * 4;                  // chunk of this head in a tile row
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          uint32_t kf[4];
-          ldmatrix_x4(kf, swz(kt, nt * 8 + (lane & 7), hc + (lane >> 3)));
-          mma16816(s[nt], qa[0], kf[0], kf[1]);
-          mma16816(s[nt], qa[1], kf[2], kf[3]);
+        for (int k = 0; k < 2; ++k) {
+          if (k >= n) break;
+          const unsigned kt = ring + buf[k] * DC_STAGE_BYTES + (h >> 1) * DC_BOX_BYTES;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            uint32_t kf[4];
+            ldmatrix_x4(kf, swz(kt, nt * 8 + (lane & 7), hc + (lane >> 3)));
+            mma16816(s[k][nt], qa[0], kf[0], kf[1]);
+            mma16816(s[k][nt], qa[1], kf[2], kf[3]);
+          }
         }
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int r = nt * 8 + tig * 2 + c;
-            bool v0, v1;
-            if (kind == 0) {
-              v0 = v1 = r < rows;
-            } else if (kind == 1) {
-              v0 = see0 && pos0 + r < len0;
-              v1 = see1 && pos0 + r < len1;
-            } else {                                   // row r is beam r's current token
-              v0 = see0 && r == g;
-              v1 = see1 && r == g + 8;
-            }
-            s[nt][c] = v0 ? s[nt][c] * a.scale_log2 : -INFINITY;
-            s[nt][2 + c] = v1 ? s[nt][2 + c] * a.scale_log2 : -INFINITY;
-            mx0 = fmaxf(mx0, s[nt][c]);
-            mx1 = fmaxf(mx1, s[nt][2 + c]);
+        for (int k = 0; k < 2; ++k) {
+          if (k >= n) break;
+          const int sk = st + k;
+          // visibility of the stage's rows for beams g (v0) and g + 8 (v1)
+          int kind, mask = 0xFFFF, pos0 = -1, rows = DC_UNIT;
+          if (sk < my_sh) {
+            kind = 0;
+            rows = min(DC_UNIT, ns - (rank + sk * DC_CLUSTER) * DC_UNIT);
+          } else {
+            const int4 u = s_unit[sk - my_sh];
+            kind = u.x >= 0 ? 1 : 2;
+            mask = u.z;
+            pos0 = u.w;
           }
+          const bool see0 = (mask >> g) & 1, see1 = (mask >> (g + 8)) & 1;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int r = nt * 8 + tig * 2 + c;
+              bool v0, v1;
+              if (kind == 0) {
+                v0 = v1 = r < rows;
+              } else if (kind == 1) {
+                v0 = see0 && pos0 + r < len0;
+                v1 = see1 && pos0 + r < len1;
+              } else {                               // row r is beam r's current token
+                v0 = see0 && r == g;
+                v1 = see1 && r == g + 8;
+              }
+              s[k][nt][c] = v0 ? s[k][nt][c] * a.scale_log2 : -INFINITY;
+              s[k][nt][2 + c] = v1 ? s[k][nt][2 + c] * a.scale_log2 : -INFINITY;
+              mx0 = fmaxf(mx0, s[k][nt][c]);
+              mx1 = fmaxf(mx1, s[k][nt][2 + c]);
+            }
+        }
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
@@ -412,14 +406,18 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
         const float c0 = fast_exp2(m0 - e0), c1 = fast_exp2(m1 - e1);
         float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+        for (int k = 0; k < 2; ++k) {
+          if (k >= n) break;
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            s[nt][c] = fast_exp2(s[nt][c] - e0);
-            s[nt][2 + c] = fast_exp2(s[nt][2 + c] - e1);
-            sum0 += s[nt][c];
-            sum1 += s[nt][2 + c];
-          }
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              s[k][nt][c] = fast_exp2(s[k][nt][c] - e0);
+              s[k][nt][2 + c] = fast_exp2(s[k][nt][2 + c] - e1);
+              sum0 += s[k][nt][c];
+              sum1 += s[k][nt][2 + c];
+            }
+        }
         // per-lane partial row sums; the quad reduction happens once at the end
         l0 = l0 * c0 + sum0;
         l1 = l1 * c1 + sum1;
@@ -429,24 +427,46 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
         for (int nt = 0; nt < 4; ++nt) {
           o[nt][0] *= c0; o[nt][1] *= c0; o[nt][2] *= c1; o[nt][3] *= c1;
         }
-        uint32_t pa[4];
-        pa[0] = pack2(s[0][0], s[0][1]);
-        pa[1] = pack2(s[0][2], s[0][3]);
-        pa[2] = pack2(s[1][0], s[1][1]);
-        pa[3] = pack2(s[1][2], s[1][3]);
 #pragma unroll
-        for (int dp = 0; dp < 2; ++dp) {
-          // four 8x8 tiles: keys 0-7 / 8-15 x dims dp*16 + 0-7 / 8-15
-          uint32_t vf[4];
-          ldmatrix_x4_trans(vf, swz(vt, (lane & 7) + ((lane >> 3) & 1) * 8,
-                                    hc + dp * 2 + (lane >> 4)));
-          mma16816(o[2 * dp], pa, vf[0], vf[1]);
-          mma16816(o[2 * dp + 1], pa, vf[2], vf[3]);
+        for (int k = 0; k < 2; ++k) {
+          if (k >= n) break;
+          const unsigned vt = ring + buf[k] * DC_STAGE_BYTES + (h >> 1) * DC_BOX_BYTES +
+                              4 * DC_BOX_BYTES;
+          uint32_t pa[4];
+          pa[0] = pack2(s[k][0][0], s[k][0][1]);
+          pa[1] = pack2(s[k][0][2], s[k][0][3]);
+          pa[2] = pack2(s[k][1][0], s[k][1][1]);
+          pa[3] = pack2(s[k][1][2], s[k][1][3]);
+#pragma unroll
+          for (int dp = 0; dp < 2; ++dp) {
+            // four 8x8 tiles: keys 0-7 / 8-15 x dims dp*16 + 0-7 / 8-15
+            uint32_t vf[4];
+            ldmatrix_x4_trans(vf, swz(vt, (lane & 7) + ((lane >> 3) & 1) * 8,
+                                      hc + dp * 2 + (lane >> 4)));
+            mma16816(o[2 * dp], pa, vf[0], vf[1]);
+            mma16816(o[2 * dp + 1], pa, vf[2], vf[3]);
+          }
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[buf]);
+      if (lane == 0)
+        for (int k = 0; k < n; ++k) mbar_arrive(&empty_bar[buf[k]]);
+    };
+
+    // the shared stages need no block-table data
+    int st = 0;
+    for (; st + 1 < my_sh; st += 2) consume(st, 2);
+    if (st < my_sh) consume(st++, 1);
+    // then the page/current stages, once the producer has published them
+    ok = ok && mbar_wait(&units_bar, 0);
+    if (ok) {
+      nu = s_nunits;
+      len0 = s_len[g];
+      len1 = s_len[g + 8];
     }
+    const int stages = my_sh + nu;
+    for (; st + 1 < stages; st += 2) consume(st, 2);
+    if (st < stages) consume(st++, 1);
     if (!ok && lane == 0 && a.status) atomicCAS(a.status, 0, GRS_ERR_TIMEOUT);
 
     // 5. push the partials of beams g and g+8 to their owners
