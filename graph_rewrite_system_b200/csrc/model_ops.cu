@@ -5,6 +5,8 @@
 // (fp32 for the CPU-equivalence configuration, bf16 for the rollout) and
 // computes in fp32.  Rows are processed one warp per row; each lane owns the
 // row elements lane, lane + 32, ... (coalesced 32-lane accesses).
+#include <algorithm>
+
 #include "grs_common.cuh"
 
 namespace grs {
@@ -274,58 +276,148 @@ __global__ void position_token_kernel(const T* raw, const float* position, const
   token[idx] = from_float<T>(v);
 }
 
+// N consecutive elements as fp32 with the widest aligned accesses (the
+// pointer must be aligned to min(16, N * sizeof(T)) bytes).
+template <int N>
+__device__ __forceinline__ void load_vec(const __nv_bfloat16* p, float* v) {
+  if constexpr (N >= 8) {
+#pragma unroll
+    for (int i = 0; i < N / 8; ++i) load8(p + 8 * i, v + 8 * i);
+  } else if constexpr (N == 4) {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  } else if constexpr (N == 2) {
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    v[0] = a.x; v[1] = a.y;
+  } else {
+    v[0] = __bfloat162float(p[0]);
+  }
+}
+template <int N>
+__device__ __forceinline__ void load_vec(const float* p, float* v) {
+  if constexpr (N >= 4) {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      const float4 a = reinterpret_cast<const float4*>(p)[i];
+      v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+    }
+  } else if constexpr (N == 2) {
+    const float2 a = *reinterpret_cast<const float2*>(p);
+    v[0] = a.x; v[1] = a.y;
+  } else {
+    v[0] = p[0];
+  }
+}
+template <int N>
+__device__ __forceinline__ void store_vec(__nv_bfloat16* p, const float* v) {
+  if constexpr (N >= 8) {
+#pragma unroll
+    for (int i = 0; i < N / 8; ++i) store8(p + 8 * i, v + 8 * i);
+  } else if constexpr (N == 4) {
+    uint2 x;
+    *reinterpret_cast<__nv_bfloat162*>(&x.x) = __floats2bfloat162_rn(v[0], v[1]);
+    *reinterpret_cast<__nv_bfloat162*>(&x.y) = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(p) = x;
+  } else if constexpr (N == 2) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v[0], v[1]);
+  } else {
+    p[0] = __float2bfloat16_rn(v[0]);
+  }
+}
+template <int N>
+__device__ __forceinline__ void store_vec(float* p, const float* v) {
+  if constexpr (N >= 4) {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i)
+      reinterpret_cast<float4*>(p)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else if constexpr (N == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  } else {
+    p[0] = v[0];
+  }
+}
+
+constexpr int ULH_ROWS = 64;   // slot rows of one beam per CTA
+
 // _update_live_nodes hidden layer (paged_model.py:223-238), per slot row:
 //   logits_k = q . key[b,k] / sqrt(W) (masked -1e4), attn = softmax_k,
 //   affinity = sigmoid(max_k logits),
 //   h = GELU(xa + sum_k attn_k * vw[b,k] + c[b])
 // with q = states W_query^T, xa = states W1[:, :W]^T (one GEMM, qxa row =
 // [q | xa]), vw[b,k] = (bound W_value^T) W1[:, W:2W]^T, c[b] = ctx W1[:, 2W:]^T + b1.
+// A CTA takes up to 64 slot rows of one beam (grid = row blocks x beams) and
+// stages that beam's keys, vw and c in shared memory (fp32) once; a warp
+// handles a row, each lane a contiguous chunk of VPLQ (q) and VPLH (xa, h)
+// elements read and written with vector accesses.
 template <typename T, int VPLQ, int VPLH>
 __global__ void __launch_bounds__(ROW_WARPS * 32) update_live_hidden_kernel(
     const T* qxa, int64_t qxa_stride, const T* keys, const T* vw, const T* cvec,
-    const uint8_t* source_mask, int pattern, int64_t rows, int slots, int width, T* hidden,
+    const uint8_t* source_mask, int pattern, int slots, int width, T* hidden,
     int64_t hidden_stride, float* affinity) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int64_t b = row / slots;
-  const T* q = qxa + row * qxa_stride;
-  float qv[VPLQ];
-#pragma unroll
-  for (int j = 0; j < VPLQ; ++j) {
-    const int i = lane + 32 * j;
-    qv[j] = i < width ? to_float(q[i]) : 0.f;
-  }
-  float logit[8];
-  const float scale = rsqrtf((float)width);
-  float mx = -INFINITY;
-  for (int k = 0; k < pattern; ++k) {
-    const T* kr = keys + (b * pattern + k) * width;
-    float d = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPLQ; ++j) {
-      const int i = lane + 32 * j;
-      if (i < width) d += qv[j] * to_float(kr[i]);
-    }
-    d = warp_sum(d) * scale;
-    if (!source_mask[b * pattern + k]) d = -1e4f;
-    logit[k] = d;
-    mx = fmaxf(mx, d);
-  }
-  float den = 0.f;
-  for (int k = 0; k < pattern; ++k) { logit[k] = __expf(logit[k] - mx); den += logit[k]; }
-  const float inv = 1.f / den;
-  if (lane == 0) affinity[row] = 1.f / (1.f + __expf(-mx));
-  const T* xa = q + width;
+  extern __shared__ __align__(16) float ulh_smem[];
   const int hw = 2 * width;
-  T* h = hidden + row * hidden_stride;
+  float* ks = ulh_smem;                          // [pattern][width]
+  float* vs = ks + pattern * width;              // [pattern][2W]
+  float* cs = vs + pattern * hw;                 // [2W]
+  __shared__ bool s_mask[8];
+  const int64_t b = blockIdx.y;
+  for (int i = threadIdx.x; i < pattern * width; i += blockDim.x)
+    ks[i] = to_float(keys[b * pattern * width + i]);
+  for (int i = threadIdx.x; i < pattern * hw; i += blockDim.x)
+    vs[i] = to_float(vw[b * pattern * hw + i]);
+  for (int i = threadIdx.x; i < hw; i += blockDim.x) cs[i] = to_float(cvec[b * hw + i]);
+  if (threadIdx.x < pattern) s_mask[threadIdx.x] = source_mask[b * pattern + threadIdx.x] != 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int q0 = lane * VPLQ, h0 = lane * VPLH;
+  const bool q_on = q0 < width, h_on = h0 < hw;
+  const float scale = rsqrtf((float)width);
+  const int end = min(slots, (blockIdx.x + 1) * ULH_ROWS);
+  for (int s = blockIdx.x * ULH_ROWS + warp; s < end; s += ROW_WARPS) {
+    const int64_t row = b * slots + s;
+    const T* q = qxa + row * qxa_stride;
+    float qv[VPLQ], xv[VPLH];
+    if (q_on) load_vec<VPLQ>(q + q0, qv);
+    else
 #pragma unroll
-  for (int j = 0; j < VPLH; ++j) {
-    const int i = lane + 32 * j;
-    if (i < hw) {
-      float v = to_float(xa[i]) + to_float(cvec[b * hw + i]);
-      for (int k = 0; k < pattern; ++k) v += logit[k] * inv * to_float(vw[(b * pattern + k) * hw + i]);
-      h[i] = from_float<T>(gelu_exact(v));
+      for (int j = 0; j < VPLQ; ++j) qv[j] = 0.f;
+    if (h_on) load_vec<VPLH>(q + width + h0, xv);
+    float logit[8];
+    float mx = -INFINITY;
+    for (int k = 0; k < pattern; ++k) {
+      float d = 0.f;
+      if (q_on) {
+        float kv[VPLQ];
+        load_vec<VPLQ>(ks + k * width + q0, kv);
+#pragma unroll
+        for (int j = 0; j < VPLQ; ++j) d += qv[j] * kv[j];
+      }
+      d = warp_sum(d) * scale;
+      if (!s_mask[k]) d = -1e4f;
+      logit[k] = d;
+      mx = fmaxf(mx, d);
+    }
+    float den = 0.f;
+    for (int k = 0; k < pattern; ++k) { logit[k] = __expf(logit[k] - mx); den += logit[k]; }
+    const float inv = 1.f / den;
+    if (lane == 0) affinity[row] = 1.f / (1.f + __expf(-mx));
+    if (h_on) {
+      float acc[VPLH];
+      load_vec<VPLH>(cs + h0, acc);
+#pragma unroll
+      for (int j = 0; j < VPLH; ++j) acc[j] += xv[j];
+      for (int k = 0; k < pattern; ++k) {
+        float vv[VPLH];
+        load_vec<VPLH>(vs + k * hw + h0, vv);
+        const float w = logit[k] * inv;
+#pragma unroll
+        for (int j = 0; j < VPLH; ++j) acc[j] += w * vv[j];
+      }
+#pragma unroll
+      for (int j = 0; j < VPLH; ++j) acc[j] = gelu_exact(acc[j]);
+      store_vec<VPLH>(hidden + row * hidden_stride + h0, acc);
     }
   }
 }
@@ -559,16 +651,27 @@ extern "C" int grs_update_live_hidden(int dtype, const void* qxa, int64_t qxa_st
                                       int slots, int width, void* hidden, int64_t hidden_stride,
                                       float* affinity, void* stream) {
   if (rows <= 0) return GRS_OK;
-  if (pattern <= 0 || pattern > 8 || slots <= 0) return GRS_ERR_SHAPE;
-  const int grid = ceil_div(rows, ROW_WARPS);
+  if (pattern <= 0 || pattern > 8 || slots <= 0 || rows % slots) return GRS_ERR_SHAPE;
   const int vq = vpl_for(width), vh = vpl_for(2 * width);
-  if (vq < 0 || vh < 0) return GRS_ERR_SHAPE;
+  if (vq < 0 || vh < 0 || width % vq || (2 * width) % vh) return GRS_ERR_SHAPE;
+  // vector accesses: every row start aligned to the per-lane chunk (<= 16 B)
+  const int esize = dtype == GRS_DTYPE_F32 ? 4 : 2;
+  const int64_t aq = std::min(16, vq * esize), ah = std::min(16, vh * esize);
+  if (((uintptr_t)qxa % aq) || ((qxa_stride * esize) % aq) || ((width * esize) % ah) ||
+      ((uintptr_t)hidden % ah) || ((hidden_stride * esize) % ah))
+    return GRS_ERR_SHAPE;
+  const size_t smem = (size_t)(3 * pattern + 2) * width * sizeof(float);
+  if (smem > 160 * 1024) return GRS_ERR_SHAPE;
+  const dim3 grid(ceil_div(slots, ULH_ROWS), (unsigned)(rows / slots));
 #define GRS_ULH(VQ, VH)                                                                        \
   if (vq == VQ && vh == VH) {                                                                  \
-    GRS_DTYPE_SWITCH(T, dtype, update_live_hidden_kernel<T, VQ, VH><<<grid, ROW_WARPS * 32, 0, grs::counted(\
-                                                                     (cudaStream_t)stream)>>>(  \
+    GRS_DTYPE_SWITCH(T, dtype,                                                                 \
+        if (smem > 48 * 1024) cudaFuncSetAttribute(update_live_hidden_kernel<T, VQ, VH>,      \
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);     \
+        update_live_hidden_kernel<T, VQ, VH><<<grid, ROW_WARPS * 32, smem,                     \
+                                               grs::counted((cudaStream_t)stream)>>>(          \
         (const T*)qxa, qxa_stride, (const T*)keys, (const T*)vw, (const T*)cvec, source_mask,  \
-        pattern, rows, slots, width, (T*)hidden, hidden_stride, affinity))                      \
+        pattern, slots, width, (T*)hidden, hidden_stride, affinity))                            \
     GRS_CUDA_CHECK_LAUNCH();                                                                   \
     return GRS_OK;                                                                             \
   }

@@ -222,7 +222,8 @@ class PagedKVCache:
         offset = 0
         for arena in self._arenas():
             width = arena.shape[1] * arena.element_size()
-            arena.index_copy_(0, idx, data[:, offset:offset + width].contiguous().view(arena.dtype))
+            rows = data[:, offset:offset + width].flatten().clone()   # aligned fresh copy
+            arena.index_copy_(0, idx, rows.view(arena.dtype).view(n, -1))
             offset += width
         return pages
 

@@ -299,12 +299,14 @@ class ShardedBeamSearch(DeviceBeamSearch):
         recv_fields, offset = [], 0
         for f, w in zip(fields, widths):
             if n_in:
-                part = recv[:, offset:offset + w].contiguous()
+                # a fresh, aligned copy: field offsets inside a row are not
+                # multiples of the field's element size
+                part = recv[:, offset:offset + w].flatten().clone()
                 recv_fields.append(part.view(f.dtype).view(n_in, *f.shape[1:]))
             else:
                 recv_fields.append(torch.empty(0, *f.shape[1:], device=dev, dtype=f.dtype))
             offset += w
-        recv_pages = (recv[:, offset:].contiguous().view(-1, page_bytes) if n_in else
+        recv_pages = (recv[:, offset:].flatten().clone().view(-1, page_bytes) if n_in else
                       torch.empty(0, page_bytes, device=dev, dtype=torch.uint8))
         new_pages = self.cache.import_pages(recv_pages).view(recv.shape[0], cols)
         table_in = torch.zeros(recv.shape[0], self.block_table.shape[1], device=dev,
