@@ -309,30 +309,14 @@ class DeviceBeamSearch:
         b, s, depth = self.beams, self.slots, self.depth
         topo, ranked, cand, fp = self.topo, prop.ranked, prop.cand, prop.fp
         cb = cand["bindings"]
-        stream = K.stream()
+        i64 = dict(device=dev, dtype=torch.int64)
         # 5. child topology
         self._mark("materialize")
         nxt = self.topology[1 - self.current].state(accepted, s_new)
-        i64 = dict(device=dev, dtype=torch.int64)
-        a_parent, a_xfer, a_source = (torch.empty(accepted, **i64) for _ in range(3))
-        a_src = torch.empty(accepted, self.max_src, **i64)
-        a_dst = torch.empty(accepted, max(self.max_dst, 1), **i64)
-        a_dst_types = torch.empty_like(a_dst)
-        _lib.check(_lib.lib().grs_topology_materialize(
-            accepted, child_proposal.data_ptr(), summary.data_ptr(), ranked.rows.data_ptr(),
-            ranked.xfer_ids.data_ptr(), ranked.next_gate.data_ptr(), fp.data_ptr(),
-            cand["batch_ids"].data_ptr(), cand["anchors"].data_ptr(), cb.data_ptr(), cb.shape[1],
-            self.table.data_ptr(), self.xfer_to_source.data_ptr(), s, s_new,
-            topo.types.data_ptr(), topo.out_node.data_ptr(), topo.out_port.data_ptr(),
-            topo.in_node.data_ptr(), topo.in_port.data_ptr(), topo.touched.data_ptr(),
-            topo.preferred.data_ptr(), topo.next_slot.data_ptr(), topo.streak.data_ptr(),
-            nxt.types.data_ptr(), nxt.out_node.data_ptr(), nxt.out_port.data_ptr(),
-            nxt.in_node.data_ptr(), nxt.in_port.data_ptr(), nxt.touched.data_ptr(),
-            nxt.preferred.data_ptr(), nxt.distance.data_ptr(), nxt.next_slot.data_ptr(),
-            nxt.streak.data_ptr(), nxt.gate.data_ptr(), nxt.fingerprint.data_ptr(),
-            a_parent.data_ptr(), a_xfer.data_ptr(), a_source.data_ptr(), a_src.data_ptr(),
-            a_src.shape[1], a_dst.data_ptr(), a_dst_types.data_ptr(), a_dst.shape[1], depth,
-            self.status.data_ptr(), stream), "topology_materialize")
+        acts = self._materialize(accepted, child_proposal, summary, ranked.rows, ranked.xfer_ids,
+                                 ranked.next_gate, fp, cand["batch_ids"], cand["anchors"], cb,
+                                 topo, s, nxt, s_new)
+        a_parent, a_xfer, a_source, a_src, a_dst, a_dst_types = acts
         self._check_range("materialize", "parent", a_parent, 0, b)
         self._check_range("materialize", "source slot", a_src, 0, s, allow_negative_one=True)
         self._check_range("materialize", "destination slot", a_dst, 0, s_new,
@@ -369,6 +353,37 @@ class DeviceBeamSearch:
         self.topo, self.current = nxt, 1 - self.current
         self.last_actions = (a_parent, a_xfer, a_src)
         self.beams, self.slots, self.depth = accepted, s_new, depth + 1
+
+    def _materialize(self, n: int, child_proposal, summary, rows, xfers, next_gate, fp,
+                     cand_batch, cand_anchor, cand_bindings, parent, slots: int, nxt,
+                     s_new: int):
+        """Child topology rows for `n` children (indices into a ranked list
+        whose candidates point into the given parent topology) written into
+        the rows of `nxt`; returns the per-child action arrays
+        (parent, xfer, source, source slots, destination slots, types)."""
+        i64 = dict(device=self.device, dtype=torch.int64)
+        a_parent, a_xfer, a_source = (torch.empty(n, **i64) for _ in range(3))
+        a_src = torch.empty(n, self.max_src, **i64)
+        a_dst = torch.empty(n, max(self.max_dst, 1), **i64)
+        a_dst_types = torch.empty_like(a_dst)
+        if n == 0:
+            return a_parent, a_xfer, a_source, a_src, a_dst, a_dst_types
+        _lib.check(_lib.lib().grs_topology_materialize(
+            n, child_proposal.data_ptr(), summary.data_ptr(), rows.data_ptr(),
+            xfers.data_ptr(), next_gate.data_ptr(), fp.data_ptr(), cand_batch.data_ptr(),
+            cand_anchor.data_ptr(), cand_bindings.data_ptr(), cand_bindings.shape[1],
+            self.table.data_ptr(), self.xfer_to_source.data_ptr(), slots, s_new,
+            parent.types.data_ptr(), parent.out_node.data_ptr(), parent.out_port.data_ptr(),
+            parent.in_node.data_ptr(), parent.in_port.data_ptr(), parent.touched.data_ptr(),
+            parent.preferred.data_ptr(), parent.next_slot.data_ptr(), parent.streak.data_ptr(),
+            nxt.types.data_ptr(), nxt.out_node.data_ptr(), nxt.out_port.data_ptr(),
+            nxt.in_node.data_ptr(), nxt.in_port.data_ptr(), nxt.touched.data_ptr(),
+            nxt.preferred.data_ptr(), nxt.distance.data_ptr(), nxt.next_slot.data_ptr(),
+            nxt.streak.data_ptr(), nxt.gate.data_ptr(), nxt.fingerprint.data_ptr(),
+            a_parent.data_ptr(), a_xfer.data_ptr(), a_source.data_ptr(), a_src.data_ptr(),
+            a_src.shape[1], a_dst.data_ptr(), a_dst_types.data_ptr(), a_dst.shape[1], self.depth,
+            self.status.data_ptr(), K.stream()), "topology_materialize")
+        return a_parent, a_xfer, a_source, a_src, a_dst, a_dst_types
 
     def check(self) -> None:
         code = int(self.status.item())

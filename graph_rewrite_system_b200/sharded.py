@@ -20,10 +20,12 @@ cache, model state and port graph, and a level runs as:
    global beam order of the next level - equal the single-GPU search on the
    same records;
 4. children stay on their parent's rank up to an even share of the new
-   beam; the overflow moves (deterministically, lowest rank with room first)
-   with one all-to-all of packed rows: model state, topology and the
-   contents of the child's cache pages, which the receiver copies into pages
-   it allocates from its own free list.
+   beam; for the overflow (placed deterministically, lowest rank with room
+   first) the child's proposal and its parent's row - model state,
+   topology, length and the contents of its cache pages, which the receiver
+   copies into pages it allocates from its own free list - move with one
+   all-to-all before the children are built, so every rank materialises and
+   advances exactly its share of the new beam.
 
 No kernel reads another GPU's memory; NCCL moves all data.
 """
@@ -101,25 +103,21 @@ def placement(src: torch.Tensor, world: int):
 
 
 # ---- packed beam rows ------------------------------------------------------
-def _row_fields(states, live, types, topo: TopologyState, lengths):
-    """The per-beam tensors that travel with a beam (first dim = beams)."""
-    return [states, live, types, topo.types, topo.out_node, topo.out_port, topo.in_node,
-            topo.in_port, topo.touched, topo.preferred, topo.distance, topo.next_slot,
-            topo.streak, topo.gate, topo.fingerprint, lengths]
-
-
 def _as_bytes(t: torch.Tensor) -> torch.Tensor:
     n = t.shape[0]
     return t.contiguous().view(n, -1).view(torch.uint8) if t.numel() else torch.empty(
         n, 0, dtype=torch.uint8, device=t.device)
 
 
-def pack_rows(fields: list[torch.Tensor], rows: torch.Tensor) -> torch.Tensor:
-    return torch.cat([_as_bytes(f.index_select(0, rows)) for f in fields], dim=1)
-
-
 def row_bytes(fields: list[torch.Tensor]) -> list[int]:
     return [math.prod(f.shape[1:]) * f.element_size() for f in fields]
+
+
+def _rows(state: TopologyState, lo: int, hi: int) -> TopologyState:
+    """Rows lo..hi of a topology view (views of the same storage)."""
+    return TopologyState(*(getattr(state, f)[lo:hi] for f in (
+        "types", "out_node", "out_port", "in_node", "in_port", "touched", "preferred",
+        "distance", "next_slot", "streak", "gate", "fingerprint")))
 
 
 class ShardedBeamSearch(DeviceBeamSearch):
@@ -234,103 +232,197 @@ class ShardedBeamSearch(DeviceBeamSearch):
         plan = torch.cat((pairs.flatten(), chosen[:, CHILD_NEXT].max().reshape(1))).cpu().tolist()
         pairs_host = [plan[r * self.world:(r + 1) * self.world] for r in range(self.world)]
         s_new = max(s, _round_up(int(plan[-1]), 8))
-        mine = torch.nonzero(src == self.rank).flatten()          # ascending global order
-        n_local = sum(pairs_host[self.rank])
-        if n_local:
-            local_summary = torch.zeros(6, **i64)
-            local_summary[0] = n_local
-            self._children(prop, local_index[mine].contiguous(), local_summary, n_local, s_new)
-        else:
-            if self.beams:
-                self.cache.release_device(self.block_table, self.lengths)
-            self._empty_beams(s_new)
-            self.slots, self.depth = s_new, depth + 1
-            self.block_table = torch.zeros(0, -(-(depth + 1) // cfg.page_size), device=dev,
-                                           dtype=torch.int32)
+        me = self.rank
+        mine = torch.nonzero(src == me).flatten()                 # ascending global order
+        stay = dest[mine] == me
+        keep_j = mine[stay]
+        leave = torch.nonzero(~stay).flatten()
+        leave = leave[torch.sort(dest[mine[leave]], stable=True).indices]   # by destination
+        out_j = mine[leave]
+        in_j = torch.nonzero((dest == me) & (src != me)).flatten()
+        in_j = in_j[torch.sort(src[in_j], stable=True).indices]   # by source, as received
+        # 5a. children that change GPU: their proposal and their parent travel
         self._mark("rebalance")
-        self._rebalance(src, mine, dest, pairs_host, accepted)
+        moved = self._exchange_parents(prop, local_index[out_j], pairs_host)
+        # 5b-6. every GPU materialises and advances exactly its share
+        self._children_sharded(prop, local_index[keep_j], moved, s_new)
+        self._reorder(torch.cat((keep_j, in_j)))
         self.global_count = accepted
         row.logical_cache_pages = accepted * self.block_table.shape[1]
         self._mark("end")
         self.rows.append(row)
         return row
 
-    def _rebalance(self, src: torch.Tensor, mine: torch.Tensor, dest: torch.Tensor,
-                   pairs: list[list[int]], accepted: int) -> None:
-        """Move the children this rank holds but does not keep, receive the
-        ones it gains, and order the result by global child index."""
+    # ---- moving children between GPUs ------------------------------------------
+    def _move_fields(self, prop, ranked_index: torch.Tensor):
+        """What a child that changes GPU carries: its proposal (xfer, next
+        gate, fingerprint, anchor, bindings) and its parent's beam row
+        (model state, topology, length); empty rows of the right shapes when
+        nothing leaves."""
+        dev, m = self.device, self.model
+        i64 = dict(device=dev, dtype=torch.int64)
+        n = 0 if prop is None else ranked_index.numel()
+        t = self.topo
+        parent = [self.states, self.live, self.types, t.types, t.out_node, t.out_port, t.in_node,
+                  t.in_port, t.touched, t.preferred, t.next_slot, t.streak, self.lengths]
+        if n == 0:
+            proposal = [torch.empty(0, **i64) for _ in range(4)] + [
+                torch.empty(0, m.max_pattern, **i64)]
+            parent = [torch.empty(0, *f.shape[1:], device=dev, dtype=f.dtype) for f in parent]
+            return proposal + parent, None
+        rows = prop.ranked.rows[ranked_index]
+        proposal = [prop.ranked.xfer_ids[ranked_index], prop.ranked.next_gate[ranked_index],
+                    prop.fp[ranked_index], prop.cand["anchors"][rows], prop.cand["bindings"][rows]]
+        parent_rows = prop.cand["batch_ids"][rows]
+        return proposal + [f.index_select(0, parent_rows) for f in parent], parent_rows
+
+    def _exchange_parents(self, prop, ranked_index: torch.Tensor, pairs) -> dict:
+        """Send the children leaving this GPU (proposal + parent row + the
+        parent's cache pages) and receive the ones arriving; the received
+        pages are copied into pages of this cache."""
         dev, world, me = self.device, self.world, self.rank
-        s_new, cols = self.slots, self.block_table.shape[1]
-        my_dest = dest[mine]
-        fields = _row_fields(self.states, self.live, self.types, self.topo, self.lengths)
+        fields, parent_rows = self._move_fields(prop, ranked_index)
         widths = row_bytes(fields)
+        cols = -(-self.depth // self.cfg.page_size)               # parent pages in use
         page_bytes = self.cache.page_bytes
         row_size = sum(widths) + cols * page_bytes
-        # outgoing rows in (destination, global index) order
-        out_mask = my_dest != me
-        out_rows = torch.nonzero(out_mask).flatten()
-        out_rows = out_rows[torch.sort(my_dest[out_rows], stable=True).indices]
         send_counts = [pairs[me][d] if d != me else 0 for d in range(world)]
-        recv_counts = [pairs[s][me] if s != me else 0 for s in range(world)]
-        send = torch.empty(0, row_size, device=dev, dtype=torch.uint8)
-        if out_rows.numel():
-            pages = self.block_table.index_select(0, out_rows)[:, :cols].flatten()
-            page_data = self.cache.export_pages(pages).view(out_rows.numel(), -1)
-            send = torch.cat((pack_rows(fields, out_rows), page_data), dim=1)
-        recv = torch.empty(sum(recv_counts), row_size, device=dev, dtype=torch.uint8)
+        recv_counts = [pairs[r][me] if r != me else 0 for r in range(world)]
+        if parent_rows is not None:
+            parts = [_as_bytes(f) for f in fields]
+            if cols:
+                pages = self.block_table.index_select(0, parent_rows)[:, :cols].flatten()
+                parts.append(self.cache.export_pages(pages).view(parent_rows.numel(), -1))
+            send = torch.cat(parts, dim=1)
+        else:
+            send = torch.empty(0, row_size, device=dev, dtype=torch.uint8)
+        n_in = sum(recv_counts)
+        recv = torch.empty(n_in, row_size, device=dev, dtype=torch.uint8)
         if world > 1:                              # collective: every rank, every level
             dist.all_to_all_single(recv.view(-1), send.contiguous().view(-1),
                                    [c * row_size for c in recv_counts],
                                    [c * row_size for c in send_counts], group=self.group)
-        if out_rows.numel():
-            self.cache.release_device(self.block_table.index_select(0, out_rows),
-                                      self.lengths.index_select(0, out_rows))
-        # global indices of what this rank holds next: kept rows + received rows
-        keep_rows = torch.nonzero(~out_mask).flatten()
-        keep_global = mine[keep_rows]
-        # received children: by source rank, then global index (the senders'
-        # packing order)
-        incoming = torch.nonzero((dest == me) & (src != me)).flatten()
-        incoming = incoming[torch.sort(src[incoming], stable=True).indices]
-        n_final = keep_rows.numel() + incoming.numel()
-        order = torch.sort(torch.cat((keep_global, incoming))).indices
-        # unpack received rows
-        n_in = recv.shape[0]
-        recv_fields, offset = [], 0
+        out, offset = [], 0
         for f, w in zip(fields, widths):
             if n_in:
                 # a fresh, aligned copy: field offsets inside a row are not
                 # multiples of the field's element size
                 part = recv[:, offset:offset + w].flatten().clone()
-                recv_fields.append(part.view(f.dtype).view(n_in, *f.shape[1:]))
+                out.append(part.view(f.dtype).view(n_in, *f.shape[1:]))
             else:
-                recv_fields.append(torch.empty(0, *f.shape[1:], device=dev, dtype=f.dtype))
+                out.append(torch.empty(0, *f.shape[1:], device=dev, dtype=f.dtype))
             offset += w
-        recv_pages = (recv[:, offset:].flatten().clone().view(-1, page_bytes) if n_in else
-                      torch.empty(0, page_bytes, device=dev, dtype=torch.uint8))
-        new_pages = self.cache.import_pages(recv_pages).view(recv.shape[0], cols)
-        table_in = torch.zeros(recv.shape[0], self.block_table.shape[1], device=dev,
-                               dtype=torch.int32)
-        table_in[:, :cols] = new_pages
-        # assemble the next beam in global order
-        merged_fields = [torch.cat((f.index_select(0, keep_rows), r))[order]
-                         for f, r in zip(fields, recv_fields)]
-        table = torch.cat((self.block_table.index_select(0, keep_rows), table_in))[order]
-        nxt = self.topology[1 - self.current].state(n_final, s_new)
-        (states, live, types, t_types, out_node, out_port, in_node, in_port, touched,
-         preferred, distance, next_slot, streak, gate, fingerprint, lengths) = merged_fields
-        for dst, src in ((nxt.types, t_types), (nxt.out_node, out_node),
-                         (nxt.out_port, out_port), (nxt.in_node, in_node),
-                         (nxt.in_port, in_port), (nxt.touched, touched),
-                         (nxt.preferred, preferred), (nxt.distance, distance),
-                         (nxt.next_slot, next_slot), (nxt.streak, streak), (nxt.gate, gate),
-                         (nxt.fingerprint, fingerprint)):
-            dst.copy_(src)
+        table = torch.zeros(n_in, max(1, self.block_table.shape[1]), device=dev,
+                            dtype=torch.int32)
+        if n_in and cols:
+            data = recv[:, offset:].flatten().clone().view(-1, page_bytes)
+            table[:, :cols] = self.cache.import_pages(data).view(n_in, cols)
+        (xfer, next_gate, fp, anchor, bindings, states, live, types, t_types, out_node, out_port,
+         in_node, in_port, touched, preferred, next_slot, streak, lengths) = out
+        parent = TopologyState(t_types, out_node, out_port, in_node, in_port, touched, preferred,
+                               torch.empty_like(touched), next_slot, streak,
+                               torch.empty(n_in, device=dev, dtype=torch.int64),
+                               torch.empty(n_in, device=dev, dtype=torch.int64))
+        return {"n": n_in, "xfer": xfer, "next_gate": next_gate, "fp": fp, "anchor": anchor,
+                "bindings": bindings, "states": states, "live": live, "types": types,
+                "topo": parent, "table": table, "lengths": lengths}
+
+    def _children_sharded(self, prop, keep_index: torch.Tensor, moved: dict, s_new: int) -> None:
+        """Materialise this GPU's children - its own kept ones from the local
+        ranked proposals and parents, then the received ones from their
+        travelling proposals and parents - advance them in one batch, append
+        to the cache and release every parent."""
+        cfg, model, dev = self.cfg, self.model, self.device
+        s, depth = self.slots, self.depth
+        n_keep, n_in = keep_index.numel(), moved["n"]
+        n = n_keep + n_in
+        i64 = dict(device=dev, dtype=torch.int64)
+        self._mark("materialize")
+        nxt = self.topology[1 - self.current].state(n, s_new)
+        acts = []
+        if n_keep:
+            summary = torch.zeros(6, **i64)
+            summary[0] = n_keep
+            acts.append(self._materialize(
+                n_keep, keep_index.contiguous(), summary, prop.ranked.rows, prop.ranked.xfer_ids,
+                prop.ranked.next_gate, prop.fp, prop.cand["batch_ids"], prop.cand["anchors"],
+                prop.cand["bindings"], self.topo, s, _rows(nxt, 0, n_keep), s_new))
+        if n_in:
+            summary = torch.zeros(6, **i64)
+            summary[0] = n_in
+            ident = torch.arange(n_in, **i64)
+            acts.append(self._materialize(
+                n_in, ident, summary, ident, moved["xfer"].contiguous(),
+                moved["next_gate"].contiguous(), moved["fp"].contiguous(), ident,
+                moved["anchor"].contiguous(), moved["bindings"].contiguous(), moved["topo"], s,
+                _rows(nxt, n_keep, n), s_new))
+        if len(acts) == 2:
+            a_parent, a_xfer, a_source, a_src, a_dst, a_dst_types = (
+                torch.cat(parts) for parts in zip(*acts))
+        elif acts:
+            a_parent, a_xfer, a_source, a_src, a_dst, a_dst_types = acts[0]
+        # 6. gather the parents (local, then received), advance, append, release
+        self._mark("advance")
+        w = model.width
+        child_cols = -(-(depth + 1) // cfg.page_size)
+        if n:
+            cols = self.block_table.shape[1]
+            states_par = torch.empty(n, s_new, w, device=dev, dtype=model.compute_dtype)
+            live_par = torch.empty(n, s_new, device=dev, dtype=torch.bool)
+            types_par = torch.empty(n, s_new, **i64)
+            table_par = torch.empty(n, cols, device=dev, dtype=torch.int32)
+            lengths_par = torch.empty(n, device=dev, dtype=torch.int32)
+            for lo, hi, st, lv, ty, tb, ln in (
+                    (0, n_keep, self.states, self.live, self.types, self.block_table,
+                     self.lengths),
+                    (n_keep, n, moved["states"], moved["live"], moved["types"], moved["table"],
+                     moved["lengths"])):
+                if hi > lo:
+                    idx = a_parent[lo:hi]
+                    K.gather_beams(st, idx, states_par[lo:hi])
+                    K.gather_beams(lv, idx, live_par[lo:hi])
+                    K.gather_beams(ty, idx, types_par[lo:hi], fill_byte=0xFF)
+                    K.gather_beams(tb, idx, table_par[lo:hi])
+                    K.gather_beams(ln, idx, lengths_par[lo:hi])
+            states, live, types, new_k, new_v, action = model.advance_device(
+                states_par, live_par, types_par, a_xfer, a_source, a_src, a_dst, a_dst_types,
+                self.cache.keys, self.cache.values, table_par, lengths_par)
+            rk, rv = model.project_action_readout_kv(action)
+            self._mark("cache_append_release")
+            child_table, child_lengths = self.cache.append_device(
+                table_par, lengths_par, new_k, new_v, action, rk, rv, child_cols=child_cols)
+        else:
+            states = torch.empty(0, s_new, w, device=dev, dtype=model.compute_dtype)
+            live = torch.empty(0, s_new, device=dev, dtype=torch.bool)
+            types = torch.empty(0, s_new, **i64)
+            child_table = torch.zeros(0, child_cols, device=dev, dtype=torch.int32)
+            child_lengths = torch.zeros(0, device=dev, dtype=torch.int32)
+        if self.beams:
+            self.cache.release_device(self.block_table, self.lengths)
+        if n_in:
+            self.cache.release_device(moved["table"], moved["lengths"])
         self.states, self.live, self.types = states, live, types
-        self.block_table, self.lengths = table.contiguous(), lengths.contiguous()
+        self.block_table, self.lengths = child_table, child_lengths
         self.topo, self.current = nxt, 1 - self.current
-        self.global_index = torch.cat((keep_global, incoming))[order]
-        self.beams = n_final
+        self.beams, self.slots, self.depth = n, s_new, depth + 1
+
+    def _reorder(self, global_index: torch.Tensor) -> None:
+        """Put this GPU's children in global order (the order the ranking's
+        ties follow), copying the topology into the spare buffer."""
+        order = torch.sort(global_index).indices
+        self.global_index = global_index[order]
+        n, s = self.beams, self.slots
+        self.states = self.states.index_select(0, order)
+        self.live = self.live.index_select(0, order)
+        self.types = self.types.index_select(0, order)
+        self.block_table = self.block_table.index_select(0, order)
+        self.lengths = self.lengths.index_select(0, order)
+        src = self.topo
+        dst = self.topology[1 - self.current].state(n, s)
+        for name in ("types", "out_node", "out_port", "in_node", "in_port", "touched",
+                     "preferred", "distance", "next_slot", "streak", "gate", "fingerprint"):
+            torch.index_select(getattr(src, name), 0, order, out=getattr(dst, name))
+        self.topo, self.current = dst, 1 - self.current
 
     # ---- results ------------------------------------------------------------
     def global_fingerprints(self) -> list[int]:
