@@ -429,8 +429,9 @@ def run_rollout(args, world, rank, device):
     search, rc = build_rollout(device, beam_size=args.beam, depth=depth, seed=0, world=world,
                                qubits=args.qubits, gates=args.gates)
     stream = torch.cuda.current_stream(device)
-    # one full untimed search first (module load, allocator warm-up)
-    search.run(min(depth, args.warmup + 2))
+    # one full untimed search first (module load; the caching allocator and
+    # NCCL meet every buffer size of the timed levels once)
+    search.run(depth)
     search.reset()
     for _ in range(args.warmup):
         search.step()
@@ -443,6 +444,7 @@ def run_rollout(args, world, rank, device):
     torch.cuda.synchronize(device)
     done = 0
     launches0 = launch_count()
+    moved0 = (getattr(search, "moved_children", 0), getattr(search, "moved_bytes", 0))
     probe = KernelProbe("bias_gelu", bias_gelu_bytes)
     with ClockSampler(device.index) as clocks, probe:
         for i in range(args.steps):
@@ -454,6 +456,8 @@ def run_rollout(args, world, rank, device):
                 break
         torch.cuda.synchronize(device)
     launches = launch_count() - launches0
+    moved = (getattr(search, "moved_children", 0) - moved0[0],
+             getattr(search, "moved_bytes", 0) - moved0[1])
     timer.collect()
     search.timer = None
     barrier(world, device)
@@ -479,6 +483,13 @@ def run_rollout(args, world, rank, device):
     h2d = (len(search.circuit.nodes) * 2 + len(search.circuit.edges) * 4) * 8
     d2h = 11 * 8 + len(summary["gate_count"]) * 8 * 4 // max(1, depth)
     stage_ms = {k: v / done for k, v in sorted(timer.totals.items())}
+    stage_host_ms = {k: v / done for k, v in sorted(timer.host_totals.items())}
+    stage_per_rank = None
+    if world > 1:                           # every rank's device stage times
+        import torch.distributed as dist
+
+        stage_per_rank = [None] * world
+        dist.all_gather_object(stage_per_rank, {k: round(v, 3) for k, v in stage_ms.items()})
     # whole-job throughput: each level advances world x beam beams, i.e.
     # `world * beam / 1000` levels of the B=1000 benchmark
     scale = world * args.beam / 1000
@@ -512,7 +523,10 @@ def run_rollout(args, world, rank, device):
                        "proposals_after_caps", "attempted_actions", "accepted_actions",
                        "invalid_structural_actions", "duplicate_speculative_successors",
                        "allocated_cache_pages", "logical_cache_pages")},
-                   "stage_ms_per_step": stage_ms},
+                   "stage_ms_per_step": stage_ms, "stage_host_ms_per_step": stage_host_ms,
+                   "stage_ms_per_step_by_rank": stage_per_rank,
+                   "children_changing_gpu_per_level": moved[0] / done,
+                   "rebalance_mb_sent_per_level_rank0": moved[1] / done / 1e6},
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -26,6 +26,7 @@ ERRORS = {
     -8: (RuntimeError, "workspace too small"),
     -9: (ValueError, "inputs exceed the library's fixed scratch capacity"),
     -10: (RuntimeError, "an in-kernel wait timed out"),
+    -11: (RuntimeError, "ranked records out of order"),
 }
 
 DTYPE_CODES = {torch.bfloat16: 0, torch.float32: 1}

@@ -11,16 +11,9 @@
 // first valid proposal with that fingerprint in rank order; the first
 // beam_size such proposals are kept and stably sorted by next gate count.
 #include "grs_common.cuh"
+#include "topology_table.cuh"
 
 namespace grs {
-
-// Per-xfer rewrite table (int32), built by the host from the patterns.
-constexpr int TAB_MAXP = 4;          // ops per pattern
-constexpr int TAB_MAXW = 4;          // qubit wires per pattern
-constexpr int TAB_MAXE = 8;          // internal destination edges
-constexpr int TAB_SRC_LEN = 0, TAB_DST_LEN = 1, TAB_DST_TYPES = 2, TAB_NWIRES = 6,
-              TAB_WIRES = 7, TAB_NINT = 7 + TAB_MAXW * 8, TAB_INT = TAB_NINT + 1,
-              TAB_WIDTH = TAB_INT + TAB_MAXE * 4;
 
 constexpr uint64_t EMPTY_KEY = 0ull;
 __device__ __forceinline__ uint64_t table_key(uint64_t fp) { return fp == EMPTY_KEY ? 1ull : fp; }

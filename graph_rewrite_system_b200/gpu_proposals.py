@@ -154,6 +154,11 @@ def build_gpu_proposals(candidates: CandidateTensors, beam: list[BeamState],
     return proposals, {"predicted_actions": int(predicted), "eligible_actions": int(eligible)}, timing
 
 
+# Largest per-parent cap (and per-parent expansion) of the grouped ranking:
+# one parent's expanded actions sit in shared memory (include/grs_b200.h).
+GROUPED_MAX_EXPANSION = 4096
+
+
 def rank_proposals_grouped(sources: torch.Tensor, probabilities: torch.Tensor, k: int,
                            parent_gate_counts: torch.Tensor, rule_index: GpuRuleIndex, *,
                            per_parent_cap: int, global_cap: int,

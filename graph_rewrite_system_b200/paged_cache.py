@@ -100,6 +100,10 @@ class PagedKVCache:
     def allocated_pages(self) -> int:
         return self.capacity - int(self._free_count.item())
 
+    def free_count_tensor(self) -> torch.Tensor:
+        """The device free-page count (int32 [1]) itself, no synchronisation."""
+        return self._free_count
+
     def allocated_pages_tensor(self) -> torch.Tensor:
         """Allocated page count as a device scalar (no synchronisation)."""
         return self.capacity - self._free_count

@@ -31,7 +31,8 @@ import torch
 
 from . import _lib
 from . import kernels as K
-from .gpu_proposals import GpuRuleIndex, RankedProposals, rank_proposals_grouped
+from .gpu_proposals import (GROUPED_MAX_EXPANSION, GpuRuleIndex, RankedProposals,
+                            rank_proposals_device, rank_proposals_grouped)
 from .paged_cache import PagedKVCache
 from .paged_model import PagedActionBindingModel
 from .synthetic import (Circuit, RolloutConfig, RuleMetadata, SELECT_ALL_THRESHOLDS)
@@ -83,22 +84,24 @@ class StageTimer:
     counterpart of the reference's --profile-stages, :268-273)."""
 
     def __init__(self):
-        self.marks: list[tuple[str, torch.cuda.Event]] = []
+        self.marks: list[tuple[str, torch.cuda.Event, float]] = []
         self.totals: dict[str, float] = {}
+        self.host_totals: dict[str, float] = {}     # host time spent issuing each stage
 
     def mark(self, name: str) -> None:
         event = torch.cuda.Event(enable_timing=True)
         event.record()
-        self.marks.append((name, event))
+        self.marks.append((name, event, time.perf_counter()))
 
     def collect(self) -> None:
         """Accumulate the closed intervals (call after a synchronisation)."""
-        for (name, start), (_, end) in zip(self.marks, self.marks[1:]):
+        for (name, start, h0), (_, end, h1) in zip(self.marks, self.marks[1:]):
             self.totals[name] = self.totals.get(name, 0.0) + start.elapsed_time(end)
+            self.host_totals[name] = self.host_totals.get(name, 0.0) + (h1 - h0) * 1e3
         self.marks = self.marks[-1:] if self.marks else []
 
     def reset(self) -> None:
-        self.marks, self.totals = [], {}
+        self.marks, self.totals, self.host_totals = [], {}, {}
 
 
 class DeviceBeamSearch:
@@ -271,12 +274,20 @@ class DeviceBeamSearch:
                           allow_negative_one=True)
         self._check_range("candidates", "binding", cand["bindings"], 0, s, allow_negative_one=True)
         # 3. proposals (effective parent cap of paged_rollout_benchmark.py:963-966)
-        cap = max(cfg.per_parent_cap, math.ceil(cfg.beam_size / max(1, self.global_beams())) * 2)
+        cap = self.parent_cap()
         self._mark("proposals")
         k = cand["sources"].numel() // b
-        ranked = rank_proposals_grouped(cand["sources"], cand["probabilities"], k, topo.gate,
-                                        self.rule_index, per_parent_cap=cap,
-                                        global_cap=cfg.global_cap, status=self.status)
+        if cap <= GROUPED_MAX_EXPANSION:
+            ranked = rank_proposals_grouped(cand["sources"], cand["probabilities"], k, topo.gate,
+                                            self.rule_index, per_parent_cap=cap,
+                                            global_cap=cfg.global_cap, status=self.status)
+        else:
+            # few parents and a wide beam (the first levels): the general
+            # expansion path takes any cap
+            ranked = rank_proposals_device(cand["batch_ids"], cand["sources"],
+                                           cand["probabilities"], topo.gate, self.rule_index,
+                                           per_parent_cap=cap, global_cap=cfg.global_cap,
+                                           status=self.status)
         self._check_range("proposals", "row", ranked.rows, 0, cand["sources"].numel(),
                           allow_negative_one=True)
         self._check_range("proposals", "xfer", ranked.xfer_ids, 0, self.rules.num_xfers,
@@ -299,6 +310,11 @@ class DeviceBeamSearch:
     def global_beams(self) -> int:
         """Beams of the whole search at this level (this GPU's beams here)."""
         return self.beams
+
+    def parent_cap(self) -> int:
+        """The effective per-parent proposal cap of paged_rollout_benchmark.py:963-966."""
+        return max(self.cfg.per_parent_cap,
+                   math.ceil(self.cfg.beam_size / max(1, self.global_beams())) * 2)
 
     def _children(self, prop: "Proposed", child_proposal: torch.Tensor, summary: torch.Tensor,
                   accepted: int, s_new: int) -> None:

@@ -9,19 +9,22 @@ cache, model state and port graph, and a level runs as:
 1. locally: readout, match logits, candidates, per-parent-capped ranking and
    the rewrite plan (child fingerprint and validity) of its own beams
    (``DeviceBeamSearch._propose``);
-2. every rank publishes its ranked records (fixed size, ``global_cap``
-   rows) with one all-gather; the records carry the reference's full ranking
+2. every rank publishes its ranked records with one all-gather, padded to
+   the most a rank can hold (ceil(global beams / world) parents times the
+   per-parent cap, at most ``global_cap``, so nothing the global cap would
+   keep is dropped); the records carry the reference's full ranking
    key - next gate count ascending, probability descending, parent gate count
    ascending, then the position of the proposal in the single-GPU expansion
    order (global parent, xfer, candidate row);
-3. every rank merges the gathered lists identically (two stable sorts on
-   packed keys) and runs the accept loop on the merged list, so the dedup
+3. every rank merges the gathered lists identically (each list arrives
+   sorted; ``grs_shard_merge`` places every record by binary searches in the
+   other lists) and runs the accept loop on the merged list, so the dedup
    sets stay identical and the accepted children - and their order, the
    global beam order of the next level - equal the single-GPU search on the
    same records;
 4. children stay on their parent's rank up to an even share of the new
    beam; for the overflow (placed deterministically, lowest rank with room
-   first) the child's proposal and its parent's row - model state,
+   first, by ``grs_shard_route``) the child's proposal and its parent's row - model state,
    topology, length and the contents of its cache pages, which the receiver
    copies into pages it allocates from its own free list - move with one
    all-to-all before the children are built, so every rank materialises and
@@ -42,64 +45,10 @@ from .rollout import DeviceBeamSearch, StepRow, _round_up
 from .topology import TopologyState
 
 # ---- ranked records --------------------------------------------------------
-# One int64 row per ranked proposal.  KEY1/KEY2 order the records; the rest
-# is the payload the accept loop and the child placement need.
-KEY1, KEY2, VALID, FP, CHILD_NEXT, RANK, INDEX = range(7)
-NUM_FIELDS = 7
-ABSENT = (1 << 63) - 1                      # KEY1 of padding rows: sorts last
-
-# bit budgets of the packed keys
-GATE_BITS, PROB_BITS = 12, 32               # next gate, ~probability bits, parent gate
-PARENT_BITS, XFER_BITS, ROW_BITS = 23, 16, 11
-
-
-def pack_keys(next_gate, prob, parent_gate, global_parent, xfer, candidate_in_parent):
-    """KEY1 = next_gate | ~prob_bits | parent_gate and KEY2 = global_parent |
-    xfer | candidate index within the parent: lexicographic order on (KEY1,
-    KEY2) is the reference ranking order (probabilities are non-negative
-    float32, whose bit patterns order like the values).  Field widths: gate
-    counts < 4096, global parents < 2^23, xfer ids < 65536, candidates per
-    parent < 2048."""
-    bits = prob.to(torch.float32).contiguous().view(torch.int32).to(torch.int64)
-    desc = (0xFFFFFFFF - bits) & 0xFFFFFFFF
-    key1 = (next_gate << (PROB_BITS + GATE_BITS)) | (desc << GATE_BITS) | parent_gate
-    key2 = (global_parent << (XFER_BITS + ROW_BITS)) | (xfer << ROW_BITS) | candidate_in_parent
-    return key1, key2
-
-
-def merge_records(gathered: torch.Tensor, cap: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Rank-order the union of every rank's records and keep the first `cap`.
-    Returns (merged [cap, NUM_FIELDS], count int64 [1]) where count is the
-    number of present (non-padding) records kept."""
-    order = torch.sort(gathered[:, KEY2], stable=True).indices
-    order = order[torch.sort(gathered[order, KEY1], stable=True).indices]
-    merged = gathered[order[:cap]]
-    count = (gathered[:, KEY1] != ABSENT).sum().clamp(max=cap).reshape(1)
-    return merged, count
-
-
-def placement(src: torch.Tensor, world: int):
-    """Where each child (global acceptance order) lives next level.
-
-    Rank r keeps its own children (those whose parent it holds) up to its
-    quota - A // world, plus one for the first A % world ranks - in order;
-    the rest go, in order, to the ranks with room, lowest rank first.
-    Returns (dest [A], pair_counts [world, world]) with pair_counts[s, d] the
-    children moving from rank s to rank d (the diagonal: kept)."""
-    a = src.numel()
-    ranks = torch.arange(world, device=src.device)
-    quota = a // world + (ranks < a % world).long()
-    onehot = torch.nn.functional.one_hot(src, world)
-    position = (onehot.cumsum(0) * onehot).sum(1) - 1           # index among same-source
-    keep = position < quota[src]
-    kept = torch.bincount(src[keep], minlength=world)
-    room = (quota - kept).cumsum(0)
-    over = (~keep).long()
-    slot = over.cumsum(0) - 1
-    dest_over = torch.searchsorted(room, slot, right=True)
-    dest = torch.where(keep, src, dest_over)
-    pairs = torch.bincount(src * world + dest, minlength=world * world).view(world, world)
-    return dest, pairs
+# grs_shard_records packs a GPU's ranked list into int64 records, field-major
+# [KEY1 | KEY2 | FP | AUX] x width followed by REC_METRICS values; the order
+# of (KEY1, KEY2) is the reference ranking order.
+REC_FIELDS, REC_METRICS = 4, 4
 
 
 # ---- packed beam rows ------------------------------------------------------
@@ -130,7 +79,8 @@ class ShardedBeamSearch(DeviceBeamSearch):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.dst_len = self.table.view(-1, _lib.lib().grs_topology_table_width())[:, 1].long()
+        self.moved_children = 0                 # children that changed GPU, all levels
+        self.moved_bytes = 0                    # bytes this GPU sent for them
 
     # ---- state ------------------------------------------------------------------
     def reset(self) -> None:
@@ -157,64 +107,85 @@ class ShardedBeamSearch(DeviceBeamSearch):
 
     # ---- collectives --------------------------------------------------------
     def _all_gather(self, t: torch.Tensor) -> torch.Tensor:
-        out = [torch.empty_like(t) for _ in range(self.world)]
-        dist.all_gather(out, t.contiguous(), group=self.group)
-        return torch.stack(out)
+        out = torch.empty(self.world * t.shape[0], *t.shape[1:], device=t.device, dtype=t.dtype)
+        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        return out.view(self.world, *t.shape)
 
     # ---- one level ----------------------------------------------------------
-    def _records(self, prop) -> torch.Tensor:
-        gcap = self.cfg.global_cap
-        rows = prop.ranked.rows
-        present = torch.arange(gcap, device=self.device) < prop.ranked.count
-        safe = rows.clamp(min=0)
-        parent = prop.cand["batch_ids"][safe]
-        key1, key2 = pack_keys(prop.ranked.next_gate, prop.cand["probabilities"][safe],
-                               self.topo.gate[parent], self.global_index[parent],
-                               prop.ranked.xfer_ids, safe % prop.k)
-        child_next = self.topo.next_slot[parent].long() + self.dst_len[prop.ranked.xfer_ids.clamp(min=0)]
-        rec = torch.stack((key1, key2, prop.valid.long(), prop.fp, child_next,
-                           torch.full_like(key1, self.rank),
-                           torch.arange(gcap, device=self.device)), dim=1)
-        rec[~present, KEY1] = ABSENT
-        return rec
+    def _send_block(self, prop, width: int) -> torch.Tensor:
+        """This GPU's ranked proposals as a record block (padding past the
+        ranked count), followed by its metrics."""
+        dev, lib = self.device, _lib.lib()
+        block = torch.empty(REC_FIELDS * width + REC_METRICS, device=dev, dtype=torch.int64)
+        free_count = self.cache.free_count_tensor()
+        if prop is None:
+            zero = torch.zeros(1, device=dev, dtype=torch.int64)
+            _lib.check(lib.grs_shard_records(
+                width, zero.data_ptr(), None, None, None, None, None, 1, None, None, None, None,
+                None, None, None, free_count.data_ptr(), self.cache.capacity, block.data_ptr(),
+                self.status.data_ptr(), K.stream()), "shard_records")
+            return block
+        r, cand, t = prop.ranked, prop.cand, self.topo
+        _lib.check(lib.grs_shard_records(
+            width, r.count.data_ptr(), r.rows.data_ptr(), r.xfer_ids.data_ptr(),
+            r.next_gate.data_ptr(), cand["probabilities"].data_ptr(),
+            cand["batch_ids"].data_ptr(), prop.k, t.gate.data_ptr(),
+            self.global_index.data_ptr(), t.next_slot.data_ptr(), self.table.data_ptr(),
+            prop.valid.data_ptr(), prop.fp.data_ptr(), r.metrics.data_ptr(),
+            free_count.data_ptr(), self.cache.capacity, block.data_ptr(),
+            self.status.data_ptr(), K.stream()), "shard_records")
+        return block
 
     def _step(self) -> StepRow | None:
-        cfg, dev = self.cfg, self.device
-        gcap, s, depth = cfg.global_cap, self.slots, self.depth
+        cfg, dev, lib = self.cfg, self.device, _lib.lib()
+        s, depth, world, me = self.slots, self.depth, self.world, self.rank
         i64 = dict(device=dev, dtype=torch.int64)
-        prop = None
-        if self.beams:
-            prop = self._propose()
-            rec = self._records(prop)
-            metrics = torch.cat((prop.ranked.count, prop.ranked.metrics,
-                                 self.cache.allocated_pages_tensor().long()))
-        else:
-            rec = torch.zeros(gcap, NUM_FIELDS, **i64)
-            rec[:, KEY1] = ABSENT
-            metrics = torch.cat((torch.zeros(3, **i64), self.cache.allocated_pages_tensor().long()))
+        # 1-2. local proposals; a rank holds at most ceil(global beams / world)
+        # parents with at most parent_cap() proposals each, so blocks of that
+        # many records lose nothing the global cap would keep
+        width = min(cfg.global_cap, -(-self.global_count // world) * self.parent_cap())
+        prop = self._propose() if self.beams else None
+        block = self._send_block(prop, width)
+        # 3. one all-gather of every GPU's block, then the merged ranking
         self._mark("exchange_records")
-        gathered = self._all_gather(rec).view(-1, NUM_FIELDS)
-        metrics = self._all_gather(metrics).sum(0)
-        merged, count = merge_records(gathered, gcap)
+        gathered = self._all_gather(block)
+        cap = min(cfg.global_cap, world * width)
+        count = torch.empty(1, **i64)
+        metrics = torch.empty(REC_METRICS, **i64)
+        valid = torch.empty(cap, device=dev, dtype=torch.uint8)
+        fp, next_gate, src, index, child_next = (torch.empty(cap, **i64) for _ in range(5))
+        _lib.check(lib.grs_shard_merge(
+            gathered.data_ptr(), world, width, block.numel(), cap, count.data_ptr(),
+            metrics.data_ptr(), valid.data_ptr(), fp.data_ptr(), next_gate.data_ptr(),
+            src.data_ptr(), index.data_ptr(), child_next.data_ptr(), self.status.data_ptr(),
+            K.stream()), "shard_merge")
         # 4. the accept loop on the merged list (identical on every rank)
         self._mark("accept")
-        valid = merged[:, VALID].to(torch.uint8)
-        fp = merged[:, FP].contiguous()
-        next_gate = (merged[:, KEY1] >> (PROB_BITS + GATE_BITS)).contiguous()
-        classes = torch.empty(gcap, device=dev, dtype=torch.uint8)
-        child_proposal = torch.empty(cfg.beam_size, **i64)
-        _lib.check(_lib.lib().grs_topology_accept(
-            gcap, count.data_ptr(), valid.data_ptr(), fp.data_ptr(), next_gate.data_ptr(),
+        classes = torch.empty(cap, device=dev, dtype=torch.uint8)
+        child_proposal = torch.zeros(cfg.beam_size, **i64)
+        _lib.check(lib.grs_topology_accept(
+            cap, count.data_ptr(), valid.data_ptr(), fp.data_ptr(), next_gate.data_ptr(),
             cfg.beam_size, self.step_keys.data_ptr(), self.step_first.data_ptr(),
             self.step_capacity, self.seen.data_ptr(), self.seen_capacity, classes.data_ptr(),
             child_proposal.data_ptr(), self.summary.data_ptr(), None, None, None, None, None,
             self.status.data_ptr(), K.stream()), "topology_accept")
+        # where every child lives next level, and this GPU's index lists
+        pairs = torch.empty(world * world, **i64)
+        extent = torch.empty(1, **i64)
+        keep_local, keep_global, out_local, in_global = (
+            torch.empty(cfg.beam_size, **i64) for _ in range(4))
+        _lib.check(lib.grs_shard_route(
+            child_proposal.data_ptr(), self.summary.data_ptr(), src.data_ptr(),
+            index.data_ptr(), child_next.data_ptr(), cap, cfg.beam_size, world, me,
+            pairs.data_ptr(), extent.data_ptr(), keep_local.data_ptr(), keep_global.data_ptr(),
+            out_local.data_ptr(), in_global.data_ptr(), self.status.data_ptr(), K.stream()),
+            "shard_route")
+        # the level's one host read
         self._mark("host_sync")
-        metrics[0] = count[0]                       # proposals kept after the global cap
-        host = torch.cat((self.summary, metrics, self.status.long(),
-                          self.cache.status_tensor().long())).cpu().tolist()
+        host = torch.cat((self.summary, count, metrics[1:], self.status.long(),
+                          self.cache.status_tensor().long(), pairs, extent)).cpu().tolist()
         (accepted, attempted, invalid, dup, _, best, proposals, predicted, eligible_n,
-         allocated, status, cache_status) = host
+         allocated, status, cache_status) = host[:12]
         if status:
             self.status.zero_()
             _lib.check(int(status), "beam search step")
@@ -225,28 +196,19 @@ class ShardedBeamSearch(DeviceBeamSearch):
         if not accepted:
             self.rows.append(row)
             return None
-        # children in global order: where they come from and where they go
-        chosen = merged[child_proposal[:accepted]]
-        src, local_index = chosen[:, RANK], chosen[:, INDEX]
-        dest, pairs = placement(src, self.world)
-        plan = torch.cat((pairs.flatten(), chosen[:, CHILD_NEXT].max().reshape(1))).cpu().tolist()
-        pairs_host = [plan[r * self.world:(r + 1) * self.world] for r in range(self.world)]
-        s_new = max(s, _round_up(int(plan[-1]), 8))
-        me = self.rank
-        mine = torch.nonzero(src == me).flatten()                 # ascending global order
-        stay = dest[mine] == me
-        keep_j = mine[stay]
-        leave = torch.nonzero(~stay).flatten()
-        leave = leave[torch.sort(dest[mine[leave]], stable=True).indices]   # by destination
-        out_j = mine[leave]
-        in_j = torch.nonzero((dest == me) & (src != me)).flatten()
-        in_j = in_j[torch.sort(src[in_j], stable=True).indices]   # by source, as received
+        pairs_host = [host[12 + r * world:12 + (r + 1) * world] for r in range(world)]
+        s_new = max(s, _round_up(int(host[-1]), 8))
+        n_keep = pairs_host[me][me]
+        n_out = sum(pairs_host[me]) - n_keep
+        n_in = sum(pairs_host[r][me] for r in range(world)) - n_keep
         # 5a. children that change GPU: their proposal and their parent travel
         self._mark("rebalance")
-        moved = self._exchange_parents(prop, local_index[out_j], pairs_host)
+        moves = sum(sum(row) for row in pairs_host) - sum(pairs_host[r][r] for r in range(world))
+        self.moved_children += moves
+        moved = self._exchange_parents(prop, out_local[:n_out], pairs_host, moves > 0)
         # 5b-6. every GPU materialises and advances exactly its share
-        self._children_sharded(prop, local_index[keep_j], moved, s_new)
-        self._reorder(torch.cat((keep_j, in_j)))
+        self._children_sharded(prop, keep_local[:n_keep], moved, s_new)
+        self._reorder(torch.cat((keep_global[:n_keep], in_global[:n_in])), n_in)
         self.global_count = accepted
         row.logical_cache_pages = accepted * self.block_table.shape[1]
         self._mark("end")
@@ -276,10 +238,11 @@ class ShardedBeamSearch(DeviceBeamSearch):
         parent_rows = prop.cand["batch_ids"][rows]
         return proposal + [f.index_select(0, parent_rows) for f in parent], parent_rows
 
-    def _exchange_parents(self, prop, ranked_index: torch.Tensor, pairs) -> dict:
+    def _exchange_parents(self, prop, ranked_index: torch.Tensor, pairs, any_moves: bool) -> dict:
         """Send the children leaving this GPU (proposal + parent row + the
         parent's cache pages) and receive the ones arriving; the received
-        pages are copied into pages of this cache."""
+        pages are copied into pages of this cache.  `any_moves` (the same on
+        every rank) skips the collective when no child changes GPU."""
         dev, world, me = self.device, self.world, self.rank
         fields, parent_rows = self._move_fields(prop, ranked_index)
         widths = row_bytes(fields)
@@ -297,8 +260,9 @@ class ShardedBeamSearch(DeviceBeamSearch):
         else:
             send = torch.empty(0, row_size, device=dev, dtype=torch.uint8)
         n_in = sum(recv_counts)
+        self.moved_bytes += sum(send_counts) * row_size
         recv = torch.empty(n_in, row_size, device=dev, dtype=torch.uint8)
-        if world > 1:                              # collective: every rank, every level
+        if world > 1 and any_moves:                # collective: every rank alike
             dist.all_to_all_single(recv.view(-1), send.contiguous().view(-1),
                                    [c * row_size for c in recv_counts],
                                    [c * row_size for c in send_counts], group=self.group)
@@ -406,9 +370,13 @@ class ShardedBeamSearch(DeviceBeamSearch):
         self.topo, self.current = nxt, 1 - self.current
         self.beams, self.slots, self.depth = n, s_new, depth + 1
 
-    def _reorder(self, global_index: torch.Tensor) -> None:
+    def _reorder(self, global_index: torch.Tensor, received: int) -> None:
         """Put this GPU's children in global order (the order the ranking's
-        ties follow), copying the topology into the spare buffer."""
+        ties follow), copying the topology into the spare buffer; the kept
+        children are already in order, so nothing moves when none arrived."""
+        if not received:
+            self.global_index = global_index
+            return
         order = torch.sort(global_index).indices
         self.global_index = global_index[order]
         n, s = self.beams, self.slots

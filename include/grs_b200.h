@@ -34,7 +34,8 @@ typedef enum {
   GRS_ERR_LENGTH = -7,       /* "prefix handle length/block table mismatch" (paged_cache.py:228) */
   GRS_ERR_WORKSPACE = -8,    /* caller workspace too small */
   GRS_ERR_TOO_LARGE = -9,    /* inputs exceed a fixed internal scratch capacity */
-  GRS_ERR_TIMEOUT = -10      /* a bounded in-kernel wait ran out (device status word) */
+  GRS_ERR_TIMEOUT = -10,     /* a bounded in-kernel wait ran out (device status word) */
+  GRS_ERR_ORDER = -11        /* ranked records out of order or inconsistent (sharded search) */
 } grs_status;
 
 enum { GRS_DTYPE_BF16 = 0, GRS_DTYPE_F32 = 1 };
@@ -376,6 +377,51 @@ GRS_API int grs_topology_fingerprint(const int64_t* types, const int32_t* out_no
                                      const int32_t* out_port, const int32_t* in_node,
                                      const int32_t* in_port, int batch, int slots, uint64_t* fp,
                                      void* stream);
+
+/* ---- beam search sharded over the GPUs of a node ---------------------------
+ * The reference ranks a level's proposals globally
+ * (paged_rollout_benchmark.py:967-1005) and accepts in that order
+ * (:1013-1046) on one GPU.  Sharded, every GPU ranks its own beams and packs
+ * the ranked list into records (int64, field-major: KEY1, KEY2, FP, AUX rows
+ * of `width`, then 4 metrics: ranked count, predicted, eligible, allocated
+ * pages).  KEY1 = next_gate << 44 | (0xffffffff - prob_bits) << 12 |
+ * parent_gate, KEY2 = global_parent << 27 | xfer << 11 | candidate row within
+ * the parent, AUX = child next slot | valid << 32; rows past the ranked count
+ * have KEY1 = INT64_MAX.  Lexicographic (KEY1, KEY2) order is the reference
+ * ranking order.  Fields that overflow their bits flag GRS_ERR_TOO_LARGE. */
+GRS_API int grs_shard_records(int64_t width, const int64_t* count, const int64_t* rows,
+                              const int64_t* xfers, const int64_t* next_gate, const float* probs,
+                              const int64_t* cand_batch, int64_t k, const int64_t* gate,
+                              const int64_t* global_index, const int32_t* next_slot,
+                              const int32_t* table, const uint8_t* valid, const int64_t* fp,
+                              const int64_t* ranked_metrics, const int32_t* free_count,
+                              int64_t capacity, int64_t* out, int32_t* status, void* stream);
+/* Merge `world` gathered record blocks (block r at gathered + r * stride, each
+ * sorted) into the first `cap` (<= world * width) records of the global
+ * ranking: valid (uint8), fp, next gate, source GPU, index in its source
+ * list and child next slot per merged position; rows past the merged count
+ * are zero with source = world.  count[0] = min(cap, records present),
+ * metrics[4] = the summed metrics.  An unsorted block flags GRS_ERR_ORDER. */
+GRS_API int grs_shard_merge(const int64_t* gathered, int world, int64_t width, int64_t stride,
+                            int64_t cap, int64_t* count, int64_t* metrics, uint8_t* valid,
+                            int64_t* fp, int64_t* next_gate, int64_t* src, int64_t* index,
+                            int64_t* child_next, int32_t* status, void* stream);
+/* Place the summary[0] accepted children (child_proposal: merged positions,
+ * global order) on GPUs: each GPU keeps its own children up to an even share
+ * (A / world, one more for the first A % world GPUs), the rest go in order to
+ * the GPUs with room, lowest first.  Writes pairs[world * world] (children
+ * moving from GPU s to d; diagonal: kept), extent[0] (largest child next
+ * slot), and for GPU `me`: keep_local / keep_global (its kept children's
+ * source-list index and global child index, global order), out_local (source
+ * indices of its leaving children by destination, global order within) and
+ * in_global (global indices of the children it receives by source GPU,
+ * global order within).  world <= 64, beam_size <= 8192. */
+GRS_API int grs_shard_route(const int64_t* child_proposal, const int64_t* summary,
+                            const int64_t* src, const int64_t* index, const int64_t* child_next,
+                            int64_t cap, int beam_size, int world, int me, int64_t* pairs,
+                            int64_t* extent, int64_t* keep_local, int64_t* keep_global,
+                            int64_t* out_local, int64_t* in_global, int32_t* status,
+                            void* stream);
 
 #ifdef __cplusplus
 }

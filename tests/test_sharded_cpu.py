@@ -36,7 +36,7 @@ def _rule_index(num_sources: int, seed: int):
 
 
 def _local_records(rank, world, parents, k, cap, per_parent_cap, seed):
-    from graph_rewrite_system_b200.sharded import ABSENT, KEY1, NUM_FIELDS, pack_keys
+    from oracle import sharded
 
     sources, probs, gates = _candidates(seed, parents, k, 7)
     index = _rule_index(7, seed)
@@ -48,32 +48,27 @@ def _local_records(rank, world, parents, k, cap, per_parent_cap, seed):
                                    np.zeros((src.size, 1), np.int64), pr, gates[mine], index,
                                    per_parent_cap=per_parent_cap, global_cap=cap)
     n = sel["parent"].size
-    t = lambda a: torch.as_tensor(np.asarray(a, np.int64))
-    key1, key2 = pack_keys(t(sel["next_gate"]), torch.as_tensor(sel["probability"]),
-                           t(gates[mine][sel["parent"]]), t(mine[sel["parent"]]),
-                           t(sel["xfer"]), t(sel["candidate"] % k))
-    rec = torch.zeros(cap, NUM_FIELDS, dtype=torch.int64)
-    rec[:, KEY1] = ABSENT
-    rec[:n, 0], rec[:n, 1] = key1, key2
-    rec[:n, 3] = t(mine[sel["parent"]] * 1000 + sel["xfer"])      # payload: identity
-    rec[:n, 5] = rank
-    rec[:n, 6] = torch.arange(n)
-    return rec
+    identity = mine[sel["parent"]] * 1000 + sel["xfer"]           # payload in the FP field
+    return sharded.pack_records(
+        cap, n, sel["candidate"], sel["xfer"], sel["next_gate"], pr, local_batch, k,
+        gates[mine], mine, np.zeros(len(mine), np.int64), np.zeros(64, np.int64),
+        np.ones(n, np.uint8), identity, [n, rank, 0, 0])
 
 
 def _worker(rank, world, port, args, queue):
     import torch.distributed as dist
 
-    from graph_rewrite_system_b200.sharded import merge_records
+    from oracle import sharded
 
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world)
     try:
-        rec = _local_records(rank, world, *args)
-        out = [torch.empty_like(rec) for _ in range(world)]
-        dist.all_gather(out, rec)
-        merged, count = merge_records(torch.cat(out), args[2])
-        queue.put((rank, merged[: int(count)].tolist()))
+        block = torch.from_numpy(_local_records(rank, world, *args))
+        out = torch.empty(world * block.numel(), dtype=torch.int64)
+        dist.all_gather_into_tensor(out, block)
+        merged, count, metrics = sharded.merge_records(list(out.view(world, -1).numpy()),
+                                                       args[2], args[2])
+        queue.put((rank, merged["fp"][:count].tolist(), metrics.tolist()))
     finally:
         dist.destroy_process_group()
 
@@ -96,11 +91,12 @@ def test_merged_ranking_equals_single_gpu_ranking(parents, k, cap, per_parent_ca
     procs = [ctx.Process(target=_worker, args=(r, world, port, args, queue)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(queue.get(timeout=120) for _ in range(world))
+    results = {r: rest for r, *rest in (queue.get(timeout=120) for _ in range(world))}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
     assert results[0] == results[1]                      # every rank merges identically
+    assert results[0][1][1] == sum(range(world))         # metrics summed over ranks
     # the single-GPU ranking of the union
     sources, probs, gates = _candidates(seed, parents, k, 7)
     index = _rule_index(7, seed)
@@ -109,25 +105,33 @@ def test_merged_ranking_equals_single_gpu_ranking(parents, k, cap, per_parent_ca
                                    np.zeros((parents * k, 1), np.int64), probs.reshape(-1),
                                    gates, index, per_parent_cap=per_parent_cap, global_cap=cap)
     expected = (sel["parent"] * 1000 + sel["xfer"]).tolist()
-    got = [row[3] for row in results[0]]
-    assert got == expected
+    assert results[0][0] == expected
 
 
 @pytest.mark.parametrize("world,sources", [(2, [0, 0, 0, 1, 0, 0]), (4, [0] * 9),
                                            (3, [2, 1, 0, 2, 2, 2, 1, 0]), (2, [1, 0])])
 def test_placement_keeps_quota_and_minimises_moves(world, sources):
-    from graph_rewrite_system_b200.sharded import placement
+    from oracle import sharded
 
-    src = torch.tensor(sources)
-    dest, pairs = placement(src, world)
     a = len(sources)
+    merged = {"src": np.asarray(sources), "index": np.arange(a) + 100,
+              "child_next": np.arange(a) % 5}
     quota = [a // world + (r < a % world) for r in range(world)]
-    assert torch.bincount(dest, minlength=world).tolist() == quota
-    assert pairs.sum().item() == a
+    lists = [sharded.route(np.arange(a), a, merged, world, me) for me in range(world)]
+    pairs = lists[0]["pairs"]
+    assert all((x["pairs"] == pairs).all() for x in lists)
+    assert pairs.sum(0).tolist() == quota                # every rank ends at its share
+    assert pairs.sum(1).tolist() == [sources.count(r) for r in range(world)]
     for r in range(world):
         own = [j for j, s in enumerate(sources) if s == r]
-        kept = [j for j in own if dest[j] == r]
-        assert kept == own[: min(len(own), quota[r])]    # first children stay, in order
-    # a child only moves when its own rank is over quota
-    assert int((dest != src).sum()) == sum(max(0, sources.count(r) - quota[r])
-                                           for r in range(world))
+        assert lists[r]["keep_global"].tolist() == own[: min(len(own), quota[r])]
+        assert lists[r]["keep_local"].tolist() == [100 + j for j in own[: quota[r]]]
+        assert len(lists[r]["out_local"]) == max(0, len(own) - quota[r])
+    # a child only moves when its own rank is over quota, and every moved
+    # child is sent once and received once
+    moves = pairs.sum() - np.trace(pairs)
+    assert moves == sum(max(0, sources.count(r) - quota[r]) for r in range(world))
+    sent = sorted(j - 100 for x in lists for j in x["out_local"])
+    received = sorted(j for x in lists for j in x["in_global"])
+    assert sent == received
+    assert lists[0]["extent"] == max(j % 5 for j in range(a))
