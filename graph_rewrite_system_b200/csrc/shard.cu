@@ -291,6 +291,58 @@ __global__ void __launch_bounds__(ROUTE_THREADS) shard_route_kernel(
   if (tid == 0) *extent = (int64_t)s_extent;
 }
 
+
+// ---- multi-segment row copies ------------------------------------------------
+// A segment copies `units` units of `unit_bytes` per row from src to dst.  Unit
+// k of row i sits at base + index[i * units + k] * unit_stride when the side
+// has an index, else at base + i * row_stride + k * unit_stride.  One launch
+// packs every field of the rows that change GPU into contiguous send rows,
+// unpacks received rows into the field tensors and cache pages, or reorders a
+// beam.
+constexpr int ROWS_MAX_SEGMENTS = 40, ROWS_SEG_WORDS = 10;
+struct RowSegment {
+  const uint8_t* src; int64_t src_row, src_unit; const int64_t* src_index;
+  uint8_t* dst; int64_t dst_row, dst_unit; const int64_t* dst_index;
+  int64_t unit_bytes, units;
+};
+struct RowSegments { RowSegment seg[ROWS_MAX_SEGMENTS]; int n; };
+
+template <typename V>
+__device__ __forceinline__ void copy_unit(const uint8_t* s, uint8_t* d, int64_t bytes) {
+  const V* sv = reinterpret_cast<const V*>(s);
+  V* dv = reinterpret_cast<V*>(d);
+  for (int64_t e = threadIdx.x; e < bytes / (int64_t)sizeof(V); e += blockDim.x) dv[e] = sv[e];
+}
+
+__global__ void __launch_bounds__(256) rows_copy_kernel(RowSegments segs, const int64_t* n_dev,
+                                                        int64_t n_max) {
+  // work items: (segment, row, unit), segment-major
+  __shared__ int64_t start[ROWS_MAX_SEGMENTS + 1];
+  if (threadIdx.x == 0) {
+    const int64_t rows = n_dev ? max((int64_t)0, min(*n_dev, n_max)) : n_max;
+    start[0] = 0;
+    for (int g = 0; g < segs.n; ++g) start[g + 1] = start[g] + rows * segs.seg[g].units;
+  }
+  __syncthreads();
+  const int64_t items = start[segs.n];
+  for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+    int g = 0;
+    while (w >= start[g + 1]) ++g;
+    const RowSegment& sg = segs.seg[g];
+    const int64_t local = w - start[g];
+    const int64_t i = local / sg.units, k = local - i * sg.units;
+    const uint8_t* src = sg.src + (sg.src_index ? sg.src_index[local] * sg.src_unit
+                                                : i * sg.src_row + k * sg.src_unit);
+    uint8_t* dst = sg.dst + (sg.dst_index ? sg.dst_index[local] * sg.dst_unit
+                                          : i * sg.dst_row + k * sg.dst_unit);
+    const uint64_t align = (uint64_t)src | (uint64_t)dst | (uint64_t)sg.unit_bytes;
+    if ((align & 15) == 0) copy_unit<uint4>(src, dst, sg.unit_bytes);
+    else if ((align & 7) == 0) copy_unit<uint2>(src, dst, sg.unit_bytes);
+    else if ((align & 3) == 0) copy_unit<uint32_t>(src, dst, sg.unit_bytes);
+    else copy_unit<uint8_t>(src, dst, sg.unit_bytes);
+  }
+}
+
 }  // namespace grs
 
 using namespace grs;
@@ -352,6 +404,34 @@ extern "C" int grs_shard_route(const int64_t* child_proposal, const int64_t* sum
   shard_route_kernel<<<1, ROUTE_THREADS, smem, counted((cudaStream_t)stream)>>>(
       child_proposal, summary, src, index, child_next, cap, beam_size, world, me, pairs, extent,
       keep_local, keep_global, out_local, in_global, status);
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_rows_copy(int nseg, const int64_t* segments, const int64_t* n_dev,
+                             int64_t n_max, void* stream) {
+  if (nseg < 0 || nseg > ROWS_MAX_SEGMENTS || n_max < 0 || (nseg > 0 && segments == nullptr))
+    return GRS_ERR_SHAPE;
+  RowSegments p{};
+  p.n = nseg;
+  for (int g = 0; g < nseg; ++g) {
+    const int64_t* w = segments + g * ROWS_SEG_WORDS;
+    RowSegment& sg = p.seg[g];
+    sg.src = reinterpret_cast<const uint8_t*>(w[0]);
+    sg.src_row = w[1]; sg.src_unit = w[2];
+    sg.src_index = reinterpret_cast<const int64_t*>(w[3]);
+    sg.dst = reinterpret_cast<uint8_t*>(w[4]);
+    sg.dst_row = w[5]; sg.dst_unit = w[6];
+    sg.dst_index = reinterpret_cast<const int64_t*>(w[7]);
+    sg.unit_bytes = w[8]; sg.units = w[9];
+    if (sg.unit_bytes < 0 || sg.units < 1 || (sg.unit_bytes > 0 && (!sg.src || !sg.dst)))
+      return GRS_ERR_SHAPE;
+  }
+  if (nseg == 0 || n_max == 0) return GRS_OK;
+  int64_t work = 0;
+  for (int g = 0; g < nseg; ++g) work += n_max * p.seg[g].units;
+  const int blocks = (int)(work < 148 * 8 ? work : 148 * 8);
+  rows_copy_kernel<<<blocks, 256, 0, counted((cudaStream_t)stream)>>>(p, n_dev, n_max);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }

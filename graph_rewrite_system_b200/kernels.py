@@ -192,3 +192,23 @@ def structural_decode(types, live, ports, rules, batch_ids, sources, anchors, bi
         pe.data_ptr(), pe.shape[1], bindings.shape[1], batch_ids.data_ptr(), sources.data_ptr(),
         anchors.data_ptr(), sources.numel(), bindings.data_ptr(), valid.data_ptr(),
         int(clear_invalid), stream()), "structural_decode")
+
+
+def rows_copy(segments, n_max: int, n_dev: torch.Tensor | None = None) -> None:
+    """One launch of grs_rows_copy.  Each segment is (src, src_row_stride,
+    src_unit_stride, src_index, dst, dst_row_stride, dst_unit_stride,
+    dst_index, unit_bytes, units); src/dst are tensors (their data pointers
+    are the bases), indexes int64 tensors or None, strides in bytes.  Rows:
+    min(n_dev, n_max) with a device count, else n_max."""
+    import numpy as np
+
+    words = []
+    for (src, sr, su, si, dst, dr, du, di, ub, units) in segments:
+        if ub == 0:
+            continue
+        words.extend((src.data_ptr(), sr, su, 0 if si is None else si.data_ptr(),
+                      dst.data_ptr(), dr, du, 0 if di is None else di.data_ptr(), ub, units))
+    table = np.asarray(words, dtype=np.int64)
+    _lib.check(_lib.lib().grs_rows_copy(
+        len(words) // 10, table.ctypes.data if len(words) else None,
+        _p(n_dev), n_max, stream()), "rows_copy")

@@ -185,7 +185,7 @@ class PagedKVCache:
             self._stream()), "release")
 
     # ---- moving rows between caches (sharded beam search) -------------------
-    def _arenas(self) -> list[torch.Tensor]:
+    def arenas(self) -> list[torch.Tensor]:
         """Every arena as a [capacity, page elements] view (page-major), per
         layer for the K/V arenas."""
         cap = self.capacity
@@ -196,39 +196,18 @@ class PagedKVCache:
 
     @property
     def page_bytes(self) -> int:
-        """Bytes one page holds across all arenas (the export row size)."""
-        return sum(a.shape[1] * a.element_size() for a in self._arenas())
+        """Bytes one page holds across all arenas."""
+        return sum(a.shape[1] * a.element_size() for a in self.arenas())
 
-    def export_pages(self, pages: torch.Tensor) -> torch.Tensor:
-        """Contents of the given pages (device int ids), one uint8 row of
-        ``page_bytes`` each, arenas in a fixed order."""
-        if pages.numel() == 0:
-            return torch.empty(0, self.page_bytes, device=self.device, dtype=torch.uint8)
-        idx = pages.long()
-        return torch.cat([a.index_select(0, idx).view(torch.uint8) for a in self._arenas()],
-                         dim=1)
-
-    def import_pages(self, data: torch.Tensor) -> torch.Tensor:
-        """Allocate ``len(data)`` pages (refcount 1, free-list order) and fill
-        them with rows produced by ``export_pages`` of a cache of the same
-        shape; returns the new page ids (device int32)."""
-        n = data.shape[0]
+    def alloc_pages(self, n: int) -> torch.Tensor:
+        """Allocate n pages (refcount 1, free-list order) for contents copied
+        in from another cache; returns their ids (device int32)."""
         pages = torch.empty(n, device=self.device, dtype=torch.int32)
-        if n == 0:
-            return pages
-        if data.shape[1] != self.page_bytes:
-            raise ValueError("page rows do not match this cache's page layout")
-        _lib.check(_lib.lib().grs_cache_alloc(
-            self._refcounts.data_ptr(), self._free.data_ptr(), self._free_count.data_ptr(),
-            self.capacity, n, pages.data_ptr(), self._status.data_ptr(), self._stream()),
-            "import_pages")
-        idx = pages.long()
-        offset = 0
-        for arena in self._arenas():
-            width = arena.shape[1] * arena.element_size()
-            rows = data[:, offset:offset + width].flatten().clone()   # aligned fresh copy
-            arena.index_copy_(0, idx, rows.view(arena.dtype).view(n, -1))
-            offset += width
+        if n:
+            _lib.check(_lib.lib().grs_cache_alloc(
+                self._refcounts.data_ptr(), self._free.data_ptr(), self._free_count.data_ptr(),
+                self.capacity, n, pages.data_ptr(), self._status.data_ptr(), self._stream()),
+                "alloc_pages")
         return pages
 
     # ---- reference API ----------------------------------------------------

@@ -51,17 +51,7 @@ from .topology import TopologyState
 REC_FIELDS, REC_METRICS = 4, 4
 
 
-# ---- packed beam rows ------------------------------------------------------
-def _as_bytes(t: torch.Tensor) -> torch.Tensor:
-    n = t.shape[0]
-    return t.contiguous().view(n, -1).view(torch.uint8) if t.numel() else torch.empty(
-        n, 0, dtype=torch.uint8, device=t.device)
-
-
-def row_bytes(fields: list[torch.Tensor]) -> list[int]:
-    return [math.prod(f.shape[1:]) * f.element_size() for f in fields]
-
-
+# ---- beam rows -------------------------------------------------------------
 def _rows(state: TopologyState, lo: int, hi: int) -> TopologyState:
     """Rows lo..hi of a topology view (views of the same storage)."""
     return TopologyState(*(getattr(state, f)[lo:hi] for f in (
@@ -172,14 +162,22 @@ class ShardedBeamSearch(DeviceBeamSearch):
         # where every child lives next level, and this GPU's index lists
         pairs = torch.empty(world * world, **i64)
         extent = torch.empty(1, **i64)
-        keep_local, keep_global, out_local, in_global = (
-            torch.empty(cfg.beam_size, **i64) for _ in range(4))
+        keep_local, keep_global, in_global = (torch.empty(cfg.beam_size, **i64)
+                                               for _ in range(3))
+        out_local = torch.zeros(cfg.beam_size, **i64)   # zero tail: safe gather indexes
         _lib.check(lib.grs_shard_route(
             child_proposal.data_ptr(), self.summary.data_ptr(), src.data_ptr(),
             index.data_ptr(), child_next.data_ptr(), cap, cfg.beam_size, world, me,
             pairs.data_ptr(), extent.data_ptr(), keep_local.data_ptr(), keep_global.data_ptr(),
             out_local.data_ptr(), in_global.data_ptr(), self.status.data_ptr(), K.stream()),
             "shard_route")
+        # leaving children's rows packed while the host waits below
+        send = None
+        if world > 1:
+            n_out_dev = pairs.view(world, world)[me].sum(0, keepdim=True) - pairs[
+                me * world + me:me * world + me + 1]
+            max_out = min(cfg.beam_size, width) if prop is not None else 0
+            send = self._pack_outgoing(prop, out_local, n_out_dev, max_out)
         # the level's one host read
         self._mark("host_sync")
         host = torch.cat((self.summary, count, metrics[1:], self.status.long(),
@@ -199,13 +197,12 @@ class ShardedBeamSearch(DeviceBeamSearch):
         pairs_host = [host[12 + r * world:12 + (r + 1) * world] for r in range(world)]
         s_new = max(s, _round_up(int(host[-1]), 8))
         n_keep = pairs_host[me][me]
-        n_out = sum(pairs_host[me]) - n_keep
         n_in = sum(pairs_host[r][me] for r in range(world)) - n_keep
         # 5a. children that change GPU: their proposal and their parent travel
         self._mark("rebalance")
         moves = sum(sum(row) for row in pairs_host) - sum(pairs_host[r][r] for r in range(world))
         self.moved_children += moves
-        moved = self._exchange_parents(prop, out_local[:n_out], pairs_host, moves > 0)
+        moved = self._exchange_parents(send, pairs_host, moves > 0)
         # 5b-6. every GPU materialises and advances exactly its share
         self._children_sharded(prop, keep_local[:n_keep], moved, s_new)
         self._reorder(torch.cat((keep_global[:n_keep], in_global[:n_in])), n_in)
@@ -216,80 +213,112 @@ class ShardedBeamSearch(DeviceBeamSearch):
         return row
 
     # ---- moving children between GPUs ------------------------------------------
-    def _move_fields(self, prop, ranked_index: torch.Tensor):
-        """What a child that changes GPU carries: its proposal (xfer, next
-        gate, fingerprint, anchor, bindings) and its parent's beam row
-        (model state, topology, length); empty rows of the right shapes when
-        nothing leaves."""
-        dev, m = self.device, self.model
-        i64 = dict(device=dev, dtype=torch.int64)
-        n = 0 if prop is None else ranked_index.numel()
-        t = self.topo
-        parent = [self.states, self.live, self.types, t.types, t.out_node, t.out_port, t.in_node,
-                  t.in_port, t.touched, t.preferred, t.next_slot, t.streak, self.lengths]
-        if n == 0:
-            proposal = [torch.empty(0, **i64) for _ in range(4)] + [
-                torch.empty(0, m.max_pattern, **i64)]
-            parent = [torch.empty(0, *f.shape[1:], device=dev, dtype=f.dtype) for f in parent]
-            return proposal + parent, None
-        rows = prop.ranked.rows[ranked_index]
-        proposal = [prop.ranked.xfer_ids[ranked_index], prop.ranked.next_gate[ranked_index],
-                    prop.fp[ranked_index], prop.cand["anchors"][rows], prop.cand["bindings"][rows]]
-        parent_rows = prop.cand["batch_ids"][rows]
-        return proposal + [f.index_select(0, parent_rows) for f in parent], parent_rows
+    PARENT_FIELDS = ("states", "live", "types", "t_types", "out_node", "out_port", "in_node",
+                     "in_port", "touched", "preferred", "next_slot", "streak", "lengths")
+    PROPOSAL_FIELDS = ("xfer", "next_gate", "fp", "anchor", "bindings")
 
-    def _exchange_parents(self, prop, ranked_index: torch.Tensor, pairs, any_moves: bool) -> dict:
-        """Send the children leaving this GPU (proposal + parent row + the
-        parent's cache pages) and receive the ones arriving; the received
-        pages are copied into pages of this cache.  `any_moves` (the same on
-        every rank) skips the collective when no child changes GPU."""
+    def _parent_tensors(self) -> list[torch.Tensor]:
+        t = self.topo
+        return [self.states, self.live, self.types, t.types, t.out_node, t.out_port, t.in_node,
+                t.in_port, t.touched, t.preferred, t.next_slot, t.streak, self.lengths]
+
+    def _row_layout(self):
+        """What a child that changes GPU carries, as one byte row: its
+        proposal (xfer, next gate, fingerprint, anchor, bindings), its
+        parent's beam row (model state, topology, length) and the parent's
+        cache pages in use.  Returns ([(name, dtype, row shape, offset,
+        bytes)], [(arena, offset, page bytes)], pages per row, row bytes);
+        every piece starts 16-byte aligned.  The layout is the same on every
+        GPU (same slot count, depth and cache geometry)."""
+        i64 = torch.int64
+        specs = [(n, i64, ()) for n in self.PROPOSAL_FIELDS[:4]]
+        specs.append(("bindings", i64, (self.model.max_pattern,)))
+        specs += [(n, f.dtype, tuple(f.shape[1:]))
+                  for n, f in zip(self.PARENT_FIELDS, self._parent_tensors())]
+        fields, offset = [], 0
+        for name, dtype, shape in specs:
+            nbytes = math.prod(shape) * torch.empty((), dtype=dtype).element_size()
+            fields.append((name, dtype, shape, offset, nbytes))
+            offset += _round_up(nbytes, 16)
+        cols = -(-self.depth // self.cfg.page_size)                # parent pages in use
+        pages = []
+        for arena in self.cache.arenas():
+            nbytes = arena.shape[1] * arena.element_size()
+            pages.append((arena, offset, nbytes))
+            offset += _round_up(nbytes * cols, 16)
+        return fields, pages, cols, _round_up(offset, 16)
+
+    def _pack_outgoing(self, prop, out_local: torch.Tensor, n_out: torch.Tensor,
+                       max_out: int):
+        """Before the level's host read: copy the rows of this GPU's leaving
+        children (out_local, device count n_out <= max_out) into send rows
+        with one grs_rows_copy launch."""
+        fields, pages, cols, row_size = self._row_layout()
+        send = torch.empty(max_out, row_size, device=self.device, dtype=torch.uint8)
+        if max_out == 0:
+            return send
+        ranked_index = out_local[:max_out]
+        rows = prop.ranked.rows.index_select(0, ranked_index).clamp_(min=0)
+        parent = prop.cand["batch_ids"].index_select(0, rows)
+        sources = [(prop.ranked.xfer_ids, ranked_index), (prop.ranked.next_gate, ranked_index),
+                   (prop.fp, ranked_index), (prop.cand["anchors"], rows),
+                   (prop.cand["bindings"], rows)]
+        sources += [(f, parent) for f in self._parent_tensors()]
+        flat = send.view(-1)
+        segments = []
+        for (src, index), (_, _, _, offset, nbytes) in zip(sources, fields):
+            stride = src.stride(0) * src.element_size()
+            segments.append((src, 0, stride, index, flat[offset:], row_size, 0, None, nbytes, 1))
+        if cols:
+            page_ids = self.block_table.index_select(0, parent)[:, :cols].long().contiguous()
+            for arena, offset, nbytes in pages:
+                segments.append((arena, 0, arena.stride(0) * arena.element_size(), page_ids,
+                                 flat[offset:], row_size, nbytes, None, nbytes, cols))
+        K.rows_copy(segments, max_out, n_out)
+        return send
+
+    def _exchange_parents(self, send: torch.Tensor, pairs, any_moves: bool) -> dict:
+        """Send the packed rows of the children leaving this GPU and unpack
+        the arriving ones: fields into fresh tensors, page contents into
+        pages allocated from this cache.  `any_moves` (the same on every
+        rank) skips the collective when no child changes GPU."""
         dev, world, me = self.device, self.world, self.rank
-        fields, parent_rows = self._move_fields(prop, ranked_index)
-        widths = row_bytes(fields)
-        cols = -(-self.depth // self.cfg.page_size)               # parent pages in use
-        page_bytes = self.cache.page_bytes
-        row_size = sum(widths) + cols * page_bytes
+        fields, pages, cols, row_size = self._row_layout()
         send_counts = [pairs[me][d] if d != me else 0 for d in range(world)]
         recv_counts = [pairs[r][me] if r != me else 0 for r in range(world)]
-        if parent_rows is not None:
-            parts = [_as_bytes(f) for f in fields]
-            if cols:
-                pages = self.block_table.index_select(0, parent_rows)[:, :cols].flatten()
-                parts.append(self.cache.export_pages(pages).view(parent_rows.numel(), -1))
-            send = torch.cat(parts, dim=1)
-        else:
-            send = torch.empty(0, row_size, device=dev, dtype=torch.uint8)
-        n_in = sum(recv_counts)
-        self.moved_bytes += sum(send_counts) * row_size
+        n_out, n_in = sum(send_counts), sum(recv_counts)
+        self.moved_bytes += n_out * row_size
         recv = torch.empty(n_in, row_size, device=dev, dtype=torch.uint8)
+        if send is None:
+            send = torch.empty(0, row_size, device=dev, dtype=torch.uint8)
         if world > 1 and any_moves:                # collective: every rank alike
-            dist.all_to_all_single(recv.view(-1), send.contiguous().view(-1),
+            dist.all_to_all_single(recv.view(-1), send[:n_out].reshape(-1),
                                    [c * row_size for c in recv_counts],
                                    [c * row_size for c in send_counts], group=self.group)
-        out, offset = [], 0
-        for f, w in zip(fields, widths):
-            if n_in:
-                # a fresh, aligned copy: field offsets inside a row are not
-                # multiples of the field's element size
-                part = recv[:, offset:offset + w].flatten().clone()
-                out.append(part.view(f.dtype).view(n_in, *f.shape[1:]))
-            else:
-                out.append(torch.empty(0, *f.shape[1:], device=dev, dtype=f.dtype))
-            offset += w
+        out = {name: torch.empty(n_in, *shape, device=dev, dtype=dtype)
+               for name, dtype, shape, _, _ in fields}
         table = torch.zeros(n_in, max(1, self.block_table.shape[1]), device=dev,
                             dtype=torch.int32)
-        if n_in and cols:
-            data = recv[:, offset:].flatten().clone().view(-1, page_bytes)
-            table[:, :cols] = self.cache.import_pages(data).view(n_in, cols)
-        (xfer, next_gate, fp, anchor, bindings, states, live, types, t_types, out_node, out_port,
-         in_node, in_port, touched, preferred, next_slot, streak, lengths) = out
-        parent = TopologyState(t_types, out_node, out_port, in_node, in_port, touched, preferred,
-                               torch.empty_like(touched), next_slot, streak,
-                               torch.empty(n_in, device=dev, dtype=torch.int64),
+        if n_in:
+            flat = recv.view(-1)
+            segments = [(flat[offset:], row_size, 0, None, out[name], nbytes, 0, None, nbytes, 1)
+                        for name, _, _, offset, nbytes in fields]
+            if cols:
+                page_ids = self.cache.alloc_pages(n_in * cols)
+                table[:, :cols] = page_ids.view(n_in, cols)
+                index = page_ids.long()
+                for arena, offset, nbytes in pages:
+                    segments.append((flat[offset:], row_size, nbytes, None, arena, 0,
+                                     arena.stride(0) * arena.element_size(), index, nbytes,
+                                     cols))
+            K.rows_copy(segments, n_in)
+        parent = TopologyState(out["t_types"], out["out_node"], out["out_port"], out["in_node"],
+                               out["in_port"], out["touched"], out["preferred"],
+                               torch.empty_like(out["touched"]), out["next_slot"],
+                               out["streak"], torch.empty(n_in, device=dev, dtype=torch.int64),
                                torch.empty(n_in, device=dev, dtype=torch.int64))
-        return {"n": n_in, "xfer": xfer, "next_gate": next_gate, "fp": fp, "anchor": anchor,
-                "bindings": bindings, "states": states, "live": live, "types": types,
-                "topo": parent, "table": table, "lengths": lengths}
+        out.update(n=n_in, topo=parent, table=table)
+        return out
 
     def _children_sharded(self, prop, keep_index: torch.Tensor, moved: dict, s_new: int) -> None:
         """Materialise this GPU's children - its own kept ones from the local
@@ -372,24 +401,29 @@ class ShardedBeamSearch(DeviceBeamSearch):
 
     def _reorder(self, global_index: torch.Tensor, received: int) -> None:
         """Put this GPU's children in global order (the order the ranking's
-        ties follow), copying the topology into the spare buffer; the kept
-        children are already in order, so nothing moves when none arrived."""
+        ties follow) with one grs_rows_copy launch, the topology into the
+        spare buffer; the kept children are already in order, so nothing
+        moves when none arrived."""
         if not received:
             self.global_index = global_index
             return
         order = torch.sort(global_index).indices
         self.global_index = global_index[order]
         n, s = self.beams, self.slots
-        self.states = self.states.index_select(0, order)
-        self.live = self.live.index_select(0, order)
-        self.types = self.types.index_select(0, order)
-        self.block_table = self.block_table.index_select(0, order)
-        self.lengths = self.lengths.index_select(0, order)
         src = self.topo
         dst = self.topology[1 - self.current].state(n, s)
-        for name in ("types", "out_node", "out_port", "in_node", "in_port", "touched",
-                     "preferred", "distance", "next_slot", "streak", "gate", "fingerprint"):
-            torch.index_select(getattr(src, name), 0, order, out=getattr(dst, name))
+        names = ("types", "out_node", "out_port", "in_node", "in_port", "touched", "preferred",
+                 "distance", "next_slot", "streak", "gate", "fingerprint")
+        pairs = [(getattr(src, name), getattr(dst, name)) for name in names]
+        beam = [self.states, self.live, self.types, self.block_table, self.lengths]
+        fresh = [torch.empty_like(t) for t in beam]
+        segments = []
+        for a, b in pairs + list(zip(beam, fresh)):
+            nbytes = a[0].numel() * a.element_size() if a.numel() else 0
+            segments.append((a, 0, a.stride(0) * a.element_size(), order, b,
+                             b.stride(0) * b.element_size(), 0, None, nbytes, 1))
+        K.rows_copy(segments, n)
+        self.states, self.live, self.types, self.block_table, self.lengths = fresh
         self.topo, self.current = dst, 1 - self.current
 
     # ---- results ------------------------------------------------------------

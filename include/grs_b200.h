@@ -422,6 +422,17 @@ GRS_API int grs_shard_route(const int64_t* child_proposal, const int64_t* summar
                             int64_t* extent, int64_t* keep_local, int64_t* keep_global,
                             int64_t* out_local, int64_t* in_global, int32_t* status,
                             void* stream);
+/* Multi-segment row copy (at most 40 segments).  `segments` is a HOST array
+ * of 10 int64 words per segment: src address, src row stride, src unit
+ * stride, src index address (0 = none), dst address, dst row stride, dst unit
+ * stride, dst index address (0 = none), unit bytes, units per row.  Unit k of
+ * row i is read from src + src_index[i * units + k] * src_unit_stride (or src
+ * + i * src_row_stride + k * src_unit_stride without an index) and written
+ * likewise.  Rows: min(*n_dev, n_max) when n_dev is given, else n_max.  Packs
+ * the fields and cache pages of beams that change GPU into send rows,
+ * unpacks received rows, and reorders beams, each in one launch. */
+GRS_API int grs_rows_copy(int nseg, const int64_t* segments, const int64_t* n_dev,
+                          int64_t n_max, void* stream);
 
 #ifdef __cplusplus
 }

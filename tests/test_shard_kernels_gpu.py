@@ -196,3 +196,49 @@ def test_route_matches_oracle(world, accepted, beam, skew, seed):
         for got, name, n in zip(lists, ("keep_local", "keep_global", "out_local", "in_global"),
                                 (n_keep, n_keep, n_out, n_in)):
             np.testing.assert_array_equal(got[:n], expected[name], err_msg=name)
+
+
+@pytest.mark.parametrize("seed,n,n_dev", [(0, 7, None), (1, 40, 13), (2, 300, 300), (3, 5, 0)])
+def test_rows_copy_matches_numpy(seed, n, n_dev):
+    """Gather (indexed source), scatter (indexed destination) and multi-unit
+    segments with 1-, 4-, 8- and 16-byte aligned rows."""
+    from graph_rewrite_system_b200 import kernels as K
+
+    rng = np.random.default_rng(seed)
+    src_rows = n + 11
+    a = rng.integers(0, 255, size=(src_rows, 37), dtype=np.uint8)       # odd row bytes
+    b = rng.integers(-1000, 1000, size=(src_rows, 6), dtype=np.int32)
+    c = rng.integers(-(1 << 40), 1 << 40, size=(src_rows, 8))            # 64-byte rows
+    pages = rng.standard_normal((50, 24)).astype(np.float32)            # 96-byte pages
+    gather = rng.integers(0, src_rows, size=n)
+    page_ids = rng.choice(50, size=(n, 2), replace=False) if n * 2 <= 50 else \
+        rng.integers(0, 50, size=(n, 2))
+    layout = [(0, 37), (48, 24), (80, 64), (144, 192)]                  # packed row offsets
+    row = 336
+    ta, tb, tc, tp = _t(a, torch.uint8), _t(b, torch.int32), _t(c), _t(pages, torch.float32)
+    ti, tpi = _t(gather), _t(page_ids.reshape(-1))
+    packed = torch.zeros(n, row, dtype=torch.uint8, device=DEV)
+    flat = packed.view(-1)
+    count = None if n_dev is None else _t([n_dev])
+    K.rows_copy([(ta, 0, 37, ti, flat[0:], row, 0, None, 37, 1),
+                 (tb, 0, 24, ti, flat[48:], row, 0, None, 24, 1),
+                 (tc, 0, 64, ti, flat[80:], row, 0, None, 64, 1),
+                 (tp, 0, 96, tpi, flat[144:], row, 96, None, 96, 2)], n, count)
+    rows = n if n_dev is None else min(n, n_dev)
+    expected = np.zeros((n, row), np.uint8)
+    for i in range(rows):
+        g = gather[i]
+        expected[i, 0:37] = a[g]
+        expected[i, 48:72] = b[g].view(np.uint8)
+        expected[i, 80:144] = c[g].view(np.uint8)
+        expected[i, 144:336] = pages[page_ids[i]].reshape(-1).view(np.uint8)
+    np.testing.assert_array_equal(packed.cpu().numpy(), expected)
+    # scatter the packed pages back into a fresh arena at new page ids
+    arena = torch.zeros(60, 24, dtype=torch.float32, device=DEV)
+    targets = rng.choice(60, size=rows * 2, replace=False) if rows * 2 <= 60 else None
+    if targets is not None and rows:
+        K.rows_copy([(flat[144:], row, 96, None, arena, 0, 96, _t(targets), 96, 2)], rows)
+        got = arena.cpu().numpy()
+        for i in range(rows):
+            for k in range(2):
+                np.testing.assert_array_equal(got[targets[i * 2 + k]], pages[page_ids[i, k]])
