@@ -11,8 +11,60 @@
 
 namespace grs {
 
+// GELU(x) = x/2 (1 + erf(x / sqrt 2)) (the reference's exact, erf-based
+// form).  erfc comes from Abramowitz & Stegun, Handbook of Mathematical
+// Functions (1964), eq. 7.1.28: for z >= 0, erf(z) = 1 - (1 + a1 z + ... +
+// a6 z^6)^-16 + e(z) with |e(z)| <= 3e-7 (about 1e-6 after fp32 rounding);
+// x < 0 uses erfc directly (1 + erf(-z) = erfc(z)), so nothing cancels.  One
+// hardware reciprocal and ten multiply-adds per element (z is clamped at 5,
+// where erfc(5) = 1.5e-12 is below fp32 resolution next to 1), so the
+// elementwise kernels that apply it stay close to bandwidth-bound.
 __device__ __forceinline__ float gelu_exact(float x) {
-  return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+  const float z = fminf(fabsf(x) * 0.70710678118654752f, 5.f);
+  float q = fmaf(0.0000430638f, z, 0.0002765672f);
+  q = fmaf(q, z, 0.0001520143f);
+  q = fmaf(q, z, 0.0092705272f);
+  q = fmaf(q, z, 0.0422820123f);
+  q = fmaf(q, z, 0.0705230784f);
+  q = fmaf(q, z, 1.f);
+  q *= q;
+  q *= q;
+  q *= q;
+  q *= q;
+  const float erfc_z = __fdividef(1.f, q);
+  return x >= 0.f ? x * fmaf(-0.5f, erfc_z, 1.f) : 0.5f * x * erfc_z;
+}
+
+// Two lanes of gelu_exact with the packed fp32x2 multiply-adds of sm_100
+// (same operations and rounding per element, half the instructions).
+__device__ __forceinline__ float2 gelu_exact2(float2 x) {
+  const float2 z = make_float2(fminf(fabsf(x.x) * 0.70710678118654752f, 5.f),
+                               fminf(fabsf(x.y) * 0.70710678118654752f, 5.f));
+  const auto c = [](float v) { return make_float2(v, v); };
+  float2 q = __ffma2_rn(c(0.0000430638f), z, c(0.0002765672f));
+  q = __ffma2_rn(q, z, c(0.0001520143f));
+  q = __ffma2_rn(q, z, c(0.0092705272f));
+  q = __ffma2_rn(q, z, c(0.0422820123f));
+  q = __ffma2_rn(q, z, c(0.0705230784f));
+  q = __ffma2_rn(q, z, c(1.f));
+  q = __fmul2_rn(q, q);
+  q = __fmul2_rn(q, q);
+  q = __fmul2_rn(q, q);
+  q = __fmul2_rn(q, q);
+  const float ex = __fdividef(1.f, q.x), ey = __fdividef(1.f, q.y);
+  return make_float2(x.x >= 0.f ? x.x * fmaf(-0.5f, ex, 1.f) : 0.5f * x.x * ex,
+                     x.y >= 0.f ? x.y * fmaf(-0.5f, ey, 1.f) : 0.5f * x.y * ey);
+}
+
+template <int N>
+__device__ __forceinline__ void gelu_inplace(float* v) {
+#pragma unroll
+  for (int j = 0; j + 1 < N; j += 2) {
+    const float2 g = gelu_exact2(make_float2(v[j], v[j + 1]));
+    v[j] = g.x;
+    v[j + 1] = g.y;
+  }
+  if (N % 2) v[N - 1] = gelu_exact(v[N - 1]);
 }
 
 template <typename T> struct DT;
@@ -129,14 +181,13 @@ __device__ __forceinline__ void store8(float* p, const float v[8]) {
 // In place: y[r, c] = GELU(y[r, c] + bias[c]) (bias optional).  Each thread
 // handles groups of 8 consecutive columns (cols % 8 == 0, 16-byte aligned
 // rows), grid-strided.
-template <typename T>
+template <typename T, typename I>
 __global__ void bias_gelu_kernel(T* y, int64_t rows, int cols, int64_t stride,
                                  const float* bias, int apply_gelu) {
-  const int groups = cols >> 3;
-  const int64_t n = rows * groups;
-  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n;
-       g += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = g / groups;
+  const I groups = (I)(cols >> 3);
+  const I n = (I)rows * groups;   // I = uint32_t whenever the group count fits
+  for (I g = (I)blockIdx.x * blockDim.x + threadIdx.x; g < n; g += (I)gridDim.x * blockDim.x) {
+    const I r = g / groups;
     const int c = (int)(g - r * groups) << 3;
     T* p = y + r * stride + c;
     float v[8];
@@ -147,10 +198,7 @@ __global__ void bias_gelu_kernel(T* y, int64_t rows, int cols, int64_t stride,
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] += b[j];
     }
-    if (apply_gelu) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = gelu_exact(v[j]);
-    }
+    if (apply_gelu) gelu_inplace<8>(v);
     store8(p, v);
   }
 }
@@ -415,8 +463,7 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) update_live_hidden_kernel(
 #pragma unroll
         for (int j = 0; j < VPLH; ++j) acc[j] += w * vv[j];
       }
-#pragma unroll
-      for (int j = 0; j < VPLH; ++j) acc[j] = gelu_exact(acc[j]);
+      gelu_inplace<VPLH>(acc);
       store_vec<VPLH>(hidden + row * hidden_stride + h0, acc);
     }
   }
@@ -586,8 +633,15 @@ extern "C" int grs_bias_gelu(int dtype, void* y, int64_t rows, int cols, int64_t
   if (cols % 8 || stride % 8 || ((uintptr_t)y & 15) || ((uintptr_t)bias & 15)) return GRS_ERR_SHAPE;
   const int64_t groups = rows * (cols / 8);
   const int grid = (int)(groups < 148 * 16 * 256 ? ceil_div(groups, 256) : 148 * 16);
-  GRS_DTYPE_SWITCH(T, dtype, bias_gelu_kernel<T><<<grid, 256, 0, grs::counted((cudaStream_t)stream)>>>(
-      (T*)y, rows, cols, stride, bias, apply_gelu))
+  if (groups < (int64_t)0xffffffffll - 148 * 16 * 256) {
+    GRS_DTYPE_SWITCH(T, dtype,
+        bias_gelu_kernel<T, uint32_t><<<grid, 256, 0, grs::counted((cudaStream_t)stream)>>>(
+            (T*)y, rows, cols, stride, bias, apply_gelu))
+  } else {
+    GRS_DTYPE_SWITCH(T, dtype,
+        bias_gelu_kernel<T, int64_t><<<grid, 256, 0, grs::counted((cudaStream_t)stream)>>>(
+            (T*)y, rows, cols, stride, bias, apply_gelu))
+  }
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
