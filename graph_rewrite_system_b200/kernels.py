@@ -212,3 +212,15 @@ def rows_copy(segments, n_max: int, n_dev: torch.Tensor | None = None) -> None:
     _lib.check(_lib.lib().grs_rows_copy(
         len(words) // 10, table.ctypes.data if len(words) else None,
         _p(n_dev), n_max, stream()), "rows_copy")
+
+
+def gemm_bias_gelu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                   gelu: bool, out: torch.Tensor, status: torch.Tensor | None = None) -> int:
+    """out = (x @ weight.T (+ bias)) then GELU on the tensor cores in one
+    pass (bf16; weight is a K-major [N, K] Linear weight).  Returns the
+    library status: GRS_ERR_SHAPE (-4) when the shapes do not fit the kernel,
+    in which case nothing was launched."""
+    return _lib.lib().grs_gemm_bf16_epilogue(
+        x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), x.shape[0],
+        weight.shape[0], x.shape[1], _p(bias), int(gelu), out.data_ptr(), out.stride(0),
+        _p(status), stream())

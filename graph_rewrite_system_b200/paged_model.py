@@ -26,8 +26,9 @@ import torch
 from torch import nn
 import torch.nn.functional as F
 
+from . import _lib
 from . import kernels as K
-from .paged_attention import paged_attention
+from .paged_attention import _status_word, paged_attention
 from .synthetic import RuleMetadata, parse_pattern
 
 
@@ -231,6 +232,8 @@ class PagedActionBindingModel(nn.Module):
                                              layer.backward_message.weight), 0))
                 w[p + "rel"] = f(layer.relation.weight)
                 w[p + "u0_t"], w[p + "u0_b"] = t(layer.update[0].weight), f(layer.update[0].bias)
+                if dt == torch.bfloat16:   # K-major operand of the tensor-core GEMM
+                    w[p + "u0_k"] = c(layer.update[0].weight)
                 w[p + "u2_t"], w[p + "u2_b"] = t(layer.update[2].weight), c(layer.update[2].bias)
                 w[p + "norm_w"], w[p + "norm_b"] = f(layer.norm.weight), f(layer.norm.bias)
         if self.readout_graph_layers_count:
@@ -303,8 +306,9 @@ class PagedActionBindingModel(nn.Module):
             x = x_buf[:, :W]
             K.linear(x, w[p + "fb_t"], out=fb)
             K.graph_aggregate(fb, w[p + "rel"], ports, slots, x_buf[:, W:])
-            K.linear(x_buf, w[p + "u0_t"], out=hidden)
-            K.bias_gelu(hidden, w[p + "u0_b"])
+            if not self._fused_update(x_buf, w.get(p + "u0_k"), w[p + "u0_b"], hidden):
+                K.linear(x_buf, w[p + "u0_t"], out=hidden)
+                K.bias_gelu(hidden, w[p + "u0_b"])
             K.linear(hidden, w[p + "u2_t"], w[p + "u2_b"], out=upd)
             target = spare.pop(0)
             K.add_layernorm(x, upd, gamma=w[p + "norm_w"], beta=w[p + "norm_b"],
@@ -313,6 +317,25 @@ class PagedActionBindingModel(nn.Module):
                 spare.append(x_buf)
             x_buf = target
         return x_buf
+
+    # rows from which the tensor-core GEMM with the fused GELU epilogue is used
+    FUSED_MIN_ROWS = 4096
+
+    def _fused_update(self, x: torch.Tensor, weight_k, bias, out: torch.Tensor) -> bool:
+        """hidden = GELU(x @ u0^T + b) in one tensor-core pass (bf16, large
+        batches); False when the caller must run the GEMM and bias+GELU
+        separately (fp32 configuration, small batch, or a shape the kernel
+        does not take)."""
+        if weight_k is None or x.shape[0] < self.FUSED_MIN_ROWS:
+            return False
+        status = getattr(self, "kernel_status", None)
+        if status is None:
+            status = _status_word(x.device)
+        code = K.gemm_bias_gelu(x, weight_k, bias, True, out, status)
+        if code == -4:                       # GRS_ERR_SHAPE: nothing launched
+            return False
+        _lib.check(code, "tensor-core GEMM")
+        return True
 
     def _ports(self, batch: dict, b: int, s: int, device):
         return K.edges_to_ports(batch["current_edge_batch"] if "current_edge_batch" in batch

@@ -133,6 +133,8 @@ class DeviceBeamSearch:
         self.step_keys = torch.empty(self.step_capacity, device=dev, dtype=torch.int64)
         self.step_first = torch.empty(self.step_capacity, device=dev, dtype=torch.int32)
         self.status = torch.zeros(1, device=dev, dtype=torch.int32)
+        # the model's tensor-core kernels report into the level's status word
+        model.kernel_status = self.status
         self.summary = torch.zeros(6, device=dev, dtype=torch.int64)
         self.rows: list[StepRow] = []
         self.timer: StageTimer | None = None

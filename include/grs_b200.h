@@ -378,6 +378,19 @@ GRS_API int grs_topology_fingerprint(const int64_t* types, const int32_t* out_no
                                      const int32_t* in_port, int batch, int slots, uint64_t* fp,
                                      void* stream);
 
+/* ---- tensor-core GEMM with a fused epilogue (sm_100a tcgen05) -------------
+ * out[M, N] = (A[M, K] . B[N, K]^T (+ bias[N])) then GELU when `gelu`, bf16 in
+ * and out, fp32 accumulation: the readout graph layers' u0 projection and its
+ * GELU (paged_model.py:381-436, model.py:26-53) in one pass.  A row-major with
+ * row stride lda, B K-major (a Linear weight [out, in]) with row stride ldb,
+ * out row stride ldo (elements).  Requires K % 64 == 0, N % 256 == 0, strides
+ * multiples of 8 elements and 16-byte aligned pointers; GRS_ERR_SHAPE
+ * otherwise (the caller then uses a library GEMM).  `status` (device int32,
+ * may be null) receives GRS_ERR_TIMEOUT if an in-kernel wait gives up. */
+GRS_API int grs_gemm_bf16_epilogue(const void* a, int64_t lda, const void* b, int64_t ldb, int M,
+                                   int N, int K, const float* bias, int gelu, void* out,
+                                   int64_t ldo, int32_t* status, void* stream);
+
 /* ---- beam search sharded over the GPUs of a node ---------------------------
  * The reference ranks a level's proposals globally
  * (paged_rollout_benchmark.py:967-1005) and accepts in that order
