@@ -65,6 +65,8 @@ def _parse_header(text: str) -> dict[str, tuple[object, list]]:
         ret = ret.replace("const", "").strip()
         if "*" in ret:
             restype = ctypes.c_char_p if ret.startswith("char") else c_ptr
+        elif ret == "void":
+            restype = None
         else:
             restype = _C_TYPES[ret.split()[0]]
         out[name] = (restype, args)

@@ -12,6 +12,10 @@ extern "C" int64_t grs_launch_count(void) {
   return grs::g_launches.load(std::memory_order_relaxed);
 }
 
+extern "C" void grs_count_launches(int64_t n) {
+  if (n > 0) grs::g_launches.fetch_add(n, std::memory_order_relaxed);
+}
+
 extern "C" const char* grs_version(void) {
   return "grs_b200 0.1 sm_100a";
 }

@@ -466,11 +466,15 @@ class PagedActionBindingModel(nn.Module):
     @torch.no_grad()
     def advance_device(self, states, live, gate_types, xfer_ids, source_ids, source_slots,
                        destination_slots, destination_types, paged_key_cache, paged_value_cache,
-                       block_table, past_lengths):
+                       block_table, past_lengths, return_readout_kv: bool = False,
+                       graphed: bool = False):
         """One-token step without host synchronisation: states [B, S, W] already
         hold every referenced slot; ids int64, past_lengths int32 on the device.
         Returns (next_states, next_live, next_types, new_keys [L,B,H,D],
-        new_values, action_token)."""
+        new_values, action_token) (+ the action's readout key and value with
+        return_readout_kv).  With `graphed` the per-beam token path replays a
+        CUDA graph and the returned keys, values, action and readout K/V are
+        overwritten by the next graphed step of the same shape."""
         w, W = self.prepare(), self.width
         dev, dt = states.device, self.compute_dtype
         b = states.shape[0]
@@ -484,6 +488,32 @@ class PagedActionBindingModel(nn.Module):
         active = torch.empty(b, device=dev, dtype=torch.bool)
         K.action_inputs(states, xfer_ids, source_ids, source_slots, w["xfer_embedding"],
                         w["source_reps"], bound, ctx_in, source_mask, active)
+        step = self._token_step if graphed else self._token_step_eager
+        raw, new_keys, new_values, action, rk, rv = step(
+            ctx_in, active, past_lengths.to(torch.int32).contiguous(),
+            block_table.to(torch.int32).contiguous(), paged_key_cache, paged_value_cache)
+        next_states, next_live, next_types = self._update_and_apply(
+            states, live, gate_types, bound, source_mask, raw, active, source_slots,
+            destination_slots, destination_types)
+        if return_readout_kv:
+            return next_states, next_live, next_types, new_keys, new_values, action, rk, rv
+        return next_states, next_live, next_types, new_keys, new_values, action
+
+    # ---- the per-beam token path of one step (CUDA graph per shape) ------------
+    USE_GRAPHS = True
+
+    def _token_step_eager(self, ctx_in, active, past_lengths, block_table, key_cache,
+                          value_cache):
+        """Action context MLP, position token, the causal layers over the paged
+        cache, output norm and the readout K/V of the new action: everything
+        of a step that works on one row per beam (paged_model.py:444-613,
+        338-347).  Returns (raw, new_keys, new_values, action, readout key,
+        readout value)."""
+        w, W = self.prepare(), self.width
+        dev, dt = ctx_in.device, self.compute_dtype
+        b = ctx_in.shape[0]
+        h = self.action_heads
+        hd = W // h
         hidden = K.bias_gelu(K.linear(ctx_in, w["ac0_t"]), w["ac0_b"])
         raw = K.linear(hidden, w["ac3_t"], w["ac3_b"])
         token = torch.empty_like(raw)
@@ -498,9 +528,9 @@ class PagedActionBindingModel(nn.Module):
             K.add_layernorm(token, gamma=w[p + "in_w"], beta=w[p + "in_b"], ln_out=ln)
             qkv = K.linear(ln, w[p + "qkv_t"]).view(b, 3, h, hd)
             q, k, v = qkv.unbind(1)
-            ctx = paged_attention(q.unsqueeze(2), paged_key_cache[layer],
-                                  paged_value_cache[layer], block_table, past_lengths,
-                                  current_key=k, current_value=v, current_valid=valid)
+            ctx = paged_attention(q.unsqueeze(2), key_cache[layer], value_cache[layer],
+                                  block_table, past_lengths, current_key=k, current_value=v,
+                                  current_valid=valid)
             o = K.linear(ctx.reshape(b, W), w[p + "out_t"])
             K.add_layernorm(token, o, gamma=w[p + "ffn_norm_w"], beta=w[p + "ffn_norm_b"],
                             sum_out=token2, ln_out=ln)
@@ -513,10 +543,49 @@ class PagedActionBindingModel(nn.Module):
         action = torch.empty_like(token)
         K.add_layernorm(token, gamma=w["out_norm_w"], beta=w["out_norm_b"], ln_out=action,
                         zero_beam=active)
-        next_states, next_live, next_types = self._update_and_apply(
-            states, live, gate_types, bound, source_mask, raw, active, source_slots,
-            destination_slots, destination_types)
-        return next_states, next_live, next_types, new_keys, new_values, action
+        rk, rv = self.project_action_readout_kv(action)
+        return raw, new_keys, new_values, action, rk, rv
+
+    def _token_step(self, ctx_in, active, past_lengths, block_table, key_cache, value_cache):
+        """_token_step_eager replayed from a CUDA graph captured once per
+        (beams, block-table width, weights, cache) key: ~60 launches of one-row-
+        per-beam work cost one replay and four input copies of host time.  The
+        outputs live in the graph's pool until the next replay of that key, so
+        they must be consumed before the next step (the search does)."""
+        if not self.USE_GRAPHS or ctx_in.shape[0] == 0:
+            return self._token_step_eager(ctx_in, active, past_lengths, block_table, key_cache,
+                                          value_cache)
+        version = self._version_key()
+        graphs = getattr(self, "_graphs", None)
+        if graphs is None or graphs[0] != version:
+            graphs = self._graphs = (version, {})
+        key = (ctx_in.shape[0], block_table.shape[1], ctx_in.dtype, key_cache.data_ptr(),
+               value_cache.data_ptr(), ctx_in.device)
+        entry = graphs[1].get(key)
+        inputs = (ctx_in, active, past_lengths, block_table)
+        if entry is None:
+            entry = graphs[1][key] = self._capture_token_step(inputs, key_cache, value_cache)
+        static, graph, outs, launches = entry
+        for dst, src in zip(static, inputs):
+            dst.copy_(src)
+        graph.replay()
+        _lib.lib().grs_count_launches(launches)
+        return outs
+
+    def _capture_token_step(self, inputs, key_cache, value_cache):
+        static = [t.clone() for t in inputs]
+        current = torch.cuda.current_stream(inputs[0].device)
+        side = torch.cuda.Stream(inputs[0].device)
+        side.wait_stream(current)
+        with torch.cuda.stream(side), _lib.pinned_stream():   # warm-up: libraries initialise
+            self._token_step_eager(*static, key_cache, value_cache)
+        current.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        before = int(_lib.lib().grs_launch_count())
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"), _lib.pinned_stream():
+            outs = self._token_step_eager(*static, key_cache, value_cache)
+        launches = int(_lib.lib().grs_launch_count()) - before
+        return static, graph, outs, launches
 
     def _update_and_apply(self, states, live, gate_types, bound, source_mask, raw, active,
                           source_slots, destination_slots, destination_types):

@@ -356,10 +356,10 @@ class DeviceBeamSearch:
         lengths_par = torch.empty(accepted, device=dev, dtype=torch.int32)
         K.gather_beams(self.lengths, a_parent, lengths_par)
         self._check_tables("advance", table_par, lengths_par)
-        states, live, types, new_k, new_v, action = model.advance_device(
+        states, live, types, new_k, new_v, action, rk, rv = model.advance_device(
             states_par, live_par, types_par, a_xfer, a_source, a_src, a_dst, a_dst_types,
-            self.cache.keys, self.cache.values, table_par, lengths_par)
-        rk, rv = model.project_action_readout_kv(action)
+            self.cache.keys, self.cache.values, table_par, lengths_par,
+            return_readout_kv=True, graphed=True)
         self._mark("cache_append_release")
         child_cols = -(-(depth + 1) // cfg.page_size)
         child_table, child_lengths = self.cache.append_device(

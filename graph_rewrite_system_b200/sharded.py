@@ -377,10 +377,10 @@ class ShardedBeamSearch(DeviceBeamSearch):
                     K.gather_beams(ty, idx, types_par[lo:hi], fill_byte=0xFF)
                     K.gather_beams(tb, idx, table_par[lo:hi])
                     K.gather_beams(ln, idx, lengths_par[lo:hi])
-            states, live, types, new_k, new_v, action = model.advance_device(
+            states, live, types, new_k, new_v, action, rk, rv = model.advance_device(
                 states_par, live_par, types_par, a_xfer, a_source, a_src, a_dst, a_dst_types,
-                self.cache.keys, self.cache.values, table_par, lengths_par)
-            rk, rv = model.project_action_readout_kv(action)
+                self.cache.keys, self.cache.values, table_par, lengths_par,
+                return_readout_kv=True, graphed=True)
             self._mark("cache_append_release")
             child_table, child_lengths = self.cache.append_device(
                 table_par, lengths_par, new_k, new_v, action, rk, rv, child_cols=child_cols)

@@ -46,6 +46,9 @@ GRS_API const char* grs_version(void);
 /* Number of kernels this library has launched in the process so far (every
  * launch site counts itself; library kernels such as CUB sorts do not). */
 GRS_API int64_t grs_launch_count(void);
+/* Add n to that counter: the library kernels a replay of a captured CUDA
+ * graph launches (counted once at capture time, not by the replay). */
+GRS_API void grs_count_launches(int64_t n);
 
 /* ---- paged attention: paged_attention.py:217-306 (paged_attention) ------
  * query [B,H,Q,D] (strides q_sb,q_sh,q_sq; D contiguous); key/value cache
