@@ -1,7 +1,7 @@
 """Benchmark of the B200 beam-search decode path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload decode-attention|rollout]
+                    [--workload rollout|decode-attention|update-gemm]
 
 Workloads (seeded synthetic inputs; the reference's hwb6 circuit, rule set
 and checkpoint are not available):
@@ -13,6 +13,9 @@ and checkpoint are not available):
   state ranked to 16 per parent and 16000 globally.  A step is one search
   level.  The decode-attention microbenchmark below is measured in the same
   run and reported under ``paged_attention``.
+* ``update-gemm``: the readout graph layers' update projection with its GELU
+  as one tcgen05 tensor-core launch, GELU(x [300000, 512] @ W^T + b), against
+  the library GEMM + bias+GELU pair on the same inputs.
 * ``decode-attention``: the shared-prefix paged decode microbenchmark -
   512 beams, one query token each, 8 heads x 32, bf16, 381 shared s0 node
   keys, 64 action K/V entries per beam in pages of 16, block tables from a
@@ -576,6 +579,9 @@ def run_reference(args, world, rank):
     """--impl reference: the CPU oracle on the same workload (rank 0 only)."""
     if rank != 0:
         return None
+    if args.workload == "update-gemm":
+        return {"impl": "reference", "unavailable": "the update-gemm microbenchmark has no CPU "
+                "arm; the rollout workload's reference arm times the CPU oracle"}
     if args.workload == "rollout":
         started = time.perf_counter()
         base = cpu_rollout(args.steps, args.warmup, sample_beams=48, budget_s=150.0)
@@ -618,13 +624,103 @@ def run_reference(args, world, rank):
     }
 
 
+def run_update_gemm(args, world, rank, device):
+    """The readout graph layers' update projection as one tensor-core launch:
+    GELU(x [300000, 512] @ u0^T [512 -> 512] + b), bf16 in and out, fp32
+    accumulation (tcgen05 GEMM with the fused epilogue).  x rotates between two
+    307 MB inputs (larger than L2); the library GEMM + separate bias+GELU pair
+    is timed the same way for comparison."""
+    from graph_rewrite_system_b200 import kernels as K
+
+    m, k, n = 300000, 512, 512
+    gen = torch.Generator(device=device).manual_seed(rank + 7)
+    xs = [torch.randn(m, k, device=device, generator=gen).to(torch.bfloat16) for _ in range(2)]
+    w = (torch.randn(n, k, device=device, generator=gen) / k ** 0.5).to(torch.bfloat16)
+    w_t = w.t().contiguous()
+    b = torch.randn(n, device=device, generator=gen)
+    out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+    status = torch.zeros(1, device=device, dtype=torch.int32)
+    stream = torch.cuda.current_stream(device)
+    flops = 2.0 * m * n * k
+
+    def fused(i):
+        code = K.gemm_bias_gelu(xs[i % 2], w, b, True, out, status)
+        if code:
+            raise RuntimeError(f"tensor-core GEMM refused the shape ({code})")
+
+    def library(i):
+        torch.mm(xs[i % 2], w_t, out=out)
+        K.bias_gelu(out, b)
+
+    def timed(fn, steps):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(steps)]
+        torch.cuda._sleep(queue_ahead_cycles(steps))
+        for i, (s0, s1) in enumerate(events):
+            s0.record(stream)
+            fn(i)
+            s1.record(stream)
+        torch.cuda.synchronize(device)
+        return max_over_ranks(sum(a.elapsed_time(z) for a, z in events), world, device) / steps
+
+    launches0 = launch_count()
+    with ClockSampler(device.index) as clocks:
+        ms = timed(fused, args.steps)
+    launches = launch_count() - launches0
+    lib_ms = timed(library, args.steps)
+    if int(status.item()):
+        raise RuntimeError(f"tensor-core GEMM reported status {int(status.item())}")
+    # end to end: x from pinned host memory, one fused launch, the result back
+    host_x = xs[0].cpu().pin_memory()
+    host_out = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+    dev_x = torch.empty_like(xs[0])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(3):
+        dev_x.copy_(host_x, non_blocking=True)
+        K.gemm_bias_gelu(dev_x, w, b, True, out, status)
+        host_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / 3, world, device)
+    peaks = measured_peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic_ratio = profiled_traffic("update_gemm_traffic_ratio")
+    algorithmic_bytes = 2.0 * (m * k + n * k + m * n) + 4 * n
+    return {
+        "metric": "update projection GEMM+GELU throughput", "value": world * achieved,
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "update-gemm: GELU(x[300000,512] @ W[512,512]^T + b), bf16, "
+                               "two rotating 307 MB inputs (larger than L2)",
+                   "library_gemm_plus_bias_gelu_ms": lib_ms,
+                   "speedup_vs_library_pair": lib_ms / ms},
+        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * 2},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                     "traffic": traffic_ratio * algorithmic_bytes if traffic_ratio else None,
+                     "kernel": "gemm_tc_kernel", "algorithmic_bytes_per_launch": algorithmic_bytes,
+                     "hbm_frac": algorithmic_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                     "peak_source": f"{peaks['source']} bf16_tflops (burst)"},
+        "clocks": clocks.summary(),
+    }
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=60)
     parser.add_argument("--warmup", type=int, default=4)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    parser.add_argument("--workload", choices=("rollout", "decode-attention"), default="rollout")
+    parser.add_argument("--workload", choices=("rollout", "decode-attention", "update-gemm"),
+                        default="rollout")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--beam", type=int, default=1000,
                         help="rollout beam size (1000 is the benchmark configuration)")
@@ -653,6 +749,8 @@ def main() -> None:
             attention = run_decode_attention(attn_args, world, rank, device)
             line["paged_attention"] = {k: attention[k] for k in (
                 "value", "unit", "ms_per_step", "roofline", "config")}
+    elif args.workload == "update-gemm":
+        line = run_update_gemm(args, world, rank, device)
     else:
         line = run_decode_attention(args, world, rank, device)
     if rank == 0:

@@ -398,6 +398,69 @@ constexpr int ULH_ROWS = 64;   // slot rows of one beam per CTA
 // A CTA takes up to 64 slot rows of one beam (grid = row blocks x beams) and
 // stages that beam's keys, vw and c in shared memory (fp32) once; a warp
 // handles a row, each lane a contiguous chunk of VPLQ (q) and VPLH (xa, h)
+
+// add_ln_kernel with each lane owning VPL contiguous elements of the row
+// (width == 32 * VPL): one 16-byte access per lane and tensor instead of
+// VPL 2-byte ones.  Same semantics as add_ln_kernel.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(ROW_WARPS * 32) add_ln_vec_kernel(AddLnArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  const int64_t beam = row / a.rows_per_beam;
+  const int c0 = lane * VPL;
+  const float sc = a.scale ? a.scale[row] : 1.f;
+  bool zc = true, wc = true;
+  if (a.zero_row) zc = zc && a.zero_row[row];
+  if (a.zero_beam) zc = zc && a.zero_beam[beam];
+  if (a.where_row) wc = wc && a.where_row[row];
+  if (a.where_beam) wc = wc && a.where_beam[beam];
+  if (a.where_len) wc = wc && a.where_len[beam] > 0;
+  float xv[VPL], s[VPL];
+  load_vec<VPL>(reinterpret_cast<const T*>(a.x) + row * a.x_stride + c0, xv);
+  if (a.y) {
+    float yv[VPL];
+    load_vec<VPL>(reinterpret_cast<const T*>(a.y) + row * a.y_stride + c0, yv);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) s[j] = xv[j] + sc * yv[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) s[j] = xv[j];
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    if (a.zero_before && !zc) s[j] = 0.f;
+    sum += s[j];
+  }
+  if (a.sum_out) store_vec<VPL>(reinterpret_cast<T*>(a.sum_out) + row * a.sum_stride + c0, s);
+  if (!a.ln_out) return;
+  const float mean = warp_sum(sum) / a.width;
+  float var = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const float d = s[j] - mean;
+    var += d * d;
+  }
+  const float rstd = rsqrtf(warp_sum(var) / a.width + a.eps);
+  float r[VPL];
+  if (wc) {
+    float g[VPL], b[VPL];
+    load_vec<VPL>(a.gamma + c0, g);
+    load_vec<VPL>(a.beta + c0, b);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) r[j] = (s[j] - mean) * rstd * g[j] + b[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) r[j] = xv[j];
+  }
+  if (!a.zero_before && !zc) {
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) r[j] = 0.f;
+  }
+  store_vec<VPL>(reinterpret_cast<T*>(a.ln_out) + row * a.ln_stride + c0, r);
+}
+
 // elements read and written with vector accesses.
 template <typename T, int VPLQ, int VPLH>
 __global__ void __launch_bounds__(ROW_WARPS * 32) update_live_hidden_kernel(
@@ -620,8 +683,26 @@ extern "C" int grs_add_layernorm(int dtype, const void* x, int64_t x_stride, con
               ln_stride, zero_row, zero_beam, where_row, where_beam, where_len, rows,
               rows_per_beam, width, eps, zero_before};
   const int grid = ceil_div(rows, ROW_WARPS);
-  GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
-      add_ln_kernel<T, V><<<grid, ROW_WARPS * 32, 0, grs::counted((cudaStream_t)stream)>>>(a)))
+  // contiguous per-lane vectors when the row is 32 whole vectors and every
+  // pointer and stride keeps them aligned
+  const int esize = dtype == GRS_DTYPE_F32 ? 4 : 2;
+  const int vpl = width / 32;
+  const int64_t vbytes = std::min<int64_t>(16, (int64_t)vpl * esize);
+  const auto ok = [&](const void* p, int64_t stride) {
+    return p == nullptr ||
+           ((reinterpret_cast<uintptr_t>(p) % vbytes) == 0 && (stride * esize) % vbytes == 0);
+  };
+  const bool vec = width % 32 == 0 && vpl >= 2 && vpl <= 16 && ok(x, x_stride) &&
+                   ok(y, y_stride) && ok(sum_out, sum_stride) && ok(ln_out, ln_stride) &&
+                   (reinterpret_cast<uintptr_t>(gamma) % 16) == 0 &&
+                   (reinterpret_cast<uintptr_t>(beta) % 16) == 0;
+  if (vec) {
+    GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
+        add_ln_vec_kernel<T, V><<<grid, ROW_WARPS * 32, 0, grs::counted((cudaStream_t)stream)>>>(a)))
+  } else {
+    GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
+        add_ln_kernel<T, V><<<grid, ROW_WARPS * 32, 0, grs::counted((cudaStream_t)stream)>>>(a)))
+  }
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
