@@ -76,13 +76,14 @@ def measured_peaks() -> dict:
 
 
 class KernelProbe:
-    """Times every call of one kernel wrapper of graph_rewrite_system_b200.kernels
-    with CUDA events on the launching stream while active, and adds up the
-    wrapper's algorithmic bytes."""
+    """Times every `every`-th call of one kernel wrapper of
+    graph_rewrite_system_b200.kernels with CUDA events on the launching stream
+    while active, and adds up those calls' algorithmic bytes (sampling keeps
+    the probe's own device time out of most of the step)."""
 
-    def __init__(self, name: str, bytes_fn):
-        self.name, self.bytes_fn = name, bytes_fn
-        self.events, self.bytes, self.rows = [], 0, 0
+    def __init__(self, name: str, bytes_fn, every: int = 4):
+        self.name, self.bytes_fn, self.every = name, bytes_fn, every
+        self.events, self.bytes, self.rows, self.calls = [], 0, 0, 0
 
     def __enter__(self):
         from graph_rewrite_system_b200 import kernels
@@ -90,6 +91,9 @@ class KernelProbe:
         self.module, self.original = kernels, getattr(kernels, self.name)
 
         def timed(*a, **kw):
+            self.calls += 1
+            if self.calls % self.every:
+                return self.original(*a, **kw)
             start = torch.cuda.Event(enable_timing=True)
             end = torch.cuda.Event(enable_timing=True)
             # keep the device busy while the host issues the launch, so the
@@ -123,17 +127,21 @@ class KernelProbe:
         traffic = traffic_ratio * per_launch if traffic_ratio else None
         return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                "kernel": kernel, "launches": n, "avg_launch_ms": ms,
+                "kernel": kernel, "launches": n, "sampled_every": self.every, "avg_launch_ms": ms,
                 "algorithmic_bytes_per_launch": per_launch,
                 "peak_source": f"{peaks['source']} hbm_gbs"}
 
 
-def bias_gelu_bytes(y, bias, gelu=True):
-    """In-place bias + GELU over y [rows, cols]: read and write y, read the bias."""
-    nbytes = 2 * y.numel() * y.element_size()
-    if bias is not None:
-        nbytes += bias.numel() * bias.element_size()
-    return nbytes, y.shape[0]
+def add_layernorm_bytes(x, y=None, *, scale=None, gamma=None, beta=None, sum_out=None,
+                        ln_out=None, zero_row=None, **_):
+    """Residual add + LayerNorm over rows of x: read x (and y), write the sum
+    and/or the normalised rows, read the per-row scale / mask and gamma, beta."""
+    rows, width, es = x.shape[0], x.shape[-1], x.element_size()
+    nbytes = rows * width * es * (1 + (y is not None) + (sum_out is not None)
+                                  + (ln_out is not None))
+    nbytes += rows * ((scale is not None) * 4 + (zero_row is not None))
+    nbytes += width * 4 * ((gamma is not None) + (beta is not None))
+    return nbytes, rows
 
 
 def launch_count() -> int:
@@ -448,7 +456,7 @@ def run_rollout(args, world, rank, device):
     done = 0
     launches0 = launch_count()
     moved0 = (getattr(search, "moved_children", 0), getattr(search, "moved_bytes", 0))
-    probe = KernelProbe("bias_gelu", bias_gelu_bytes)
+    probe = KernelProbe("add_layernorm", add_layernorm_bytes)
     with ClockSampler(device.index) as clocks, probe:
         for i in range(args.steps):
             starts[i].record(stream)
@@ -518,8 +526,8 @@ def run_rollout(args, world, rank, device):
                 "h2d_bytes_per_step": h2d // depth, "d2h_bytes_per_step": d2h,
                 "scope": "DeviceBeamSearch.run(): s0 upload, all levels, beam summary download"},
         "gpu_launches": launches,
-        "roofline": probe.roofline(measured_peaks(), "bias_gelu_kernel",
-                                   profiled_traffic("bias_gelu_traffic_ratio")),
+        "roofline": probe.roofline(measured_peaks(), "add_ln_vec_kernel",
+                                   profiled_traffic("add_ln_traffic_ratio")),
         "search": {"last_level": {k: getattr(last, k) for k in (
                        "input_states", "output_states", "best_speculative_gate_count",
                        "predicted_actions", "eligible_actions_before_parent_cap",

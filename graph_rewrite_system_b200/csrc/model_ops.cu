@@ -399,6 +399,54 @@ constexpr int ULH_ROWS = 64;   // slot rows of one beam per CTA
 // stages that beam's keys, vw and c in shared memory (fp32) once; a warp
 // handles a row, each lane a contiguous chunk of VPLQ (q) and VPLH (xa, h)
 
+// graph_aggregate_kernel with each lane owning VPL contiguous elements
+// (width == 32 * VPL): 16-byte row accesses instead of 2-byte ones.  Every
+// element accumulates the same terms in the same order, so results are
+// bit-identical to the strided kernel.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(ROW_WARPS * 32) graph_aggregate_vec_kernel(
+    const T* fb, int64_t fb_stride, const float* rel, const int32_t* in_node,
+    const int32_t* in_port, const int32_t* out_node, const int32_t* out_port, int64_t rows,
+    int slots, int port_slots, int width, T* agg, int64_t agg_stride) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t beam_base = (row / slots) * slots;
+  const int64_t prow = (row / slots) * port_slots + row % slots;
+  const int c0 = lane * VPL;
+  float acc[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) acc[j] = 0.f;
+  int deg = 0;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const int src = in_node[prow * 4 + p];
+    if (src >= 0) {
+      const int r = in_port[prow * 4 + p] * 4 + p;
+      float f[VPL], e[VPL];
+      load_vec<VPL>(fb + (beam_base + src) * fb_stride + c0, f);
+      load_vec<VPL>(rel + (int64_t)r * width + c0, e);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) acc[j] += f[j] + e[j];
+      ++deg;
+    }
+    const int dst = out_node[prow * 4 + p];
+    if (dst >= 0) {
+      const int r = 16 + p * 4 + out_port[prow * 4 + p];
+      float f[VPL], e[VPL];
+      load_vec<VPL>(fb + (beam_base + dst) * fb_stride + width + c0, f);
+      load_vec<VPL>(rel + (int64_t)r * width + c0, e);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) acc[j] += f[j] + e[j];
+      ++deg;
+    }
+  }
+  const float inv = 1.f / (float)(deg > 0 ? deg : 1);
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) acc[j] *= inv;
+  store_vec<VPL>(agg + row * agg_stride + c0, acc);
+}
+
 // add_ln_kernel with each lane owning VPL contiguous elements of the row
 // (width == 32 * VPL): one 16-byte access per lane and tensor instead of
 // VPL 2-byte ones.  Same semantics as add_ln_kernel.
@@ -463,7 +511,7 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) add_ln_vec_kernel(AddLnArgs a)
 
 // elements read and written with vector accesses.
 template <typename T, int VPLQ, int VPLH>
-__global__ void __launch_bounds__(ROW_WARPS * 32) update_live_hidden_kernel(
+__global__ void __launch_bounds__(ROW_WARPS * 32, 4) update_live_hidden_kernel(
     const T* qxa, int64_t qxa_stride, const T* keys, const T* vw, const T* cvec,
     const uint8_t* source_mask, int pattern, int slots, int width, T* hidden,
     int64_t hidden_stride, float* affinity) {
@@ -497,7 +545,10 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) update_live_hidden_kernel(
     if (h_on) load_vec<VPLH>(q + width + h0, xv);
     float logit[8];
     float mx = -INFINITY;
-    for (int k = 0; k < pattern; ++k) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {   // pattern <= 8: logits stay in registers
+      logit[k] = 0.f;
+      if (k >= pattern) continue;
       float d = 0.f;
       if (q_on) {
         float kv[VPLQ];
@@ -511,7 +562,12 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) update_live_hidden_kernel(
       mx = fmaxf(mx, d);
     }
     float den = 0.f;
-    for (int k = 0; k < pattern; ++k) { logit[k] = __expf(logit[k] - mx); den += logit[k]; }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k >= pattern) continue;
+      logit[k] = __expf(logit[k] - mx);
+      den += logit[k];
+    }
     const float inv = 1.f / den;
     if (lane == 0) affinity[row] = 1.f / (1.f + __expf(-mx));
     if (h_on) {
@@ -519,7 +575,9 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) update_live_hidden_kernel(
       load_vec<VPLH>(cs + h0, acc);
 #pragma unroll
       for (int j = 0; j < VPLH; ++j) acc[j] += xv[j];
-      for (int k = 0; k < pattern; ++k) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k >= pattern) continue;
         float vv[VPLH];
         load_vec<VPLH>(vs + k * hw + h0, vv);
         const float w = logit[k] * inv;
@@ -746,10 +804,26 @@ extern "C" int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride,
   if (rows <= 0) return GRS_OK;
   if (slots <= 0 || port_slots < slots) return GRS_ERR_SHAPE;
   const int grid = ceil_div(rows, ROW_WARPS);
-  GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
-      graph_aggregate_kernel<T, V><<<grid, ROW_WARPS * 32, 0, grs::counted((cudaStream_t)stream)>>>(
-          (const T*)fb, fb_stride, rel, in_node, in_port, out_node, out_port, rows, slots,
-          port_slots, width, (T*)agg, agg_stride)))
+  const int esize = dtype == GRS_DTYPE_F32 ? 4 : 2;
+  const int vpl = width / 32;
+  const int64_t vbytes = std::min<int64_t>(16, (int64_t)vpl * esize);
+  const bool vec = width % 32 == 0 && vpl >= 2 && vpl <= 16 &&
+                   reinterpret_cast<uintptr_t>(fb) % vbytes == 0 &&
+                   (fb_stride * esize) % vbytes == 0 && (width * esize) % vbytes == 0 &&
+                   reinterpret_cast<uintptr_t>(agg) % vbytes == 0 &&
+                   (agg_stride * esize) % vbytes == 0 && reinterpret_cast<uintptr_t>(rel) % 16 == 0;
+  if (vec) {
+    GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
+        graph_aggregate_vec_kernel<T, V><<<grid, ROW_WARPS * 32, 0,
+                                           grs::counted((cudaStream_t)stream)>>>(
+            (const T*)fb, fb_stride, rel, in_node, in_port, out_node, out_port, rows, slots,
+            port_slots, width, (T*)agg, agg_stride)))
+  } else {
+    GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
+        graph_aggregate_kernel<T, V><<<grid, ROW_WARPS * 32, 0, grs::counted((cudaStream_t)stream)>>>(
+            (const T*)fb, fb_stride, rel, in_node, in_port, out_node, out_port, rows, slots,
+            port_slots, width, (T*)agg, agg_stride)))
+  }
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
