@@ -43,7 +43,19 @@ struct GemmEpilogue {
   __nv_bfloat16* out;
   int64_t ldo;
   int32_t* status;
+  // residual + LayerNorm epilogue (N == 256: a whole row per tile)
+  const __nv_bfloat16* residual;
+  int64_t ldr;
+  const float* gamma;
+  const float* beta;
+  const uint8_t* zero_row;  // rows whose output is zeroed, or null
+  float eps;
 };
+
+// named barrier of the four epilogue warps that share one TMEM lane quarter
+__device__ __forceinline__ void quarter_sync(int quarter) {
+  asm volatile("bar.sync %0, 128;\n" ::"r"(1 + quarter) : "memory");
+}
 
 // erf-based GELU on fp32 pairs: Abramowitz & Stegun 7.1.28 for erfc (the
 // same form as the row kernels' GELU), packed fp32x2 multiply-adds.
@@ -66,6 +78,36 @@ __device__ __forceinline__ float2 gelu_pair(float2 x) {
                      x.y >= 0.f ? x.y * fmaf(-0.5f, ey, 1.f) : 0.5f * x.y * ey);
 }
 
+__device__ __forceinline__ void add_bias32(float v[32], const float* bias) {
+  const float4* b4 = reinterpret_cast<const float4*>(bias);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 bb = __ldg(b4 + j);
+    v[4 * j] += bb.x;
+    v[4 * j + 1] += bb.y;
+    v[4 * j + 2] += bb.z;
+    v[4 * j + 3] += bb.w;
+  }
+}
+
+// chunk c (32 columns = four 16-byte pieces) of row `lane` of a warp's
+// 32 x 64 bf16 staging block, placed by the 128-byte swizzle of the output
+// tensor map (16-byte piece index ^ row % 8)
+__device__ __forceinline__ void stage_row_chunks(uint8_t* stage, int lane, int c,
+                                                 const uint32_t packed[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int chunk = c * 4 + j;
+    *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
+        make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+  }
+}
+
+// Epilogue modes: bias (+ GELU); or bias + residual + LayerNorm over the
+// 256-column row (+ zeroing of masked rows).
+constexpr int GT_EPI_GELU = 0, GT_EPI_LAYERNORM = 1;
+
+template <int MODE>
 __global__ void __launch_bounds__(GT_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                const __grid_constant__ CUtensorMap tm_out, int M, int N, int K, GemmEpilogue e) {
@@ -147,7 +189,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
         mma_commit(&tmem_full[b]);
       }
     }
-  } else {  // epilogue warps: TMEM -> registers -> bias, GELU -> bf16 -> smem -> TMA store
+  } else if (MODE == GT_EPI_GELU) {
+    // epilogue warps: TMEM -> registers -> bias, GELU -> bf16 -> smem -> TMA store
     const int quarter = warp & 3, cgroup = (warp - 2) >> 2;   // 64 columns per warp
     uint8_t* stage = smem + GT_STAGES * GT_STAGE_BYTES + (warp - 2) * GT_OUT_BYTES;
     int i = 0;
@@ -166,17 +209,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
         const int col = cgroup * 64 + c * 32;
         float v[32];
         tmem_load32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * GT_BN + col), v);
-        if (e.bias) {
-          const float4* b4 = reinterpret_cast<const float4*>(e.bias + n0 + col);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 bb = __ldg(b4 + j);
-            v[4 * j] += bb.x;
-            v[4 * j + 1] += bb.y;
-            v[4 * j + 2] += bb.z;
-            v[4 * j + 3] += bb.w;
-          }
-        }
+        if (e.bias) add_bias32(v, e.bias + n0 + col);
         uint32_t packed[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -185,14 +218,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
           __nv_bfloat162 h = __floats2bfloat162_rn(p.x, p.y);
           packed[j] = *reinterpret_cast<uint32_t*>(&h);
         }
-        // row `lane` of the block, 16-byte chunks placed by the 128-byte
-        // swizzle the output tensor map uses (chunk ^ row % 8)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int chunk = c * 4 + j;
-          *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
-              make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-        }
+        stage_row_chunks(stage, lane, c, packed);
       }
       tc_fence_before();
       fence_async_shared();
@@ -200,6 +226,125 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       if (lane == 0) {
         mbar_arrive(&tmem_empty[b]);          // this warp is done with accumulator b
         tma_store_2d(&tm_out, stage, n0 + cgroup * 64, m0 + quarter * 32);
+      }
+    }
+    if (lane == 0) tma_store_wait_all();
+  } else {
+    // epilogue warps, LayerNorm mode: each row's 256 columns are spread over
+    // the four warps of its lane quarter; per-warp (mean, centred sum of
+    // squares) pairs meet in shared memory and merge exactly, so one pass
+    // over the accumulator gives the statistics and a second writes the row
+    __shared__ float ln_part[4][4][32], ln_m2[4][4][32];
+    const int quarter = warp & 3, cgroup = (warp - 2) >> 2;
+    uint8_t* stage = smem + GT_STAGES * GT_STAGE_BYTES + (warp - 2) * GT_OUT_BYTES;
+    int i = 0;
+    bool gave_up = false;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int m0 = t * GT_BM;                                 // N == 256: one tile per row block
+      const int b = i & 1, u = i >> 1;
+      // after a wait gave up, the warp still runs every named barrier so the
+      // other warps of its quarter are not left waiting
+      if (!gave_up && !mbar_wait(&tmem_full[b], u & 1)) {
+        gave_up = true;
+        failed = 1;
+      }
+      tc_fence_after();
+      if (lane == 0) tma_store_wait_read();
+      __syncwarp();
+      const int row = m0 + quarter * 32 + lane;
+      const bool in = row < M;
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * GT_BN);
+      // v = acc + bias + residual for one 32-column chunk
+      const auto load_row = [&](int c, float v[32]) {
+        const int col = cgroup * 64 + c * 32;
+        tmem_load32(taddr + (uint32_t)col, v);
+        add_bias32(v, e.bias + col);
+        if (in) {
+          const uint4* x4 = reinterpret_cast<const uint4*>(e.residual + (int64_t)row * e.ldr + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 w = x4[j];
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __bfloat1622float2(h[k]);
+              v[8 * j + 2 * k] += f.x;
+              v[8 * j + 2 * k + 1] += f.y;
+            }
+          }
+        }
+      };
+      // this thread's 64 columns: exact mean and centred sum of squares of
+      // each 32-column chunk, merged (Chan, Golub & LeVeque's pairwise update)
+      float mean_t = 0.f, m2_t = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        float v[32];
+        load_row(c, v);
+        float mc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mc += v[j];
+        mc *= (1.f / 32.f);
+        float m2c = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float d = v[j] - mc;
+          m2c += d * d;
+        }
+        if (c == 0) {
+          mean_t = mc;
+          m2_t = m2c;
+        } else {                       // two halves of 32: n_a n_b / n = 16
+          const float delta = mc - mean_t;
+          mean_t += 0.5f * delta;
+          m2_t += m2c + 16.f * delta * delta;
+        }
+      }
+      ln_part[quarter][cgroup][lane] = mean_t;
+      ln_m2[quarter][cgroup][lane] = m2_t;
+      quarter_sync(quarter);
+      // the row's four 64-column groups, merged pairwise the same way
+      const float* pm = &ln_part[quarter][0][lane];
+      const float* p2 = &ln_m2[quarter][0][lane];
+      const float d01 = pm[32] - pm[0], d23 = pm[96] - pm[64];
+      const float mean01 = pm[0] + 0.5f * d01, mean23 = pm[64] + 0.5f * d23;
+      const float m201 = p2[0] + p2[32] + 32.f * d01 * d01;
+      const float m223 = p2[64] + p2[96] + 32.f * d23 * d23;
+      const float dd = mean23 - mean01;
+      const float mean = mean01 + 0.5f * dd;
+      const float var = (m201 + m223 + 64.f * dd * dd) * (1.f / GT_BN);
+      quarter_sync(quarter);
+      const float rstd = rsqrtf(var + e.eps);
+      const bool keep = !in || e.zero_row == nullptr || e.zero_row[row] != 0;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int col = cgroup * 64 + c * 32;
+        float v[32];
+        load_row(c, v);
+        uint32_t packed[16];
+        const float4* g4 = reinterpret_cast<const float4*>(e.gamma + col);
+        const float4* b4 = reinterpret_cast<const float4*>(e.beta + col);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 g = __ldg(g4 + j), bb = __ldg(b4 + j);
+          float r[4] = {(v[4 * j] - mean) * rstd * g.x + bb.x,
+                        (v[4 * j + 1] - mean) * rstd * g.y + bb.y,
+                        (v[4 * j + 2] - mean) * rstd * g.z + bb.z,
+                        (v[4 * j + 3] - mean) * rstd * g.w + bb.w};
+          if (!keep) r[0] = r[1] = r[2] = r[3] = 0.f;
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(r[0], r[1]);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(r[2], r[3]);
+          packed[2 * j] = *reinterpret_cast<uint32_t*>(&h0);
+          packed[2 * j + 1] = *reinterpret_cast<uint32_t*>(&h1);
+        }
+        stage_row_chunks(stage, lane, c, packed);
+      }
+      tc_fence_before();
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&tmem_empty[b]);
+        tma_store_2d(&tm_out, stage, cgroup * 64, m0 + quarter * 32);
       }
     }
     if (lane == 0) tma_store_wait_all();
@@ -274,33 +419,66 @@ bool gemm_map(CUtensorMap* out, const void* base, int64_t rows, int64_t cols, in
 
 using namespace grs;
 
-extern "C" int grs_gemm_bf16_epilogue(const void* a, int64_t lda, const void* b, int64_t ldb,
-                                      int M, int N, int K, const float* bias, int gelu,
-                                      void* out, int64_t ldo, int32_t* status, void* stream) {
+namespace grs {
+namespace {
+
+int launch_gemm(int mode, const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N,
+                int K, void* out, int64_t ldo, const GemmEpilogue& e, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0 || K % GT_BK || N % GT_BN || lda % 8 || ldb % 8 || ldo % 8 ||
       lda < K || ldb < K || ldo < N)
     return GRS_ERR_SHAPE;
   if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
-       reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(bias)) & 15)
+       reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(e.bias)) & 15)
     return GRS_ERR_SHAPE;
   CUtensorMap tm_a, tm_b, tm_out;
   if (!gemm_map(&tm_a, a, M, K, lda, GT_BM) || !gemm_map(&tm_b, b, N, K, ldb, GT_BN) ||
       !gemm_map(&tm_out, out, M, N, ldo, 32))
     return GRS_ERR_SHAPE;
-  static bool attr[64] = {};
+  static bool attr[2][64] = {};
+  static int sms[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr[dev]) {
-    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GT_SMEM);
-    attr[dev] = true;
+  if (dev < 64 && !attr[mode][dev]) {
+    cudaFuncSetAttribute(mode == GT_EPI_GELU ? gemm_tc_kernel<GT_EPI_GELU>
+                                             : gemm_tc_kernel<GT_EPI_LAYERNORM>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, GT_SMEM);
+    attr[mode][dev] = true;
   }
-  GemmEpilogue e{bias, gelu, static_cast<__nv_bfloat16*>(out), ldo, status};
-  static int sms[64] = {};
   if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int64_t tiles = (int64_t)((M + GT_BM - 1) / GT_BM) * (N / GT_BN);
   const int grid = (int)std::min<int64_t>(tiles, dev < 64 && sms[dev] ? sms[dev] : 148);
-  gemm_tc_kernel<<<grid, GT_THREADS, GT_SMEM, counted((cudaStream_t)stream)>>>(tm_a, tm_b, tm_out,
-                                                                               M, N, K, e);
+  if (mode == GT_EPI_GELU)
+    gemm_tc_kernel<GT_EPI_GELU><<<grid, GT_THREADS, GT_SMEM, counted(stream)>>>(
+        tm_a, tm_b, tm_out, M, N, K, e);
+  else
+    gemm_tc_kernel<GT_EPI_LAYERNORM><<<grid, GT_THREADS, GT_SMEM, counted(stream)>>>(
+        tm_a, tm_b, tm_out, M, N, K, e);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
+}
+
+}  // namespace
+}  // namespace grs
+
+extern "C" int grs_gemm_bf16_epilogue(const void* a, int64_t lda, const void* b, int64_t ldb,
+                                      int M, int N, int K, const float* bias, int gelu,
+                                      void* out, int64_t ldo, int32_t* status, void* stream) {
+  GemmEpilogue e{bias, gelu, static_cast<__nv_bfloat16*>(out), ldo, status,
+                 nullptr, 0, nullptr, nullptr, nullptr, 0.f};
+  return launch_gemm(GT_EPI_GELU, a, lda, b, ldb, M, N, K, out, ldo, e, (cudaStream_t)stream);
+}
+
+extern "C" int grs_gemm_bf16_layernorm(const void* a, int64_t lda, const void* b, int64_t ldb,
+                                       int M, int K, const float* bias, const void* residual,
+                                       int64_t ldr, const float* gamma, const float* beta,
+                                       const uint8_t* zero_row, float eps, void* out,
+                                       int64_t ldo, int32_t* status, void* stream) {
+  if (bias == nullptr || residual == nullptr || gamma == nullptr || beta == nullptr ||
+      ldr % 8 || (reinterpret_cast<uintptr_t>(residual) & 15) ||
+      (reinterpret_cast<uintptr_t>(gamma) & 15) || (reinterpret_cast<uintptr_t>(beta) & 15))
+    return GRS_ERR_SHAPE;
+  GemmEpilogue e{bias, 0, static_cast<__nv_bfloat16*>(out), ldo, status,
+                 static_cast<const __nv_bfloat16*>(residual), ldr, gamma, beta, zero_row, eps};
+  return launch_gemm(GT_EPI_LAYERNORM, a, lda, b, ldb, M, GT_BN, K, out, ldo, e,
+                     (cudaStream_t)stream);
 }

@@ -224,3 +224,18 @@ def gemm_bias_gelu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | N
         x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), x.shape[0],
         weight.shape[0], x.shape[1], _p(bias), int(gelu), out.data_ptr(), out.stride(0),
         _p(status), stream())
+
+
+def gemm_residual_layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                            residual: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+                            zero_row: torch.Tensor | None, out: torch.Tensor,
+                            status: torch.Tensor | None = None, eps: float = 1e-5) -> int:
+    """out = LayerNorm(residual + x @ weight.T + bias) * gamma + beta (rows
+    with zero_row == 0 zeroed) on the tensor cores in one pass; weight is a
+    K-major [256, K] Linear weight, bf16.  Returns the library status
+    (GRS_ERR_SHAPE, -4, when nothing was launched)."""
+    return _lib.lib().grs_gemm_bf16_layernorm(
+        x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), x.shape[0], x.shape[1],
+        bias.data_ptr(), residual.data_ptr(), residual.stride(0), gamma.data_ptr(),
+        beta.data_ptr(), _p(zero_row), eps, out.data_ptr(), out.stride(0), _p(status),
+        stream())

@@ -232,8 +232,10 @@ class PagedActionBindingModel(nn.Module):
                                              layer.backward_message.weight), 0))
                 w[p + "rel"] = f(layer.relation.weight)
                 w[p + "u0_t"], w[p + "u0_b"] = t(layer.update[0].weight), f(layer.update[0].bias)
-                if dt == torch.bfloat16:   # K-major operand of the tensor-core GEMM
+                if dt == torch.bfloat16:   # K-major operands of the tensor-core GEMMs
                     w[p + "u0_k"] = c(layer.update[0].weight)
+                    w[p + "u2_k"] = c(layer.update[2].weight)
+                    w[p + "u2_bf"] = c(layer.update[2].bias).float()
                 w[p + "u2_t"], w[p + "u2_b"] = t(layer.update[2].weight), c(layer.update[2].bias)
                 w[p + "norm_w"], w[p + "norm_b"] = f(layer.norm.weight), f(layer.norm.bias)
         if self.readout_graph_layers_count:
@@ -309,10 +311,13 @@ class PagedActionBindingModel(nn.Module):
             if not self._fused_update(x_buf, w.get(p + "u0_k"), w[p + "u0_b"], hidden):
                 K.linear(x_buf, w[p + "u0_t"], out=hidden)
                 K.bias_gelu(hidden, w[p + "u0_b"])
-            K.linear(hidden, w[p + "u2_t"], w[p + "u2_b"], out=upd)
             target = spare.pop(0)
-            K.add_layernorm(x, upd, gamma=w[p + "norm_w"], beta=w[p + "norm_b"],
-                            ln_out=target[:, :W], zero_row=live_flat)
+            if not self._fused_update_norm(hidden, w.get(p + "u2_k"), w.get(p + "u2_bf"), x,
+                                           w[p + "norm_w"], w[p + "norm_b"], live_flat,
+                                           target[:, :W]):
+                K.linear(hidden, w[p + "u2_t"], w[p + "u2_b"], out=upd)
+                K.add_layernorm(x, upd, gamma=w[p + "norm_w"], beta=w[p + "norm_b"],
+                                ln_out=target[:, :W], zero_row=live_flat)
             if not (keep_input and i == 0):
                 spare.append(x_buf)
             x_buf = target
@@ -335,6 +340,23 @@ class PagedActionBindingModel(nn.Module):
         if code == -4:                       # GRS_ERR_SHAPE: nothing launched
             return False
         _lib.check(code, "tensor-core GEMM")
+        return True
+
+    def _fused_update_norm(self, hidden, weight_k, bias, residual, gamma, beta, zero_row,
+                           out) -> bool:
+        """out = LayerNorm(residual + hidden @ u2^T + b) (dead rows zeroed)
+        in one tensor-core pass; False when the caller must run the GEMM and
+        the add+LayerNorm separately."""
+        if weight_k is None or hidden.shape[0] < self.FUSED_MIN_ROWS:
+            return False
+        status = getattr(self, "kernel_status", None)
+        if status is None:
+            status = _status_word(hidden.device)
+        code = K.gemm_residual_layernorm(hidden, weight_k, bias, residual, gamma, beta, zero_row,
+                                         out, status)
+        if code == -4:                       # GRS_ERR_SHAPE: nothing launched
+            return False
+        _lib.check(code, "tensor-core GEMM + LayerNorm")
         return True
 
     def _ports(self, batch: dict, b: int, s: int, device):

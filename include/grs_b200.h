@@ -393,6 +393,18 @@ GRS_API int grs_topology_fingerprint(const int64_t* types, const int32_t* out_no
 GRS_API int grs_gemm_bf16_epilogue(const void* a, int64_t lda, const void* b, int64_t ldb, int M,
                                    int N, int K, const float* bias, int gelu, void* out,
                                    int64_t ldo, int32_t* status, void* stream);
+/* The same tensor-core GEMM with N = 256 and a residual + LayerNorm epilogue
+ * (the readout graph layers' u2 projection and their add+LayerNorm,
+ * model.py:26-53):  s = residual[M, 256] + A . B^T + bias;  out = (s - mean(s))
+ * / sqrt(var(s) + eps) * gamma + beta, rows with zero_row[r] == 0 written as
+ * zeros (zero_row may be null).  fp32 statistics, two-pass variance; bias,
+ * gamma, beta fp32 [256]; residual bf16 with row stride ldr.  GRS_ERR_SHAPE
+ * for shapes or alignments the kernel does not take. */
+GRS_API int grs_gemm_bf16_layernorm(const void* a, int64_t lda, const void* b, int64_t ldb, int M,
+                                    int K, const float* bias, const void* residual, int64_t ldr,
+                                    const float* gamma, const float* beta, const uint8_t* zero_row,
+                                    float eps, void* out, int64_t ldo, int32_t* status,
+                                    void* stream);
 
 /* ---- beam search sharded over the GPUs of a node ---------------------------
  * The reference ranks a level's proposals globally
