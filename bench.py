@@ -8,11 +8,13 @@ and checkpoint are not available):
 
 * ``rollout`` (default): the full beam-search step - synthetic 6-qubit,
   259-gate circuit, width-256 / 8-head / 4 causal + 4 readout-graph-layer
-  model with seeded random weights, bf16, beam 1000, depth 64 (W warm-up
-  levels then K timed levels; defaults 4 + 60), page 16, 80 candidates per
-  state ranked to 16 per parent and 16000 globally.  A step is one search
-  level.  The decode-attention microbenchmark below is measured in the same
-  run and reported under ``paged_attention``.
+  model with seeded random weights, bf16, beam 1000 per GPU, depth W + K
+  (defaults 4 + 60), page 16, up to 2048 candidates per state ranked to 16
+  per parent and 16000 globally.  A step is one search level.  One whole
+  untimed search of the same depth runs first, then W warm-up levels and K
+  timed levels of a fresh search.  With N > 1 the beam is sharded (1000 beams
+  per GPU, weak scaling).  The decode-attention microbenchmark below is
+  measured in the same run and reported under ``paged_attention``.
 * ``update-gemm``: the readout graph layers' update projection with its GELU
   as one tcgen05 tensor-core launch, GELU(x [300000, 512] @ W^T + b), against
   the library GEMM + bias+GELU pair on the same inputs.
@@ -21,14 +23,16 @@ and checkpoint are not available):
   keys, 64 action K/V entries per beam in pages of 16, block tables from a
   random prefix tree.  A step is one decode-attention launch over all beams.
 
-Timing: W untimed warm-up steps, then K timed steps; before every timed step
-a 256 MiB buffer is written to flush L2; each step is bracketed by CUDA events
-on the launching stream, with barrier + synchronize around the timed region
-and the max over ranks.  ``e2e`` repeats the step through the public Python
-API with the per-step inputs copied from pinned host memory and the result
-copied back, inside the timed region.  Clocks are sampled with nvidia-smi
-during the timed region.  ``--impl reference`` times the CPU oracle (the
-reference's algorithm restated on the host) on the same workload.
+Timing: each timed step is bracketed by CUDA events on the launching stream,
+with barrier + synchronize around the timed region and the max over ranks.
+Every workload reads inputs larger than L2 each step: the rollout's beam
+state (hundreds of MB of bf16 activations per level), the decode benchmark's
+16 rotating input sets, the GEMM's two rotating 307 MB inputs.  ``e2e`` runs
+the workload through the public Python API with host inputs and host
+results inside the timed region (the rollout: ``DeviceBeamSearch.run()`` from
+the host circuit to the host beam summary).  Clocks are sampled with
+nvidia-smi during the timed region.  ``--impl reference`` times the CPU
+oracle (the reference's algorithm restated on the host) on the same workload.
 """
 from __future__ import annotations
 
