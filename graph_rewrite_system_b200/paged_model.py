@@ -523,6 +523,7 @@ class PagedActionBindingModel(nn.Module):
 
     # ---- the per-beam token path of one step (CUDA graph per shape) ------------
     USE_GRAPHS = True
+    GRAPH_CACHE_LIMIT = 16   # captured token-step graphs kept (least recently used dropped)
 
     def _token_step_eager(self, ctx_in, active, past_lengths, block_table, key_cache,
                           value_cache):
@@ -580,13 +581,19 @@ class PagedActionBindingModel(nn.Module):
         version = self._version_key()
         graphs = getattr(self, "_graphs", None)
         if graphs is None or graphs[0] != version:
+            if graphs is not None and graphs[1]:
+                torch.cuda.synchronize(ctx_in.device)   # no replay of a dropped graph pending
             graphs = self._graphs = (version, {})
         key = (ctx_in.shape[0], block_table.shape[1], ctx_in.dtype, key_cache.data_ptr(),
                value_cache.data_ptr(), ctx_in.device)
-        entry = graphs[1].get(key)
+        entry = graphs[1].pop(key, None)
         inputs = (ctx_in, active, past_lengths, block_table)
         if entry is None:
-            entry = graphs[1][key] = self._capture_token_step(inputs, key_cache, value_cache)
+            if len(graphs[1]) >= self.GRAPH_CACHE_LIMIT:
+                torch.cuda.synchronize(ctx_in.device)
+                graphs[1].pop(next(iter(graphs[1])))    # least recently used
+            entry = self._capture_token_step(inputs, key_cache, value_cache)
+        graphs[1][key] = entry                          # most recently used last
         static, graph, outs, launches = entry
         for dst, src in zip(static, inputs):
             dst.copy_(src)

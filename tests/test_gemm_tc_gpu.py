@@ -113,3 +113,35 @@ def test_gemm_layernorm_matches_torch(m, k, masked):
     err = (out.float() - ref).abs().max().item()
     assert err <= 3e-2 * max(1.0, ref.abs().max().item()), err
     assert torch.isnan(out_buf[:, :256].float()).all()          # left half untouched
+
+
+def test_graphed_token_step_matches_eager_with_eviction():
+    """The per-beam token path replayed from captured CUDA graphs equals the
+    eager path on the same inputs, while beam counts cycle through more
+    shapes than the graph cache keeps (so graphs are evicted and captured
+    again)."""
+    import bench
+
+    search, _ = bench.build_rollout(DEV, beam_size=8, depth=4)
+    model, cache = search.model, search.cache
+    model.GRAPH_CACHE_LIMIT = 2
+    try:
+        g = torch.Generator(device=DEV).manual_seed(11)
+        W, cols = model.width, 4
+        for b in (5, 9, 13, 5, 9, 13, 9):
+            ctx = torch.randn(b, 3 * W, device=DEV, generator=g).to(model.compute_dtype)
+            active = torch.rand(b, device=DEV, generator=g) > 0.2
+            lengths = torch.randint(0, cols * cache.page_size, (b,), device=DEV, generator=g,
+                                    dtype=torch.int32)
+            table = torch.randint(0, cache.capacity, (b, cols), device=DEV, generator=g,
+                                  dtype=torch.int32)
+            eager = model._token_step_eager(ctx, active, lengths, table, cache.keys, cache.values)
+            eager = [t.clone() for t in eager]
+            graphed = model._token_step(ctx, active, lengths, table, cache.keys, cache.values)
+            torch.cuda.synchronize()
+            for a, z in zip(eager, graphed):
+                scale = max(1.0, a.float().abs().max().item())
+                assert (a.float() - z.float()).abs().max().item() <= 1e-2 * scale
+            assert len(model._graphs[1]) <= 2
+    finally:
+        del model.GRAPH_CACHE_LIMIT
