@@ -389,6 +389,37 @@ __device__ __forceinline__ void store_vec(float* p, const float* v) {
 
 constexpr int ULH_ROWS = 64;   // slot rows of one beam per CTA
 
+// Lane-interleaved shared-memory rows for per-lane chunks of V floats (V a
+// multiple of 4, row length 32 V): float4 j of lane L sits at float4 index
+// j * 32 + L, so a warp's 16-byte loads of one j hit 32 consecutive float4s
+// (no bank conflicts; the plain layout puts lanes V floats apart, which maps
+// up to 16 lanes onto the same four banks).
+template <int V>
+__device__ __forceinline__ void lds_interleaved(const float* row, int lane, float* out) {
+#pragma unroll
+  for (int j = 0; j < V / 4; ++j) {
+    const float4 f = reinterpret_cast<const float4*>(row)[j * 32 + lane];
+    out[4 * j] = f.x;
+    out[4 * j + 1] = f.y;
+    out[4 * j + 2] = f.z;
+    out[4 * j + 3] = f.w;
+  }
+}
+// rows of 32 V elements from global memory into that layout, as fp32
+template <int V, typename T>
+__device__ __forceinline__ void stage_interleaved(float* dst, const T* src, int rows) {
+  const int n = rows * 32 * V;
+  for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) {
+    const int row = i / (32 * V), e = i - row * 32 * V;
+    float4 f;
+    f.x = to_float(src[i]);
+    f.y = to_float(src[i + 1]);
+    f.z = to_float(src[i + 2]);
+    f.w = to_float(src[i + 3]);
+    reinterpret_cast<float4*>(dst + row * 32 * V)[((e % V) / 4) * 32 + e / V] = f;
+  }
+}
+
 // _update_live_nodes hidden layer (paged_model.py:223-238), per slot row:
 //   logits_k = q . key[b,k] / sqrt(W) (masked -1e4), attn = softmax_k,
 //   affinity = sigmoid(max_k logits),
@@ -514,7 +545,7 @@ template <typename T, int VPLQ, int VPLH>
 __global__ void __launch_bounds__(ROW_WARPS * 32, 4) update_live_hidden_kernel(
     const T* qxa, int64_t qxa_stride, const T* keys, const T* vw, const T* cvec,
     const uint8_t* source_mask, int pattern, int slots, int width, T* hidden,
-    int64_t hidden_stride, float* affinity) {
+    int64_t hidden_stride, float* affinity, int interleave) {
   extern __shared__ __align__(16) float ulh_smem[];
   const int hw = 2 * width;
   float* ks = ulh_smem;                          // [pattern][width]
@@ -522,11 +553,21 @@ __global__ void __launch_bounds__(ROW_WARPS * 32, 4) update_live_hidden_kernel(
   float* cs = vs + pattern * hw;                 // [2W]
   __shared__ bool s_mask[8];
   const int64_t b = blockIdx.y;
-  for (int i = threadIdx.x; i < pattern * width; i += blockDim.x)
-    ks[i] = to_float(keys[b * pattern * width + i]);
-  for (int i = threadIdx.x; i < pattern * hw; i += blockDim.x)
-    vs[i] = to_float(vw[b * pattern * hw + i]);
-  for (int i = threadIdx.x; i < hw; i += blockDim.x) cs[i] = to_float(cvec[b * hw + i]);
+  // `interleave` (width == 32 VPLQ, 2 width == 32 VPLH, both multiples of
+  // 4): the lane-interleaved layout; otherwise rows as they are
+  constexpr bool kCanInterleave = VPLQ % 4 == 0 && VPLH % 4 == 0;
+  const bool inter = kCanInterleave && interleave;
+  if (inter) {
+    stage_interleaved<(kCanInterleave ? VPLQ : 4)>(ks, keys + b * pattern * width, pattern);
+    stage_interleaved<(kCanInterleave ? VPLH : 4)>(vs, vw + b * pattern * hw, pattern);
+    stage_interleaved<(kCanInterleave ? VPLH : 4)>(cs, cvec + b * hw, 1);
+  } else {
+    for (int i = threadIdx.x; i < pattern * width; i += blockDim.x)
+      ks[i] = to_float(keys[b * pattern * width + i]);
+    for (int i = threadIdx.x; i < pattern * hw; i += blockDim.x)
+      vs[i] = to_float(vw[b * pattern * hw + i]);
+    for (int i = threadIdx.x; i < hw; i += blockDim.x) cs[i] = to_float(cvec[b * hw + i]);
+  }
   if (threadIdx.x < pattern) s_mask[threadIdx.x] = source_mask[b * pattern + threadIdx.x] != 0;
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -552,7 +593,12 @@ __global__ void __launch_bounds__(ROW_WARPS * 32, 4) update_live_hidden_kernel(
       float d = 0.f;
       if (q_on) {
         float kv[VPLQ];
-        load_vec<VPLQ>(ks + k * width + q0, kv);
+        if constexpr (kCanInterleave) {
+          if (inter) lds_interleaved<VPLQ>(ks + k * width, lane, kv);
+          else load_vec<VPLQ>(ks + k * width + q0, kv);
+        } else {
+          load_vec<VPLQ>(ks + k * width + q0, kv);
+        }
 #pragma unroll
         for (int j = 0; j < VPLQ; ++j) d += qv[j] * kv[j];
       }
@@ -572,14 +618,24 @@ __global__ void __launch_bounds__(ROW_WARPS * 32, 4) update_live_hidden_kernel(
     if (lane == 0) affinity[row] = 1.f / (1.f + __expf(-mx));
     if (h_on) {
       float acc[VPLH];
-      load_vec<VPLH>(cs + h0, acc);
+      if constexpr (kCanInterleave) {
+        if (inter) lds_interleaved<VPLH>(cs, lane, acc);
+        else load_vec<VPLH>(cs + h0, acc);
+      } else {
+        load_vec<VPLH>(cs + h0, acc);
+      }
 #pragma unroll
       for (int j = 0; j < VPLH; ++j) acc[j] += xv[j];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         if (k >= pattern) continue;
         float vv[VPLH];
-        load_vec<VPLH>(vs + k * hw + h0, vv);
+        if constexpr (kCanInterleave) {
+          if (inter) lds_interleaved<VPLH>(vs + k * hw, lane, vv);
+          else load_vec<VPLH>(vs + k * hw + h0, vv);
+        } else {
+          load_vec<VPLH>(vs + k * hw + h0, vv);
+        }
         const float w = logit[k] * inv;
 #pragma unroll
         for (int j = 0; j < VPLH; ++j) acc[j] += w * vv[j];
@@ -872,6 +928,7 @@ extern "C" int grs_update_live_hidden(int dtype, const void* qxa, int64_t qxa_st
   const size_t smem = (size_t)(3 * pattern + 2) * width * sizeof(float);
   if (smem > 160 * 1024) return GRS_ERR_SHAPE;
   const dim3 grid(ceil_div(slots, ULH_ROWS), (unsigned)(rows / slots));
+  const int interleave = width == 32 * vq && 2 * width == 32 * vh && vq % 4 == 0 && vh % 4 == 0;
 #define GRS_ULH(VQ, VH)                                                                        \
   if (vq == VQ && vh == VH) {                                                                  \
     GRS_DTYPE_SWITCH(T, dtype,                                                                 \
@@ -880,7 +937,7 @@ extern "C" int grs_update_live_hidden(int dtype, const void* qxa, int64_t qxa_st
         update_live_hidden_kernel<T, VQ, VH><<<grid, ROW_WARPS * 32, smem,                     \
                                                grs::counted((cudaStream_t)stream)>>>(          \
         (const T*)qxa, qxa_stride, (const T*)keys, (const T*)vw, (const T*)cvec, source_mask,  \
-        pattern, slots, width, (T*)hidden, hidden_stride, affinity))                            \
+        pattern, slots, width, (T*)hidden, hidden_stride, affinity, interleave))                \
     GRS_CUDA_CHECK_LAUNCH();                                                                   \
     return GRS_OK;                                                                             \
   }
