@@ -8,11 +8,12 @@ and checkpoint are not available):
 
 * ``rollout`` (default): the full beam-search step - synthetic 6-qubit,
   259-gate circuit, width-256 / 8-head / 4 causal + 4 readout-graph-layer
-  model with seeded random weights, bf16, beam 1000 per GPU, depth W + K
-  (defaults 4 + 60), page 16, up to 2048 candidates per state ranked to 16
-  per parent and 16000 globally.  A step is one search level.  One whole
-  untimed search of the same depth runs first, then W warm-up levels and K
-  timed levels of a fresh search.  With N > 1 the beam is sharded (1000 beams
+  model with seeded random weights, bf16, beam 1000 per GPU, depth 64 (the
+  metric's T), page 16, up to 2048 candidates per state ranked to 16 per
+  parent and 16000 globally.  A step is one search level.  One whole untimed
+  64-level search runs first; then a fresh 64-level search whose last K
+  levels are timed (levels 65-K..64; the 64-K levels before them, at least
+  W, are the untimed warm-up).  With N > 1 the beam is sharded (1000 beams
   per GPU, weak scaling).  The decode-attention microbenchmark below is
   measured in the same run and reported under ``paged_attention``.
 * ``update-gemm``: the readout graph layers' update projection with its GELU
@@ -29,8 +30,10 @@ Every workload reads inputs larger than L2 each step: the rollout's beam
 state (hundreds of MB of bf16 activations per level), the decode benchmark's
 16 rotating input sets, the GEMM's two rotating 307 MB inputs.  ``e2e`` runs
 the workload through the public Python API with host inputs and host
-results inside the timed region (the rollout: ``DeviceBeamSearch.run()`` from
-the host circuit to the host beam summary).  Clocks are sampled with
+results inside the timed region (the rollout: the same K levels of another
+fresh search, each ``DeviceBeamSearch.step()`` plus the level's children
+copied to pinned host memory; ``e2e_full_search`` adds the whole
+``run()`` from the host circuit to the host beam summary).  Clocks are sampled with
 nvidia-smi during the timed region.  ``--impl reference`` times the CPU
 oracle (the reference's algorithm restated on the host) on the same workload.
 """
@@ -82,12 +85,12 @@ def measured_peaks() -> dict:
 class KernelProbe:
     """Times every `every`-th call of one kernel wrapper of
     graph_rewrite_system_b200.kernels with CUDA events on the launching stream
-    while active, and adds up those calls' algorithmic bytes (sampling keeps
-    the probe's own device time out of most of the step)."""
+    while active, and adds up those calls' algorithmic bytes and FLOPs
+    (sampling keeps the probe's own device time out of most of the step)."""
 
-    def __init__(self, name: str, bytes_fn, every: int = 4):
-        self.name, self.bytes_fn, self.every = name, bytes_fn, every
-        self.events, self.bytes, self.rows, self.calls = [], 0, 0, 0
+    def __init__(self, name: str, work_fn, every: int = 4):
+        self.name, self.work_fn, self.every = name, work_fn, every
+        self.events, self.bytes, self.flops, self.calls = [], 0, 0, 0
 
     def __enter__(self):
         from graph_rewrite_system_b200 import kernels
@@ -107,9 +110,9 @@ class KernelProbe:
             out = self.original(*a, **kw)
             end.record()
             self.events.append((start, end))
-            nbytes, rows = self.bytes_fn(*a, **kw)
+            nbytes, flops = self.work_fn(*a, **kw)
             self.bytes += nbytes
-            self.rows += rows
+            self.flops += flops
             return out
 
         setattr(kernels, self.name, timed)
@@ -119,33 +122,39 @@ class KernelProbe:
         setattr(self.module, self.name, self.original)
 
     def roofline(self, peaks: dict, kernel: str, traffic_ratio) -> dict | None:
-        """`traffic_ratio`: DRAM bytes / algorithmic bytes of this kernel from
-        a committed ncu capture (None when absent)."""
+        """Tensor-pipe roofline (FLOPs) with the HBM fraction beside it.
+        `traffic_ratio`: DRAM bytes / algorithmic bytes of this kernel from a
+        committed ncu capture (None when absent)."""
         if not self.events:
             return None
         torch.cuda.synchronize()
         n = len(self.events)
         ms = sum(s.elapsed_time(e) for s, e in self.events) / n
-        per_launch = self.bytes / n
-        achieved = per_launch / (ms * 1e-3) / 1e9
-        traffic = traffic_ratio * per_launch if traffic_ratio else None
-        return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                "kernel": kernel, "launches": n, "sampled_every": self.every, "avg_launch_ms": ms,
-                "algorithmic_bytes_per_launch": per_launch,
-                "peak_source": f"{peaks['source']} hbm_gbs"}
+        flops, nbytes = self.flops / n, self.bytes / n
+        achieved = flops / (ms * 1e-3) / 1e12
+        peak = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "traffic": traffic_ratio * nbytes if traffic_ratio else None,
+                "kernel": kernel, "launches": n, "sampled_every": self.every,
+                "avg_launch_ms": ms, "algorithmic_flops_per_launch": flops,
+                "algorithmic_bytes_per_launch": nbytes,
+                "hbm_achieved_gbs": nbytes / (ms * 1e-3) / 1e9,
+                "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside "
+                               f"the long search step); HBM: {peaks['source']} hbm_gbs"}
 
 
-def add_layernorm_bytes(x, y=None, *, scale=None, gamma=None, beta=None, sum_out=None,
-                        ln_out=None, zero_row=None, **_):
-    """Residual add + LayerNorm over rows of x: read x (and y), write the sum
-    and/or the normalised rows, read the per-row scale / mask and gamma, beta."""
-    rows, width, es = x.shape[0], x.shape[-1], x.element_size()
-    nbytes = rows * width * es * (1 + (y is not None) + (sum_out is not None)
-                                  + (ln_out is not None))
-    nbytes += rows * ((scale is not None) * 4 + (zero_row is not None))
-    nbytes += width * 4 * ((gamma is not None) + (beta is not None))
-    return nbytes, rows
+def gemm_work(x, weight, bias=None, *, gelu=False, residual=None, zero_row=None, out=None,
+              status=None):
+    """Algorithmic bytes and FLOPs of one kernels.gemm call: read x, the
+    weight, the bias and the residual once, write the output; 2 M N K."""
+    m, k = x.shape
+    n = weight.shape[0]
+    nbytes = 2 * (m * k + n * k + m * n) + (4 * n if bias is not None else 0)
+    nbytes += 2 * m * n if residual is not None else 0
+    nbytes += m if zero_row is not None else 0
+    return nbytes, 2.0 * m * n * k
 
 
 def launch_count() -> int:
@@ -437,66 +446,122 @@ def build_rollout(device, *, beam_size=1000, depth=64, seed=0, world=1, qubits=6
     return DeviceBeamSearch(model, rules, circuit, rc, device), rc
 
 
+ROLLOUT_DEPTH = 64                      # the metric's T: every rollout search is 64 levels deep
+
+
+def rollout_window(steps: int, warmup: int) -> tuple[int, int]:
+    """(timed levels, first timed level) of the 64-level search: its last
+    `steps` levels, after at least `warmup` untimed ones."""
+    steps = max(1, min(steps, ROLLOUT_DEPTH - warmup))
+    return steps, ROLLOUT_DEPTH - steps + 1
+
+
 def run_rollout(args, world, rank, device):
     from graph_rewrite_system_b200.rollout import StageTimer
 
-    depth = args.warmup + args.steps
+    depth = ROLLOUT_DEPTH
+    steps, first = rollout_window(args.steps, args.warmup)
     search, rc = build_rollout(device, beam_size=args.beam, depth=depth, seed=0, world=world,
                                qubits=args.qubits, gates=args.gates)
     stream = torch.cuda.current_stream(device)
     # one full untimed search first (module load; the caching allocator and
     # NCCL meet every buffer size of the timed levels once)
     search.run(depth)
+    # the timed search: levels 1 .. first-1 untimed (they include the
+    # warm-up), levels first .. 64 timed one by one
     search.reset()
-    for _ in range(args.warmup):
-        search.step()
+    for _ in range(first - 1):
+        if search.step() is None:
+            raise RuntimeError(f"the search ended before level {first}")
     torch.cuda.synchronize(device)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    timer = StageTimer()
-    search.timer = timer
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     barrier(world, device)
     torch.cuda.synchronize(device)
     done = 0
     launches0 = launch_count()
     moved0 = (getattr(search, "moved_children", 0), getattr(search, "moved_bytes", 0))
-    probe = KernelProbe("add_layernorm", add_layernorm_bytes)
+    probe = KernelProbe("gemm", gemm_work)
     with ClockSampler(device.index) as clocks, probe:
-        for i in range(args.steps):
+        # NVTX range "timed_levels": lets a profiler restrict itself to the
+        # timed window (ncu --nvtx --nvtx-include "timed_levels/")
+        torch.cuda.nvtx.range_push("timed_levels")
+        for i in range(steps):
             starts[i].record(stream)
             row = search.step()
             ends[i].record(stream)
             done += 1
             if row is None:
                 break
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(device)
     launches = launch_count() - launches0
     moved = (getattr(search, "moved_children", 0) - moved0[0],
              getattr(search, "moved_bytes", 0) - moved0[1])
-    timer.collect()
-    search.timer = None
     barrier(world, device)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts[:done], ends[:done])]
     total_ms = max_over_ranks(sum(step_ms), world, device)
     search.check()
     rows = search.rows
     last = rows[-1]
-    # end to end through the public API: host circuit in, full search, beam summary out
-    e2e_start = torch.cuda.Event(enable_timing=True)
-    e2e_end = torch.cuda.Event(enable_timing=True)
+    window = f"{first}..{first + done - 1}"
+
+    # end to end through the public API over the same window: a fresh search
+    # (the host circuit uploaded at reset), the levels before the window
+    # untimed, then every timed level is step() (with its host read of the
+    # level summary) plus the level's children - parent, xfer, source and
+    # destination slots, gate count - copied into pinned host memory
+    search.reset()
+    for _ in range(first - 1):
+        search.step()
     torch.cuda.synchronize(device)
     barrier(world, device)
-    e2e_start.record(stream)
+    e2e_start = torch.cuda.Event(enable_timing=True)
+    e2e_end = torch.cuda.Event(enable_timing=True)
+    d2h_actions = 0
+    e2e_done = 0
+    with ClockSampler(device.index):      # the same host conditions as the timed window
+        e2e_start.record(stream)
+        for _ in range(done):
+            if search.step() is None:
+                break
+            d2h_actions += search.level_actions_host()["nbytes"]
+            e2e_done += 1
+        e2e_end.record(stream)
+        torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world, device)
+    search.check()
+    # where a level's time goes: CUDA events at the stage boundaries of the
+    # same levels in one more search (kept out of the timed window)
+    search.reset()
+    for _ in range(first - 1):
+        search.step()
+    timer = StageTimer()
+    search.timer = timer
+    barrier(world, device)
+    for _ in range(done):
+        if search.step() is None:
+            break
+    torch.cuda.synchronize(device)
+    timer.collect()
+    search.timer = None
+    search.check()
+    summary_bytes = 12 * 8                 # the per-level summary words step() reads
+    # the whole public call: host circuit in, 64 levels, beam summary out
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    full_start = torch.cuda.Event(enable_timing=True)
+    full_end = torch.cuda.Event(enable_timing=True)
+    full_start.record(stream)
     search.run(depth)
     if world > 1:
         summary = {"gate_count": search.global_fingerprints()}
     else:
         summary = search.beam_summary()
-    e2e_end.record(stream)
+    full_end.record(stream)
     torch.cuda.synchronize(device)
-    e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world, device)
-    h2d = (len(search.circuit.nodes) * 2 + len(search.circuit.edges) * 4) * 8
-    d2h = 11 * 8 + len(summary["gate_count"]) * 8 * 4 // max(1, depth)
+    full_ms = max_over_ranks(full_start.elapsed_time(full_end), world, device)
+    full_h2d = (len(search.circuit.nodes) * 2 + len(search.circuit.edges) * 4) * 8
     stage_ms = {k: v / done for k, v in sorted(timer.totals.items())}
     stage_host_ms = {k: v / done for k, v in sorted(timer.host_totals.items())}
     stage_per_rank = None
@@ -510,15 +575,17 @@ def run_rollout(args, world, rank, device):
     scale = world * args.beam / 1000
     line = {
         "metric": METRIC, "value": scale * done * 1e3 / total_ms, "unit": "steps/s",
-        "n_gpus": world, "steps": done, "warmup": args.warmup,
+        "n_gpus": world, "steps": done, "warmup": first - 1,
         "ms_per_step": total_ms / done, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "full rollout step: synthetic 6-qubit 259-gate circuit, "
-                               "d_model 256, 8 heads, 4 causal + 4 message-passing layers, "
-                               "random init, beam 1000, depth 64, page 16, up to 2048 "
-                               "candidates per state -> 16 per parent -> 16000 proposals",
-                   "beam": rc.beam_size, "depth": depth, "timed_levels": f"{args.warmup + 1}"
-                   f"..{args.warmup + done}", "page_size": rc.page_size,
+        "config": {"workload": f"full rollout step: synthetic {args.qubits}-qubit "
+                               f"{args.gates}-gate circuit, d_model 256, 8 heads, 4 causal + "
+                               f"4 message-passing layers, random init, beam {args.beam} per "
+                               f"GPU, depth {depth}, page 16, up to 2048 candidates per state "
+                               f"-> 16 per parent -> 16000 proposals; levels {window} of the "
+                               f"{depth}-level search timed",
+                   "beam": rc.beam_size, "depth": depth, "timed_levels": window,
+                   "untimed_levels_before_window": first - 1, "page_size": rc.page_size,
                    "l2": "inputs larger than L2 (beam state ~0.2 GB bf16 per activation)",
                    "circuit": f"{args.qubits} qubits, {args.gates} gates",
                    "beam_per_gpu": args.beam,
@@ -526,14 +593,22 @@ def run_rollout(args, world, rank, device):
                                    f"records, identical global accept, all-to-all rebalance; "
                                    f"value counts B=1000-equivalent levels")
                                   if world > 1 else "single GPU"},
-        "e2e": {"value": scale * depth * 1e3 / e2e_ms, "unit": "steps/s",
-                "h2d_bytes_per_step": h2d // depth, "d2h_bytes_per_step": d2h,
-                "scope": "DeviceBeamSearch.run(): s0 upload, all levels, beam summary download"},
+        "e2e": {"value": scale * e2e_done * 1e3 / e2e_ms, "unit": "steps/s",
+                "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": summary_bytes + d2h_actions // max(1, e2e_done),
+                "timed_levels": f"{first}..{first + e2e_done - 1}",
+                "scope": "DeviceBeamSearch.step() per level plus the level's children copied "
+                         "to pinned host memory; the search state stays resident, its only "
+                         "host input (the s0 circuit) is uploaded at reset, before the window"},
+        "e2e_full_search": {"value": scale * depth * 1e3 / full_ms, "unit": "steps/s",
+                            "levels": depth, "h2d_bytes": full_h2d,
+                            "scope": "DeviceBeamSearch.run(): s0 circuit upload, all 64 "
+                                     "levels, beam summary download"},
         "gpu_launches": launches,
-        "roofline": probe.roofline(measured_peaks(), "add_ln_vec_kernel",
-                                   profiled_traffic("add_ln_traffic_ratio")),
+        "roofline": probe.roofline(measured_peaks(), "gemm_tc_kernel (store epilogue)",
+                                   profiled_traffic("gemm_store_traffic_ratio")),
         "search": {"last_level": {k: getattr(last, k) for k in (
-                       "input_states", "output_states", "best_speculative_gate_count",
+                       "step", "input_states", "output_states", "best_speculative_gate_count",
                        "predicted_actions", "eligible_actions_before_parent_cap",
                        "proposals_after_caps", "attempted_actions", "accepted_actions",
                        "invalid_structural_actions", "duplicate_speculative_successors",
@@ -545,15 +620,16 @@ def run_rollout(args, world, rank, device):
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        base = cpu_rollout(3, 3, sample_beams=32, budget_s=20.0)
+        base = cpu_rollout(done, first - 1, sample_beams=32)
         line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
     return line
 
 
-def cpu_rollout(levels: int, warmup: int, sample_beams: int, full_beams: int = 1000,
-                budget_s: float | None = None):
+def cpu_rollout(levels: int, warmup: int, sample_beams: int, full_beams: int = 1000):
     """The oracle beam search (the reference's loop restated on the host,
-    fp32) on a bounded beam; per-level time scaled linearly to full_beams."""
+    fp32) on a bounded beam of the 64-level search: `warmup` untimed levels,
+    then `levels` timed ones (the GPU arm's window); per-level time scaled
+    linearly to full_beams."""
     from graph_rewrite_system_b200 import synthetic
     from oracle.model import OracleModel
     from oracle.rollout import OracleBeamSearch
@@ -563,7 +639,7 @@ def cpu_rollout(levels: int, warmup: int, sample_beams: int, full_beams: int = 1
     cfg = synthetic.ROLLOUT_MODEL
     params = synthetic.deterministic_parameters(synthetic.parameter_shapes(cfg, rules), 0)
     model = OracleModel({k: torch.from_numpy(v) for k, v in params.items()}, rules, cfg)
-    rc = synthetic.RolloutConfig(beam_size=sample_beams, depth=warmup + levels)
+    rc = synthetic.RolloutConfig(beam_size=sample_beams, depth=ROLLOUT_DEPTH)
     circuit = synthetic.random_circuit(rc.num_qubits, rc.num_gates, 0)
     search = OracleBeamSearch(model, rules, circuit, rc, synthetic.SELECT_ALL_THRESHOLDS)
     search.reset()
@@ -576,15 +652,15 @@ def cpu_rollout(levels: int, warmup: int, sample_beams: int, full_beams: int = 1
             if search.step() is None:
                 break
             done += 1
-            if budget_s is not None and time.perf_counter() - started > budget_s:
-                break
         elapsed = time.perf_counter() - started
     per_level = elapsed / max(done, 1) * (full_beams / sample_beams)
     return {"value": 1.0 / per_level, "unit": "steps/s", "cores": torch.get_num_threads(),
             "kind": "port",
             "sample": f"oracle beam search, beam {sample_beams} (of {full_beams}), levels "
-                      f"{warmup + 1}..{warmup + done}, per-level time scaled x"
-                      f"{full_beams / sample_beams:g}", "levels_timed": done}
+                      f"{warmup + 1}..{warmup + done} of the {ROLLOUT_DEPTH}-level search "
+                      f"(levels 1..{warmup} untimed), per-level time scaled x"
+                      f"{full_beams / sample_beams:g}", "levels_timed": done,
+            "timed_levels": f"{warmup + 1}..{warmup + done}"}
 
 
 def run_reference(args, world, rank):
@@ -596,15 +672,20 @@ def run_reference(args, world, rank):
                 "arm; the rollout workload's reference arm times the CPU oracle"}
     if args.workload == "rollout":
         started = time.perf_counter()
-        base = cpu_rollout(args.steps, args.warmup, sample_beams=48, budget_s=150.0)
+        steps, first = rollout_window(args.steps, args.warmup)
+        base = cpu_rollout(steps, first - 1, sample_beams=64)
         value = base["value"]
         return {
             "metric": METRIC, "impl": "reference", "value": value, "unit": "steps/s",
-            "n_gpus": world, "steps": base["levels_timed"], "warmup": args.warmup,
+            "n_gpus": world, "steps": base["levels_timed"], "warmup": first - 1,
             "ms_per_step": 1e3 / value, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "full rollout step (CPU oracle of the reference loop), "
-                                   "bounded beam scaled to beam 1000"},
+            "config": {"workload": "full rollout step (CPU oracle of the reference loop): "
+                                   f"synthetic {args.qubits}-qubit {args.gates}-gate circuit, "
+                                   f"depth {ROLLOUT_DEPTH}, levels {base['timed_levels']} timed, "
+                                   "bounded beam scaled to beam 1000",
+                       "depth": ROLLOUT_DEPTH, "timed_levels": base["timed_levels"],
+                       "beam": 1000},
             "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},

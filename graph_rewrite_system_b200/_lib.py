@@ -15,6 +15,7 @@ import torch
 LIBRARY_PATH = Path(__file__).resolve().parent / "libgrs_b200.so"
 
 GRS_OK = 0
+GRS_ERR_SHAPE = -4
 ERRORS = {
     -1: (RuntimeError, "paged KV cache exhausted"),
     -2: (RuntimeError, "retaining an unallocated page"),

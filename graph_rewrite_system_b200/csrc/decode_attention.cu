@@ -61,7 +61,7 @@ constexpr int DC_BOX_BYTES = DC_UNIT * 128;              // one tile: 16 rows x 
 constexpr int DC_STAGE_BYTES = 2 * 4 * DC_BOX_BYTES;     // K and V, up to 4 tiles each
 constexpr int DC_MAX_COLS = 32;       // block-table columns
 constexpr int DC_MAX_UNITS = 64;      // page/current units per CTA
-constexpr int DC_SPIN_LIMIT = 1 << 22;   // mbarrier polls before a wait gives up
+constexpr unsigned long long DC_WAIT_LIMIT_NS = 1000000000ull;   // a wait gives up after 1 s
 
 struct DecodeArgs {
   const __nv_bfloat16* q; int64_t q_sb, q_sh;
@@ -102,11 +102,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
       : "memory");
   return done != 0;
 }
-// bounded wait for the phase with the given parity to complete
+// bounded wait for the phase with the given parity to complete: gives up
+// after DC_WAIT_LIMIT_NS of %globaltimer (try_wait may park the thread per
+// poll, so the bound is on elapsed time)
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
-  for (int i = 0; i < DC_SPIN_LIMIT; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t start;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(start));
+  for (unsigned i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-  return false;
+    if ((i & 63) == 0) {
+      uint64_t now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (now - start > DC_WAIT_LIMIT_NS) return false;
+    }
+  }
 }
 // TMA tile loads into this CTA's own shared memory; the
 // innermost coordinate is always 0 (a whole 128-byte chunk)

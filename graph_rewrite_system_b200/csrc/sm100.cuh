@@ -11,7 +11,17 @@
 namespace grs {
 namespace sm100 {
 
-constexpr int SPIN_LIMIT = 1 << 24;   // mbarrier polls before a wait gives up
+// A wait gives up after this long (ns of %globaltimer): try_wait may park
+// the thread for a hardware-chosen interval per poll, so the bound is on
+// elapsed time, not on a poll count.  No phase of these kernels takes more
+// than microseconds when healthy.
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -45,9 +55,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // bounded wait for the phase of the given parity; false if it gave up
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (int i = 0; i < SPIN_LIMIT; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-  return false;
+    if ((i & 63) == 0 && globaltimer_ns() - start > WAIT_LIMIT_NS) return false;
+  }
+}
+
+// the same wait made by a whole warp, with one answer for every lane: warps
+// that go on to warp-collective instructions (tcgen05.ld) must not split
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
 
 // 2-D tiled TMA load of box (x, y) into this CTA's shared memory; x is the

@@ -1,8 +1,9 @@
 """Thin typed wrappers over the model kernels of libgrs_b200.so.
 
 Each function takes torch CUDA tensors, checks the layout it needs and calls
-one C-ABI entry point on the current stream.  GEMMs are plain cuBLAS calls
-through ``torch.mm``/``torch.addmm`` (``linear``).
+one C-ABI entry point on the current stream.  bf16 projections run on the
+library's tcgen05 GEMM (``gemm``, ``gemm_layernorm``, ``match_logits_gemm``);
+``linear`` is the fp32 form used by the CPU-equivalence configuration.
 """
 from __future__ import annotations
 
@@ -41,10 +42,113 @@ def _row_stride(t: torch.Tensor) -> int:
 
 def linear(x: torch.Tensor, weight_t: torch.Tensor, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
-    """x [M, K] @ weight_t [K, N] (+ bias) with cuBLAS."""
+    """x [M, K] @ weight_t [K, N] (+ bias), fp32 (the CPU-equivalence
+    configuration); bf16 activations go through ``gemm``."""
+    if x.dtype != torch.float32:
+        raise ValueError("bf16 projections run on the tensor-core GEMM (kernels.gemm)")
     if bias is None:
         return torch.mm(x, weight_t, out=out)
     return torch.addmm(bias, x, weight_t, out=out)
+
+
+def _gemm_operands(x: torch.Tensor, weight: torch.Tensor):
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("the tensor-core GEMM takes bf16 operands")
+    if x.dim() != 2 or weight.dim() != 2 or x.shape[1] != weight.shape[1]:
+        raise ValueError(f"gemm shapes {tuple(x.shape)} x {tuple(weight.shape)}^T do not match")
+    if x.stride(1) != 1 or weight.stride(1) != 1:
+        raise ValueError("gemm operands need contiguous rows")
+
+
+def gemm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *,
+         gelu: bool = False, residual: torch.Tensor | None = None,
+         zero_row: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         status: torch.Tensor | None = None) -> torch.Tensor:
+    """out = (x @ weight.T (+ bias) (+ residual)) then GELU when `gelu`, rows
+    with zero_row == 0 zeroed; one tcgen05 GEMM launch (bf16 in and out, fp32
+    accumulation).  weight is a K-major [N, K] Linear weight, bias fp32 [N].
+    Shapes the kernel does not take raise; there is no other path."""
+    _gemm_operands(x, weight)
+    m, n = x.shape[0], weight.shape[0]
+    if out is None:
+        out = torch.empty(m, n, device=x.device, dtype=torch.bfloat16)
+    if m == 0:
+        return out
+    if residual is not None and (residual.shape != (m, n) or residual.dtype != torch.bfloat16):
+        raise ValueError("residual must be bf16 [M, N]")
+    _lib.check(_lib.lib().grs_gemm_bf16(
+        x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), m, n, x.shape[1],
+        _p(bias), int(gelu), _p(residual), 0 if residual is None else _row_stride(residual),
+        _p(zero_row), out.data_ptr(), _row_stride(out), _p(status), stream()), "tensor-core GEMM")
+    return out
+
+
+def gemm_layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                   residual: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, *,
+                   out: torch.Tensor, row_scale: torch.Tensor | None = None,
+                   zero_row: torch.Tensor | None = None, where_row: torch.Tensor | None = None,
+                   where_beam: torch.Tensor | None = None, where_len: torch.Tensor | None = None,
+                   rows_per_beam: int = 1, status: torch.Tensor | None = None,
+                   eps: float = 1e-5) -> torch.Tensor:
+    """out = LayerNorm(residual + row_scale * (x @ weight.T + bias)) over
+    256- or 128-column rows, with the row kernels' masks: rows whose where_row /
+    where_beam is 0 or whose where_len <= 0 keep `residual`, rows whose
+    zero_row is 0 are zeroed.  One tcgen05 GEMM launch."""
+    _gemm_operands(x, weight)
+    m, n = x.shape[0], weight.shape[0]
+    if n not in (128, 256) or residual.shape != (m, n) or out.shape != (m, n):
+        raise ValueError("gemm_layernorm normalises [M, 256] or [M, 128] rows")
+    if m == 0:
+        return out
+    _lib.check(_lib.lib().grs_gemm_bf16_layernorm_ex(
+        x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), m, n, x.shape[1],
+        bias.data_ptr(), _p(row_scale), residual.data_ptr(), _row_stride(residual),
+        gamma.data_ptr(), beta.data_ptr(), _p(zero_row), _p(where_row), _p(where_beam),
+        _p(where_len), rows_per_beam, eps, out.data_ptr(), _row_stride(out), _p(status),
+        stream()), "tensor-core GEMM + LayerNorm")
+    return out
+
+
+def graph_mlp(x: torch.Tensor, u0: torch.Tensor, b0: torch.Tensor, u2: torch.Tensor,
+              b2: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+              *, out: torch.Tensor, zero_row: torch.Tensor | None = None,
+              status: torch.Tensor | None = None, eps: float = 1e-5) -> torch.Tensor:
+    """One InitialGraphLayer update, width 256, in one tcgen05 launch:
+    out = LayerNorm(residual + GELU(x @ u0.T + b0) @ u2.T + b2), rows with
+    zero_row == 0 zeroed; x = [states | aggregated messages] [M, 512]."""
+    _gemm_operands(x, u0)
+    m = x.shape[0]
+    if (x.shape[1] != 512 or u0.shape != (512, 512) or u2.shape != (256, 512)
+            or residual.shape != (m, 256) or out.shape != (m, 256)):
+        raise ValueError("graph_mlp is the width-256 graph layer update")
+    if m == 0:
+        return out
+    _lib.check(_lib.lib().grs_graph_mlp_bf16(
+        x.data_ptr(), x.stride(0), u0.data_ptr(), u0.stride(0), b0.data_ptr(), u2.data_ptr(),
+        u2.stride(0), b2.data_ptr(), m, residual.data_ptr(), _row_stride(residual),
+        gamma.data_ptr(), beta.data_ptr(), _p(zero_row), eps, out.data_ptr(), _row_stride(out),
+        _p(status), stream()), "fused graph-layer MLP")
+    return out
+
+
+def match_logits_gemm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                      first_types: torch.Tensor, live: torch.Tensor, types: torch.Tensor,
+                      scale: float, logits: torch.Tensor, eligible: torch.Tensor,
+                      status: torch.Tensor | None = None) -> None:
+    """Match logits of x [M, K] against the source-vector x retrieval_node
+    product weight [32, K] (rows past the source count zero) in one tcgen05
+    launch: fp32 logits [M, sources] masked to -1e4 off the eligible pairs,
+    eligible [M, sources]."""
+    _gemm_operands(x, weight)
+    m, ns = x.shape[0], first_types.numel()
+    if weight.shape[0] != 32 or ns > 32:
+        raise ValueError("match_logits_gemm takes at most 32 sources")
+    if m == 0:
+        return
+    _lib.check(_lib.lib().grs_match_logits_bf16(
+        x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), m, x.shape[1], ns,
+        bias.data_ptr(), first_types.data_ptr(), live.data_ptr(), types.data_ptr(), scale,
+        logits.data_ptr(), eligible.data_ptr(), _p(status), stream()), "tensor-core match logits")
 
 
 def add_layernorm(x, y=None, *, scale=None, gamma=None, beta=None, sum_out=None, ln_out=None,

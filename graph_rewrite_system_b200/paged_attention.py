@@ -8,7 +8,13 @@ block-table pages plus, when given, the current token at position
 The sm_100a kernels live in ``csrc/paged_attention.cu``; CPU tensors raise.
 
 ``shared_key``/``shared_value`` ([N, H, D], beam-invariant) extend the
-reference API for the shared-prefix decode microbenchmark.
+reference API for the shared-prefix decode microbenchmark; ``status`` (device
+int32) receives in-kernel errors of the decode kernels (default: a
+per-device word read by ``check_decode_status``).
+
+bf16 one-query decode runs on ``grs_decode_causal`` (page-staged, one CTA per
+beam) or, with a shared prefix, ``grs_decode_attention_shared`` (8-CTA
+clusters); other shapes and fp32 on ``grs_paged_attention``.
 """
 from __future__ import annotations
 
@@ -53,6 +59,7 @@ def paged_attention(
     shared_key: torch.Tensor | None = None,
     shared_value: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    status: torch.Tensor | None = None,
 ) -> torch.Tensor:
     has_current = current_key is not None
     if has_current != (current_value is not None and current_valid is not None):
@@ -99,6 +106,24 @@ def paged_attention(
         valid = current_valid
         if valid.dtype not in (torch.uint8, torch.bool) or not valid.is_contiguous():
             valid = valid.to(torch.uint8).contiguous()
+    status_word = _status_word(query.device) if status is None else status
+    if (shared_key is None and query.dtype == torch.bfloat16 and query_length == 1
+            and head_width == 32):
+        # one query per (beam, head) over the beam's pages (+ the current
+        # token): the page-staged causal decode kernel
+        code = _lib.lib().grs_decode_causal(
+            query.data_ptr(), query.stride(0), query.stride(1), key_cache.data_ptr(),
+            value_cache.data_ptr(), key_cache.stride(0), key_cache.stride(1),
+            key_cache.stride(2), block_table.data_ptr(), block_table.stride(0),
+            lengths.data_ptr(), key_cache.shape[0], _lib.ptr(ck), _lib.ptr(cv), ck_sb, ck_sh,
+            _lib.ptr(valid), output.data_ptr(), output.stride(0), output.stride(1), batch, heads,
+            key_cache.shape[1], status_word.data_ptr(), _lib.stream_of(query))
+        if code == 0:
+            return output
+        # only a layout the kernel does not take (nothing launched) goes on to
+        # the general kernel; a failed launch raises
+        if code != _lib.GRS_ERR_SHAPE:
+            _lib.check(code, "causal decode attention")
     sk = sv = None
     num_shared = 0
     if shared_key is not None:
@@ -108,7 +133,7 @@ def paged_attention(
     if (shared_key is not None and query.dtype == torch.bfloat16 and query_length == 1
             and head_width == 32 and heads <= 8 and query.stride(3) == 1
             and key_cache.stride(3) == 1 and value_cache.stride() == key_cache.stride()):
-        status = _lib.lib().grs_decode_attention_shared(
+        code = _lib.lib().grs_decode_attention_shared(
             query.data_ptr(), query.stride(0), query.stride(1), key_cache.data_ptr(),
             value_cache.data_ptr(), key_cache.stride(0), key_cache.stride(1),
             key_cache.stride(2), block_table.data_ptr(), block_table.stride(0),
@@ -116,10 +141,14 @@ def paged_attention(
             _lib.ptr(cv), ck_sb, ck_sh,
             _lib.ptr(valid), sk.data_ptr(), sv.data_ptr(), num_shared, output.data_ptr(),
             output.stride(0), output.stride(1), batch, heads, key_cache.shape[1],
-            _status_word(query.device).data_ptr(), _lib.stream_of(query))
-        if status == 0:
+            status_word.data_ptr(), _lib.stream_of(query))
+        if code == 0:
             return output
-    status = _lib.lib().grs_paged_attention(
+        # only a layout the cluster kernel does not take (nothing launched)
+        # goes on to the general kernel; a failed launch raises
+        if code != _lib.GRS_ERR_SHAPE:
+            _lib.check(code, "shared-prefix decode attention")
+    code = _lib.lib().grs_paged_attention(
         _lib.DTYPE_CODES[query.dtype],
         query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
         key_cache.data_ptr(), value_cache.data_ptr(),
@@ -131,5 +160,5 @@ def paged_attention(
         batch, heads, query_length, head_width, key_cache.shape[1], block_table.shape[1],
         key_cache.shape[0], _lib.stream_of(query),
     )
-    _lib.check(status, "paged_attention")
+    _lib.check(code, "paged_attention")
     return output

@@ -3,8 +3,11 @@
 ``PagedActionBindingModel`` has the reference's submodules and parameter
 names (paged_model.py:97-195, model.py:12-206), so a reference ``state_dict``
 loads unchanged.  Its decode-path methods run on the kernels of
-``csrc/model_ops.cu``, ``csrc/paged_attention.cu`` and ``csrc/candidates.cu``
-with plain cuBLAS GEMMs in between:
+``csrc/model_ops.cu``, ``csrc/paged_attention.cu``, ``csrc/candidates.cu``
+and, for every bf16 projection, the tcgen05 GEMM of ``csrc/gemm_tc.cu`` with
+the following bias / GELU / residual / LayerNorm / match-logit work fused
+into its epilogue (the fp32 CPU-equivalence configuration uses fp32 GEMMs and
+the separate row kernels):
 
 * ``initialize_incremental`` (paged_model.py:438-442)
 * ``advance_incremental`` with paged K/V (paged_model.py:444-613)
@@ -232,10 +235,6 @@ class PagedActionBindingModel(nn.Module):
                                              layer.backward_message.weight), 0))
                 w[p + "rel"] = f(layer.relation.weight)
                 w[p + "u0_t"], w[p + "u0_b"] = t(layer.update[0].weight), f(layer.update[0].bias)
-                if dt == torch.bfloat16:   # K-major operands of the tensor-core GEMMs
-                    w[p + "u0_k"] = c(layer.update[0].weight)
-                    w[p + "u2_k"] = c(layer.update[2].weight)
-                    w[p + "u2_bf"] = c(layer.update[2].bias).float()
                 w[p + "u2_t"], w[p + "u2_b"] = t(layer.update[2].weight), c(layer.update[2].bias)
                 w[p + "norm_w"], w[p + "norm_b"] = f(layer.norm.weight), f(layer.norm.bias)
         if self.readout_graph_layers_count:
@@ -269,8 +268,68 @@ class PagedActionBindingModel(nn.Module):
         w["nav_t"], w["nao_t"] = t(self.node_action_value.weight), t(self.node_action_output.weight)
         w["na_norm_w"], w["na_norm_b"] = f(self.node_action_norm.weight), f(self.node_action_norm.bias)
         w["retrieval_node_t"] = t(self.retrieval_node.weight)
+        if dt == torch.bfloat16:
+            self._prepare_tensor_core(w)
         self._w, self._prepared_key = w, key
         return w
+
+    @torch.no_grad()
+    def _prepare_tensor_core(self, w: dict) -> None:
+        """K-major bf16 operands ([out, in], the Linear layout) of the tcgen05
+        GEMMs and their fp32 epilogue biases rounded to bf16 first, as bf16
+        autocast rounds a Linear's bias."""
+        W = self.width
+        k = lambda m: m.detach().to(torch.bfloat16).contiguous()
+        b = lambda v: v.detach().to(torch.bfloat16).float().contiguous()
+        dev = self.gate_embedding.weight.device
+        w["zero_bias"] = torch.zeros(W, device=dev, dtype=torch.float32)
+        for prefix, layers in (("graph", self.graph_layers),
+                               ("readout_graph", getattr(self, "readout_graph_layers", []))):
+            for i, layer in enumerate(layers):
+                p = f"{prefix}{i}."
+                w[p + "fb_k"] = k(torch.cat((layer.forward_message.weight,
+                                             layer.backward_message.weight), 0))
+                w[p + "u0_k"], w[p + "u0_bf"] = k(layer.update[0].weight), b(layer.update[0].bias)
+                w[p + "u2_k"], w[p + "u2_bf"] = k(layer.update[2].weight), b(layer.update[2].bias)
+        if self.readout_graph_layers_count:
+            w["readout_graph_output_k"] = k(self.readout_graph_output.weight)
+        w["ac0_k"], w["ac0_bf"] = k(self.action_context[0].weight), b(self.action_context[0].bias)
+        w["ac3_k"], w["ac3_bf"] = k(self.action_context[3].weight), b(self.action_context[3].bias)
+        d0 = self.action_delta[0].weight
+        w["qxa_k"] = k(torch.cat((self.node_query.weight, d0[:, :W]), 0))
+        w["bk_k"], w["bv_k"] = k(self.binding_key.weight), k(self.binding_value.weight)
+        w["d0b_k"], w["d0c_k"] = k(d0[:, W:2 * W]), k(d0[:, 2 * W:])
+        w["d0_bf"] = b(self.action_delta[0].bias)
+        w["d3_k"], w["d3_bf"] = k(self.action_delta[3].weight), b(self.action_delta[3].bias)
+        ds0 = self.destination_state[0].weight
+        w["ds0a_k"], w["ds0_bf"] = k(ds0[:, :W]), b(self.destination_state[0].bias)
+        w["ds2_k"], w["ds2_bf"] = k(self.destination_state[2].weight), b(self.destination_state[2].bias)
+        for i, layer in enumerate(self.causal_action_layers):
+            p = f"causal{i}."
+            w[p + "qkv_k"], w[p + "out_k"] = k(layer.qkv.weight), k(layer.output.weight)
+            w[p + "f0_k"], w[p + "f0_bf"] = k(layer.ffn[0].weight), b(layer.ffn[0].bias)
+            w[p + "f3_k"], w[p + "f3_bf"] = k(layer.ffn[3].weight), b(layer.ffn[3].bias)
+        w["naq_k"], w["nak_k"] = k(self.node_action_query.weight), k(self.node_action_key.weight)
+        w["nav_k"], w["nao_k"] = k(self.node_action_value.weight), k(self.node_action_output.weight)
+        if self.num_sources <= 32:
+            w["match_k"] = self._match_weight(w["source_vectors_t"].t().float())
+
+    def _match_weight(self, source_vectors: torch.Tensor) -> torch.Tensor:
+        """[32, W] bf16: the source vectors times the retrieval_node weight,
+        so node projection and source product (model.py:375-389) are one
+        GEMM; rows past the source count are zero."""
+        prod = source_vectors.float() @ self.retrieval_node.weight.detach().float()
+        out = torch.zeros(32, self.width, device=prod.device, dtype=torch.float32)
+        out[: prod.shape[0]] = prod
+        return out.to(torch.bfloat16).contiguous()
+
+    def _tc(self) -> bool:
+        """bf16: every projection runs on the tcgen05 GEMM."""
+        return self.compute_dtype == torch.bfloat16
+
+    def _status(self, device) -> torch.Tensor:
+        status = getattr(self, "kernel_status", None)
+        return _status_word(device) if status is None else status
 
     @torch.no_grad()
     def _source_representations_fp32(self) -> torch.Tensor:
@@ -293,28 +352,46 @@ class PagedActionBindingModel(nn.Module):
         """Run `count` InitialGraphLayer blocks (model.py:26-53).  x_buf is
         [M, 2W] with the layer input in its first W columns; returns the
         [M, 2W] buffer whose first W columns hold the output.  With
-        keep_input the first W columns of x_buf are left untouched."""
+        keep_input the first W columns of x_buf are left untouched.
+
+        bf16: the message projection (a tcgen05 GEMM), the aggregation kernel,
+        then the update MLP with its GELU, the residual, the LayerNorm and the
+        dead-row mask in one fused tcgen05 launch (width 256; other widths run
+        the two GEMMs with fused epilogues)."""
         w, W = self.prepare(), self.width
         m = x_buf.shape[0]
+        tc = self._tc()
+        status = self._status(x_buf.device) if tc else None
         spare = [torch.empty_like(x_buf)]
         if keep_input and count > 1:
             spare.append(torch.empty_like(x_buf))
         fb = torch.empty(m, 2 * W, device=x_buf.device, dtype=x_buf.dtype)
-        hidden = torch.empty(m, 2 * W, device=x_buf.device, dtype=x_buf.dtype)
-        upd = torch.empty(m, W, device=x_buf.device, dtype=x_buf.dtype)
+        hidden = None if tc and W == 256 else torch.empty(m, 2 * W, device=x_buf.device,
+                                                          dtype=x_buf.dtype)
+        upd = None if tc else torch.empty(m, W, device=x_buf.device, dtype=x_buf.dtype)
         live_flat = live.reshape(-1)
         for i in range(count):
             p = f"{prefix}{i}."
             x = x_buf[:, :W]
-            K.linear(x, w[p + "fb_t"], out=fb)
-            K.graph_aggregate(fb, w[p + "rel"], ports, slots, x_buf[:, W:])
-            if not self._fused_update(x_buf, w.get(p + "u0_k"), w[p + "u0_b"], hidden):
+            target = spare.pop(0)
+            if tc:
+                K.gemm(x, w[p + "fb_k"], out=fb, status=status)
+                K.graph_aggregate(fb, w[p + "rel"], ports, slots, x_buf[:, W:])
+                if W == 256:   # update MLP + residual + LayerNorm, GELU kept on chip
+                    K.graph_mlp(x_buf, w[p + "u0_k"], w[p + "u0_bf"], w[p + "u2_k"],
+                                w[p + "u2_bf"], x, w[p + "norm_w"], w[p + "norm_b"],
+                                zero_row=live_flat, out=target[:, :W], status=status)
+                else:
+                    K.gemm(x_buf, w[p + "u0_k"], w[p + "u0_bf"], gelu=True, out=hidden,
+                           status=status)
+                    K.gemm_layernorm(hidden, w[p + "u2_k"], w[p + "u2_bf"], x, w[p + "norm_w"],
+                                     w[p + "norm_b"], zero_row=live_flat, out=target[:, :W],
+                                     status=status)
+            else:
+                K.linear(x, w[p + "fb_t"], out=fb)
+                K.graph_aggregate(fb, w[p + "rel"], ports, slots, x_buf[:, W:])
                 K.linear(x_buf, w[p + "u0_t"], out=hidden)
                 K.bias_gelu(hidden, w[p + "u0_b"])
-            target = spare.pop(0)
-            if not self._fused_update_norm(hidden, w.get(p + "u2_k"), w.get(p + "u2_bf"), x,
-                                           w[p + "norm_w"], w[p + "norm_b"], live_flat,
-                                           target[:, :W]):
                 K.linear(hidden, w[p + "u2_t"], w[p + "u2_b"], out=upd)
                 K.add_layernorm(x, upd, gamma=w[p + "norm_w"], beta=w[p + "norm_b"],
                                 ln_out=target[:, :W], zero_row=live_flat)
@@ -322,42 +399,6 @@ class PagedActionBindingModel(nn.Module):
                 spare.append(x_buf)
             x_buf = target
         return x_buf
-
-    # rows from which the tensor-core GEMM with the fused GELU epilogue is used
-    FUSED_MIN_ROWS = 4096
-
-    def _fused_update(self, x: torch.Tensor, weight_k, bias, out: torch.Tensor) -> bool:
-        """hidden = GELU(x @ u0^T + b) in one tensor-core pass (bf16, large
-        batches); False when the caller must run the GEMM and bias+GELU
-        separately (fp32 configuration, small batch, or a shape the kernel
-        does not take)."""
-        if weight_k is None or x.shape[0] < self.FUSED_MIN_ROWS:
-            return False
-        status = getattr(self, "kernel_status", None)
-        if status is None:
-            status = _status_word(x.device)
-        code = K.gemm_bias_gelu(x, weight_k, bias, True, out, status)
-        if code == -4:                       # GRS_ERR_SHAPE: nothing launched
-            return False
-        _lib.check(code, "tensor-core GEMM")
-        return True
-
-    def _fused_update_norm(self, hidden, weight_k, bias, residual, gamma, beta, zero_row,
-                           out) -> bool:
-        """out = LayerNorm(residual + hidden @ u2^T + b) (dead rows zeroed)
-        in one tensor-core pass; False when the caller must run the GEMM and
-        the add+LayerNorm separately."""
-        if weight_k is None or hidden.shape[0] < self.FUSED_MIN_ROWS:
-            return False
-        status = getattr(self, "kernel_status", None)
-        if status is None:
-            status = _status_word(hidden.device)
-        code = K.gemm_residual_layernorm(hidden, weight_k, bias, residual, gamma, beta, zero_row,
-                                         out, status)
-        if code == -4:                       # GRS_ERR_SHAPE: nothing launched
-            return False
-        _lib.check(code, "tensor-core GEMM + LayerNorm")
-        return True
 
     def _ports(self, batch: dict, b: int, s: int, device):
         return K.edges_to_ports(batch["current_edge_batch"] if "current_edge_batch" in batch
@@ -405,15 +446,24 @@ class PagedActionBindingModel(nn.Module):
         states = states.to(self.compute_dtype).contiguous()
         flat = states.view(b * s, W)
         live_flat = live.reshape(-1)
-        q = K.linear(flat, w["naq_t"])
+        tc = self._tc()
+        status = self._status(states.device) if tc else None
+        live_u8 = live_flat.view(torch.uint8) if live_flat.dtype == torch.bool else live_flat
+        q = K.gemm(flat, w["naq_k"], status=status) if tc else K.linear(flat, w["naq_t"])
         query = q.view(b, s, h, W // h).transpose(1, 2)
         ctx = paged_attention(query, readout_key_cache, readout_value_cache, block_table, lengths)
         ctx2d = ctx.transpose(1, 2).reshape(b * s, W)
-        u = K.linear(ctx2d, w["nao_t"])
         x_buf = torch.empty(b * s, 2 * W, device=states.device, dtype=states.dtype)
         lengths32 = lengths.to(torch.int32).contiguous()
-        K.add_layernorm(flat, u, gamma=w["na_norm_w"], beta=w["na_norm_b"], ln_out=x_buf[:, :W],
-                        zero_row=live_flat, where_len=lengths32, rows_per_beam=s)
+        if tc:   # output projection + residual + LayerNorm + masks in one GEMM
+            K.gemm_layernorm(ctx2d, w["nao_k"], w["zero_bias"], flat, w["na_norm_w"],
+                             w["na_norm_b"], zero_row=live_u8, where_len=lengths32,
+                             rows_per_beam=s, out=x_buf[:, :W], status=status)
+        else:
+            u = K.linear(ctx2d, w["nao_t"])
+            K.add_layernorm(flat, u, gamma=w["na_norm_w"], beta=w["na_norm_b"],
+                            ln_out=x_buf[:, :W], zero_row=live_flat, where_len=lengths32,
+                            rows_per_beam=s)
         if not self.readout_graph_layers_count:
             return x_buf[:, :W].contiguous().view(b, s, W), live, gate_types
         if ports is None:
@@ -422,9 +472,14 @@ class PagedActionBindingModel(nn.Module):
             ports = self._ports(batch, b, s, states.device)
         g = self._graph_layers("readout_graph", self.readout_graph_layers_count, x_buf, live,
                                ports, s, keep_input=True)
-        proj = K.linear(g[:, :W], w["readout_graph_output_t"])
         out = torch.empty(b * s, W, device=states.device, dtype=states.dtype)
-        K.add_layernorm(x_buf[:, :W], proj, sum_out=out, zero_row=live_flat, zero_before=True)
+        if tc:   # (states + readout_graph_output(g)) * live in one GEMM
+            K.gemm(g[:, :W], w["readout_graph_output_k"], residual=x_buf[:, :W],
+                   zero_row=live_u8, out=out, status=status)
+        else:
+            proj = K.linear(g[:, :W], w["readout_graph_output_t"])
+            K.add_layernorm(x_buf[:, :W], proj, sum_out=out, zero_row=live_flat,
+                            zero_before=True)
         return out.view(b, s, W), live, gate_types
 
     @torch.no_grad()
@@ -434,6 +489,10 @@ class PagedActionBindingModel(nn.Module):
         b = action_states.shape[0]
         shape = (b, self.action_heads, self.width // self.action_heads)
         a = action_states.to(self.compute_dtype).contiguous()
+        if self._tc():
+            status = self._status(a.device)
+            return (K.gemm(a, w["nak_k"], status=status).view(shape),
+                    K.gemm(a, w["nav_k"], status=status).view(shape))
         return K.linear(a, w["nak_t"]).view(shape), K.linear(a, w["nav_t"]).view(shape)
 
     # ---- one action -------------------------------------------------------------
@@ -537,8 +596,14 @@ class PagedActionBindingModel(nn.Module):
         b = ctx_in.shape[0]
         h = self.action_heads
         hd = W // h
-        hidden = K.bias_gelu(K.linear(ctx_in, w["ac0_t"]), w["ac0_b"])
-        raw = K.linear(hidden, w["ac3_t"], w["ac3_b"])
+        tc = self._tc()
+        status = self._status(dev) if tc else None
+        if tc:
+            hidden = K.gemm(ctx_in, w["ac0_k"], w["ac0_bf"], gelu=True, status=status)
+            raw = K.gemm(hidden, w["ac3_k"], w["ac3_bf"], status=status)
+        else:
+            hidden = K.bias_gelu(K.linear(ctx_in, w["ac0_t"]), w["ac0_b"])
+            raw = K.linear(hidden, w["ac3_t"], w["ac3_b"])
         token = torch.empty_like(raw)
         K.position_token(raw, w["action_position"], past_lengths, active, token)
         valid = active
@@ -549,18 +614,29 @@ class PagedActionBindingModel(nn.Module):
         for layer in range(self.action_layers_count):
             p = f"causal{layer}."
             K.add_layernorm(token, gamma=w[p + "in_w"], beta=w[p + "in_b"], ln_out=ln)
-            qkv = K.linear(ln, w[p + "qkv_t"]).view(b, 3, h, hd)
+            if tc:
+                qkv = K.gemm(ln, w[p + "qkv_k"], status=status).view(b, 3, h, hd)
+            else:
+                qkv = K.linear(ln, w[p + "qkv_t"]).view(b, 3, h, hd)
             q, k, v = qkv.unbind(1)
             ctx = paged_attention(q.unsqueeze(2), key_cache[layer], value_cache[layer],
                                   block_table, past_lengths, current_key=k, current_value=v,
-                                  current_valid=valid)
-            o = K.linear(ctx.reshape(b, W), w[p + "out_t"])
+                                  current_valid=valid, status=status)
+            if tc:
+                o = K.gemm(ctx.reshape(b, W), w[p + "out_k"], status=status)
+            else:
+                o = K.linear(ctx.reshape(b, W), w[p + "out_t"])
             K.add_layernorm(token, o, gamma=w[p + "ffn_norm_w"], beta=w[p + "ffn_norm_b"],
                             sum_out=token2, ln_out=ln)
-            f0 = K.bias_gelu(K.linear(ln, w[p + "f0_t"]), w[p + "f0_b"])
-            f3 = K.linear(f0, w[p + "f3_t"], w[p + "f3_b"])
             token = torch.empty_like(token2)
-            K.add_layernorm(token2, f3, sum_out=token, zero_beam=active, zero_before=True)
+            if tc:   # FFN; the second GEMM adds the residual and zeroes inactive beams
+                f0 = K.gemm(ln, w[p + "f0_k"], w[p + "f0_bf"], gelu=True, status=status)
+                K.gemm(f0, w[p + "f3_k"], w[p + "f3_bf"], residual=token2, zero_row=active,
+                       out=token, status=status)
+            else:
+                f0 = K.bias_gelu(K.linear(ln, w[p + "f0_t"]), w[p + "f0_b"])
+                f3 = K.linear(f0, w[p + "f3_t"], w[p + "f3_b"])
+                K.add_layernorm(token2, f3, sum_out=token, zero_beam=active, zero_before=True)
             new_keys[layer].copy_(k)
             new_values[layer].copy_(v)
         action = torch.empty_like(token)
@@ -584,8 +660,13 @@ class PagedActionBindingModel(nn.Module):
             if graphs is not None and graphs[1]:
                 torch.cuda.synchronize(ctx_in.device)   # no replay of a dropped graph pending
             graphs = self._graphs = (version, {})
-        key = (ctx_in.shape[0], block_table.shape[1], ctx_in.dtype, key_cache.data_ptr(),
-               value_cache.data_ptr(), ctx_in.device)
+        # the captured attention bakes in the arena's address and its page
+        # count (the page-id bound): a new cache allocated at a freed cache's
+        # address with another capacity must not replay the old graph
+        key = (ctx_in.shape[0], block_table.shape[1], block_table.dtype, ctx_in.dtype,
+               key_cache.data_ptr(), tuple(key_cache.shape), key_cache.dtype,
+               value_cache.data_ptr(), tuple(value_cache.shape), value_cache.dtype,
+               ctx_in.device)
         entry = graphs[1].pop(key, None)
         inputs = (ctx_in, active, past_lengths, block_table)
         if entry is None:
@@ -625,26 +706,44 @@ class PagedActionBindingModel(nn.Module):
         m = b * s
         pattern = bound.shape[1]
         flat = states.view(m, W)
-        qxa = K.linear(flat, w["qxa_t"])                                   # [M, 3W]
-        keys = K.linear(bound.view(b * pattern, W), w["bk_t"])             # [B*P, W]
-        vw = K.linear(K.linear(bound.view(b * pattern, W), w["bv_t"]), w["d0b_t"])  # [B*P, 2W]
-        cvec = K.linear(raw, w["d0c_t"], w["d0_b"])                         # [B, 2W]
+        tc = self._tc()
+        status = self._status(dev) if tc else None
+        bound2d = bound.view(b * pattern, W)
+        if tc:
+            qxa = K.gemm(flat, w["qxa_k"], status=status)                         # [M, 3W]
+            keys = K.gemm(bound2d, w["bk_k"], status=status)                      # [B*P, W]
+            vw = K.gemm(K.gemm(bound2d, w["bv_k"], status=status), w["d0b_k"],
+                        status=status)                                            # [B*P, 2W]
+            cvec = K.gemm(raw, w["d0c_k"], w["d0_bf"], status=status)             # [B, 2W]
+        else:
+            qxa = K.linear(flat, w["qxa_t"])
+            keys = K.linear(bound2d, w["bk_t"])
+            vw = K.linear(K.linear(bound2d, w["bv_t"]), w["d0b_t"])
+            cvec = K.linear(raw, w["d0c_t"], w["d0_b"])
         hidden = torch.empty(m, 2 * W, device=dev, dtype=dt)
         affinity = torch.empty(m, device=dev, dtype=torch.float32)
         K.update_live_hidden(qxa, keys, vw, cvec, source_mask, s, W, hidden, affinity)
-        delta = K.linear(hidden, w["d3_t"], w["d3_b"])
         next_states = torch.empty_like(states)
-        K.add_layernorm(flat, delta, scale=affinity, gamma=w["action_norm_w"],
-                        beta=w["action_norm_b"], ln_out=next_states.view(m, W),
-                        where_row=live.reshape(-1), where_beam=active, rows_per_beam=s)
+        if tc:   # action_delta output + affinity scale + residual + LayerNorm + masks
+            K.gemm_layernorm(hidden, w["d3_k"], w["d3_bf"], flat, w["action_norm_w"],
+                             w["action_norm_b"], row_scale=affinity, where_row=live.reshape(-1),
+                             where_beam=active, rows_per_beam=s, out=next_states.view(m, W),
+                             status=status)
+        else:
+            delta = K.linear(hidden, w["d3_t"], w["d3_b"])
+            K.add_layernorm(flat, delta, scale=affinity, gamma=w["action_norm_w"],
+                            beta=w["action_norm_b"], ln_out=next_states.view(m, W),
+                            where_row=live.reshape(-1), where_beam=active, rows_per_beam=s)
         next_live = live.clone()
         next_types = gate_types.clone()
         dpattern = destination_slots.shape[1]
-        r = K.linear(raw, w["ds0a_t"], w["ds0_b"])
+        r = K.gemm(raw, w["ds0a_k"], w["ds0_bf"], status=status) if tc else \
+            K.linear(raw, w["ds0a_t"], w["ds0_b"])
         dh = torch.empty(b * dpattern, 2 * W, device=dev, dtype=dt)
         K.destination_hidden(r, w["ds_type_table"], w["ds_pos_table"], destination_slots,
                              destination_types, active, dh)
-        created = K.linear(dh, w["ds2_t"], w["ds2_b"])
+        created = K.gemm(dh, w["ds2_k"], w["ds2_bf"], status=status) if tc else \
+            K.linear(dh, w["ds2_t"], w["ds2_b"])
         K.apply_slots(next_states, next_live, next_types, source_slots, source_mask,
                       destination_slots, destination_types, active, created)
         return next_states, next_live, next_types
@@ -657,15 +756,24 @@ class PagedActionBindingModel(nn.Module):
         w = self.prepare()
         b, s, W = states.shape
         flat = states.to(self.compute_dtype).contiguous().view(b * s, W)
+        logits = torch.empty(b, s, self.num_sources, device=states.device, dtype=torch.float32)
+        eligible = torch.empty(b, s, self.num_sources, device=states.device, dtype=torch.bool)
+        scale = 1.0 / math.sqrt(self.retrieval_width)
+        if self._tc():
+            if self.num_sources > 32:
+                raise ValueError("the tensor-core match logits take at most 32 source patterns")
+            weight = w["match_k"] if source_vectors is None else \
+                self._match_weight(source_vectors.to(flat.device))
+            K.match_logits_gemm(flat, weight, w["source_bias"], w["first_types"],
+                                live.contiguous(), gate_types.to(torch.int64).contiguous(), scale,
+                                logits, eligible, status=self._status(flat.device))
+            return logits, eligible
         node = K.linear(flat, w["retrieval_node_t"])
         sv_t = w["source_vectors_t"] if source_vectors is None else \
             source_vectors.t().contiguous().to(self.compute_dtype)
         acc = K.linear(node, sv_t)
-        logits = torch.empty(b, s, self.num_sources, device=states.device, dtype=torch.float32)
-        eligible = torch.empty(b, s, self.num_sources, device=states.device, dtype=torch.bool)
         K.match_logits(acc, w["source_bias"], w["first_types"], live.contiguous(),
-                       gate_types.to(torch.int64).contiguous(), 1.0 / math.sqrt(self.retrieval_width),
-                       logits, eligible)
+                       gate_types.to(torch.int64).contiguous(), scale, logits, eligible)
         return logits, eligible
 
     # ---- structural decode ------------------------------------------------------

@@ -369,7 +369,7 @@ class DeviceBeamSearch:
         self.states, self.live, self.types = states, live, types
         self.block_table, self.lengths = child_table, child_lengths
         self.topo, self.current = nxt, 1 - self.current
-        self.last_actions = (a_parent, a_xfer, a_src)
+        self.last_actions = (a_parent, a_xfer, a_src, a_dst)
         self.beams, self.slots, self.depth = accepted, s_new, depth + 1
 
     def _materialize(self, n: int, child_proposal, summary, rows, xfers, next_gate, fp,
@@ -422,8 +422,31 @@ class DeviceBeamSearch:
     # ---- inspection -------------------------------------------------------------
     def last_children(self) -> list[tuple[int, int, tuple[int, ...]]]:
         """(parent, xfer, binding) of the beams produced by the last step."""
-        parent, xfer, src = (t.tolist() for t in self.last_actions)
+        parent, xfer, src = (t.tolist() for t in self.last_actions[:3])
         return [(p, x, tuple(v for v in b if v >= 0)) for p, x, b in zip(parent, xfer, src)]
+
+    def level_actions_host(self) -> dict:
+        """The last level's children on the host: parent (index into the
+        previous level's beam), xfer id, source and destination slots (-1
+        padded) and gate count, each copied through a pinned buffer with one
+        synchronisation.  `nbytes` is the device-to-host volume."""
+        names = ("parent", "xfer", "source_slots", "destination_slots")
+        tensors = list(zip(names, self.last_actions)) + [("gate_count", self.topo.gate)]
+        bufs = getattr(self, "_host_bufs", {})
+        out, nbytes = {}, 0
+        for name, t in tensors:
+            buf = bufs.get(name)
+            if buf is None or buf.numel() < t.numel():
+                buf = torch.empty(max(t.numel(), 1), dtype=t.dtype, pin_memory=True)
+                bufs[name] = buf
+            view = buf[: t.numel()].view(t.shape)
+            view.copy_(t, non_blocking=True)
+            out[name] = view
+            nbytes += t.numel() * t.element_size()
+        self._host_bufs = bufs
+        torch.cuda.current_stream(self.device).synchronize()
+        out["nbytes"] = nbytes
+        return out
 
     def beam_summary(self) -> dict:
         """Gate counts, next slots and fingerprints of the current beam (host)."""

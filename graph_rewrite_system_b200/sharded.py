@@ -394,6 +394,12 @@ class ShardedBeamSearch(DeviceBeamSearch):
             self.cache.release_device(self.block_table, self.lengths)
         if n_in:
             self.cache.release_device(moved["table"], moved["lengths"])
+        if n:       # parents index this GPU's kept parents, then the received rows
+            self.last_actions = (a_parent, a_xfer, a_src, a_dst)
+        else:
+            self.last_actions = (torch.empty(0, **i64), torch.empty(0, **i64),
+                                 torch.empty(0, self.max_src, **i64),
+                                 torch.empty(0, max(self.max_dst, 1), **i64))
         self.states, self.live, self.types = states, live, types
         self.block_table, self.lengths = child_table, child_lengths
         self.topo, self.current = nxt, 1 - self.current

@@ -71,6 +71,27 @@ GRS_API int grs_paged_attention(int dtype, const void* query, int64_t q_sb, int6
                         int query_len, int head_width, int page_size, int max_blocks,
                         int num_pages, void* stream);
 
+/* Causal one-token decode (bf16, head width 32, one query, heads <= 16): the
+ * causal action layers' attention (paged_attention.py:18-159 with the current
+ * token, :101-132; paged_model.py:66-94) with grs_paged_attention's
+ * semantics for query_len 1 and no shared prefix.  One CTA per beam stages
+ * the beam's pages with one bulk copy per page of K and of V; needs pages
+ * contiguous in the arena (kc_sh == 32, kc_st == heads * 32, kc_sp == page *
+ * kc_st, the value arena with the same strides), page dividing 64, 16-byte
+ * aligned query / cache / current tensors and strides that are multiples of
+ * 8 elements; GRS_ERR_SHAPE otherwise (nothing launched).  current_key may
+ * be null (no current token); current_valid may be null (all valid).  Page
+ * ids outside [0, num_pages) set GRS_ERR_BAD_PAGE in `status` and their
+ * tokens are skipped; a bounded wait that gives up sets GRS_ERR_TIMEOUT. */
+GRS_API int grs_decode_causal(const void* query, int64_t q_sb, int64_t q_sh,
+                              const void* key_cache, const void* value_cache, int64_t kc_sp,
+                              int64_t kc_st, int64_t kc_sh, const int32_t* block_table,
+                              int64_t bt_s, const int32_t* lengths, int num_pages,
+                              const void* current_key, const void* current_value, int64_t ck_sb,
+                              int64_t ck_sh, const uint8_t* current_valid, void* out,
+                              int64_t o_sb, int64_t o_sh, int batch, int heads, int page,
+                              int32_t* status, void* stream);
+
 /* Shared-prefix decode (bf16, head width 32, one query, heads <= 8): the
  * same semantics as grs_paged_attention with query_len 1 (token order:
  * shared prefix, pages, current token), in one launch of 8-CTA clusters of
@@ -393,6 +414,18 @@ GRS_API int grs_topology_fingerprint(const int64_t* types, const int32_t* out_no
 GRS_API int grs_gemm_bf16_epilogue(const void* a, int64_t lda, const void* b, int64_t ldb, int M,
                                    int N, int K, const float* bias, int gelu, void* out,
                                    int64_t ldo, int32_t* status, void* stream);
+/* The general form of the tensor-core GEMM used for every bf16 projection of
+ * the paged action model (paged_model.py:36-94, 213-241, 338-436, 513-604;
+ * model.py:26-53): out = (A . B^T (+ bias) (+ residual)) then GELU when
+ * `gelu`, rows with zero_row[r] == 0 written as zeros (the residual + dead-row
+ * mask is the readout graph output's add, paged_model.py:434-436).  N a
+ * multiple of 128, K of 64; residual bf16 [M, N] with row stride ldr, or
+ * null; zero_row may be null.  GRS_ERR_SHAPE for shapes or alignments the
+ * kernel does not take (nothing launched). */
+GRS_API int grs_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N,
+                          int K, const float* bias, int gelu, const void* residual, int64_t ldr,
+                          const uint8_t* zero_row, void* out, int64_t ldo, int32_t* status,
+                          void* stream);
 /* The same tensor-core GEMM with N = 256 and a residual + LayerNorm epilogue
  * (the readout graph layers' u2 projection and their add+LayerNorm,
  * model.py:26-53):  s = residual[M, 256] + A . B^T + bias;  out = (s - mean(s))
@@ -405,6 +438,49 @@ GRS_API int grs_gemm_bf16_layernorm(const void* a, int64_t lda, const void* b, i
                                     const float* gamma, const float* beta, const uint8_t* zero_row,
                                     float eps, void* out, int64_t ldo, int32_t* status,
                                     void* stream);
+/* grs_gemm_bf16_layernorm with N = 256 or 128 and the masks of the model's
+ * other add+LayerNorm passes: s = residual + row_scale[r] * (A . B^T + bias) (row_scale may be
+ * null: 1), rows whose where_row[r], where_beam[r / rows_per_beam] is 0 or
+ * whose where_len[r / rows_per_beam] <= 0 keep the residual unchanged, rows
+ * with zero_row[r] == 0 are zeroed (each mask may be null).  These are the
+ * node readout's output projection + norm (paged_model.py:373-379: rows of
+ * beams with no action history keep their state) and the live-node update's
+ * action_delta output + norm (paged_model.py:236-241: the update scaled by
+ * the affinity, only live slots of active beams change). */
+GRS_API int grs_gemm_bf16_layernorm_ex(const void* a, int64_t lda, const void* b, int64_t ldb,
+                                       int M, int N, int K, const float* bias,
+                                       const float* row_scale,
+                                       const void* residual, int64_t ldr, const float* gamma,
+                                       const float* beta, const uint8_t* zero_row,
+                                       const uint8_t* where_row, const uint8_t* where_beam,
+                                       const int32_t* where_len, int rows_per_beam, float eps,
+                                       void* out, int64_t ldo, int32_t* status, void* stream);
+/* One InitialGraphLayer update on the tensor cores, width 256 (model.py:26-53):
+ * out = LayerNorm(residual + GELU(A . U0^T + b0) . U2^T + b2) * gamma + beta,
+ * rows with zero_row[r] == 0 zeroed.  A = [states | aggregated messages] bf16
+ * [M, 512] (row stride lda), U0 [512, 512] and U2 [256, 512] K-major bf16,
+ * b0 [512], b2, gamma, beta [256] fp32, residual bf16 [M, 256] (the states:
+ * usually the first 256 columns of A), out bf16 [M, 256].  The [M, 512] GELU
+ * activation stays in shared memory: one launch, no intermediate tensor.
+ * GRS_ERR_SHAPE for strides or alignments the kernel does not take. */
+GRS_API int grs_graph_mlp_bf16(const void* a, int64_t lda, const void* u0, int64_t ldu0,
+                               const float* b0, const void* u2, int64_t ldu2, const float* b2,
+                               int M, const void* residual, int64_t ldr, const float* gamma,
+                               const float* beta, const uint8_t* zero_row, float eps, void* out,
+                               int64_t ldo, int32_t* status, void* stream);
+/* Match logits on the tensor cores (model.py:375-389): logits[r, v] =
+ * (x[r] . w[v]) * scale + bias[v] where the slot is live and its gate type
+ * equals first_types[v], else -1e4; eligible[r, v] the same condition.  w is
+ * the bf16 product of the source vectors and the retrieval_node weight
+ * ([32, K], rows >= num_sources zero), so the node projection and the
+ * source product are one GEMM with N = 32; num_sources <= 32, K % 64 == 0;
+ * live uint8 [M], types int64 [M], logits fp32 [M, num_sources], eligible
+ * uint8 [M, num_sources]. */
+GRS_API int grs_match_logits_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, int M,
+                                  int K, int num_sources, const float* bias,
+                                  const int64_t* first_types, const uint8_t* live,
+                                  const int64_t* types, float scale, float* logits,
+                                  uint8_t* eligible, int32_t* status, void* stream);
 
 /* ---- beam search sharded over the GPUs of a node ---------------------------
  * The reference ranks a level's proposals globally

@@ -1,8 +1,8 @@
 """Generate the golden fixtures of tests/golden from the reference's own code.
 
-Run in a container where the reference repository is available:
+Run where a checkout of the reference repository is available:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path to the reference checkout>
 
 Each fixture stores seeded inputs and the outputs the reference's Python
 implementation produced for them (CPU, fp32).  The tests pin the CPU oracle
@@ -180,9 +180,12 @@ def topology_case(*, seed=0, beams=90, depth=7, qubits=4, gates=40, per_step=120
     import json
     import random
 
+    import tempfile
+
     import beam_search_benchmark as bsb
     import incremental_graph as ig
     import lazy_rollout_benchmark as lrb
+    import paged_rollout_benchmark as prb
     from graph_rewrite_system_b200 import synthetic
 
     rng = random.Random(seed)
@@ -258,18 +261,25 @@ def topology_case(*, seed=0, beams=90, depth=7, qubits=4, gates=40, per_step=120
                 "previous_preferred": sorted(int(x) for x in child.previous_preferred),
                 "local_streak": int(child.local_streak), "gate_count": int(child.gate_count),
                 "depth": int(child.depth)})
+        beam = [r[0] for r in records]
+        # the reference's own beam-level dump line for the new beam
+        # (paged_rollout_benchmark.py:213-239)
+        with tempfile.TemporaryDirectory() as tmp:
+            dump = Path(tmp) / "levels.jsonl"
+            prb.append_beam_level(dump, step + 1, beam)
+            level_line = dump.read_text()
         out["steps"].append({
             "proposals": [[p.parent, p.xfer_id, p.anchor_slot, list(p.binding),
                            p.next_gate_count] for p in proposals],
             "attempted": attempted, "invalid": invalid, "duplicates": duplicates,
-            "children": children})
-        beam = [r[0] for r in records]
+            "children": children, "beam_level_line": level_line})
     return {"json": np.array(json.dumps(out))}
 
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, required=True,
+                        help="path of the reference repository checkout (imported read-only)")
     parser.add_argument("--only", default="")
     args = parser.parse_args()
     sys.path.insert(0, str(args.reference))
@@ -296,6 +306,8 @@ def main() -> None:
         np.savez_compressed(HERE / "model_cpu_equivalence.npz", **model_case(args.reference))
     if not only or "topology" in only:
         np.savez_compressed(HERE / "topology_accept.npz", **topology_case())
+    if not only or "checkpoint" in only:
+        np.savez_compressed(HERE / "checkpoint_tiny.npz", **checkpoint_case(args.reference))
     print("golden fixtures written to", HERE)
 
 
@@ -337,10 +349,11 @@ def random_prefixes(ref_graph, circuit_snapshot, rules, num_beams, num_actions, 
     return samples
 
 
-def model_case(reference: Path, *, seed=0, beams=8, actions=8):
+def model_case(reference: Path, *, seed=1, beams=16, actions=8, dag_nodes=64):
     """Full-prefix encode, one-token paged decode, paged readout, match logits,
     structural decode and threshold candidates of the reference model
-    (CPU equivalence configuration, seeded weights)."""
+    (CPU equivalence configuration, seeded weights): 16 beams with an
+    8-action prefix each over a random 64-node DAG, page size 4."""
     import dataset as ref_dataset
     import incremental_graph as ref_graph
     import paged_cache as ref_cache
@@ -373,7 +386,7 @@ def model_case(reference: Path, *, seed=0, beams=8, actions=8):
         state[k] = torch.from_numpy(v)
     model.load_state_dict(state)
 
-    circuit = synthetic.random_dag(48, 8, seed + 1)
+    circuit = synthetic.random_dag(dag_nodes, 8, seed + 1)
     snapshot = circuit.snapshot()
     samples = random_prefixes(ref_graph, snapshot, rules, beams, actions, seed + 2)
     batch = ref_dataset.collate_prefixes(samples, ref_rules)
@@ -446,6 +459,51 @@ def model_case(reference: Path, *, seed=0, beams=8, actions=8):
         out["decode_batch"], out["decode_sources"], out["decode_anchors"] = bi.numpy(), so.numpy(), sl.numpy()
         out["decode_bindings"], out["decode_valid"] = bindings.numpy(), valid.numpy()
     out["seed"] = np.int64(seed)
+    return out
+
+
+def checkpoint_case(reference: Path, *, seed=4, beams=3, actions=4):
+    """A trainer-style checkpoint payload of a tiny reference model built by
+    the reference's own build_model (model_factory.py:7-41), saved the way
+    train.py:482-490 saves it, with the reference model's full-prefix encode
+    of a small seeded batch (paged_model.py:657-777)."""
+    import dataset as ref_dataset
+    import incremental_graph as ref_graph
+    import model_factory as ref_factory
+    from graph_rewrite_system_b200 import synthetic
+
+    rules = synthetic.small_rules()
+    ref_rules = ref_dataset.RuleMetadata.from_payload({
+        "source_patterns": list(rules.source_patterns),
+        "xfer_to_source": list(rules.xfer_to_source),
+        "xfer_sources": list(rules.xfer_sources),
+        "xfer_destinations": list(rules.xfer_destinations)})
+    args = {"architecture": "paged_action", "width": 32, "retrieval_width": 16,
+            "graph_layers": 1, "action_layers": 1, "action_heads": 2,
+            "max_sequence_length": 16, "readout_graph_layers": 1,
+            "readout_attention_backend": "sdpa", "lr": 3e-4}
+    model = ref_factory.build_model(ref_rules, rules.num_xfers, args).eval()
+    g = torch.Generator().manual_seed(seed)
+    state = model.state_dict()
+    for name, value in state.items():
+        if value.is_floating_point():
+            state[name] = torch.randn(value.shape, generator=g) * 0.1 + (
+                1.0 if name.endswith("norm.weight") else 0.0)
+    model.load_state_dict(state)
+    circuit = synthetic.random_dag(32, 8, seed)
+    samples = random_prefixes(ref_graph, circuit.snapshot(), rules, beams, actions, seed + 1)
+    batch = ref_dataset.collate_prefixes(samples, ref_rules)
+    with torch.no_grad():
+        states, live, types = model.encode(batch)
+    payload = {"model": model.state_dict(), "args": args, "metrics": {"loss": 0.0},
+               "format": "paged_action_binding"}
+    torch.save(payload, HERE / "checkpoint_tiny.pt")
+    out = {"batch_" + k: batch[k].numpy() for k in (
+        "initial_types", "edge_batch", "edge_src", "edge_dst", "edge_relation",
+        "current_types", "current_edge_batch", "current_edge_src", "current_edge_dst",
+        "current_edge_relation", "action_xfers", "action_sources", "binding_slots",
+        "destination_slots", "destination_types")}
+    out.update(encode_states=states.numpy(), encode_live=live.numpy(), encode_types=types.numpy())
     return out
 
 

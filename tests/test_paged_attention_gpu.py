@@ -186,3 +186,68 @@ def test_cluster_decode_takes_the_cluster_kernel(cuda_device):
                                  shared_value=f(w.shared_value))
     np.testing.assert_allclose(out.float().cpu().numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
     check_decode_status(cuda_device)
+
+
+@pytest.mark.parametrize("batch,heads,page,cap,max_len,current", [
+    (1000, 8, 16, 300, 63, True), (37, 6, 8, 90, 64, True), (21, 16, 4, 200, 150, True),
+    (33, 8, 16, 100, 129, False), (5, 1, 16, 10, 16, True), (64, 8, 16, 64, 1, True)])
+def test_causal_decode_bf16(cuda_device, batch, heads, page, cap, max_len, current):
+    """One query per (beam, head) with the current token: the page-staged
+    causal decode kernel (lengths 0, chunk-sized, multi-chunk)."""
+    out, exp = _random_case(11 + batch, batch, heads, 32, page, cap, 1, max_len, torch.bfloat16,
+                            cuda_device, current=current)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+
+
+def _causal_abi(dev, q, kc, vc, table, lengths, ck, cv, valid, out, status):
+    from graph_rewrite_system_b200 import _lib
+
+    return _lib.lib().grs_decode_causal(
+        q.data_ptr(), q.stride(0), q.stride(1), kc.data_ptr(), vc.data_ptr(), kc.stride(0),
+        kc.stride(1), kc.stride(2), table.data_ptr(), table.stride(0), lengths.data_ptr(),
+        kc.shape[0], ck.data_ptr(), cv.data_ptr(), ck.stride(0), ck.stride(1), valid.data_ptr(),
+        out.data_ptr(), out.stride(0), out.stride(1), q.shape[0], q.shape[1], kc.shape[1],
+        status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+
+
+def test_causal_decode_takes_the_kernel_and_flags_bad_pages(cuda_device):
+    """The rollout's layout (8 heads x 32, page 16, query and current rows
+    strided inside a QKV buffer) is accepted by grs_decode_causal itself; a
+    page id outside the arena sets GRS_ERR_BAD_PAGE and its tokens are
+    skipped, leaving the other beams exact."""
+    dev = cuda_device
+    g = torch.Generator().manual_seed(5)
+    b, h, page, cap = 64, 8, 16, 40
+    qkv = torch.randn(b, 3, h, 32, generator=g).bfloat16()
+    kc = torch.randn(cap, page, h, 32, generator=g).bfloat16()
+    vc = torch.randn(cap, page, h, 32, generator=g).bfloat16()
+    table = torch.randint(0, cap, (b, 4), generator=g, dtype=torch.int32)
+    lengths = torch.randint(0, 64, (b,), generator=g, dtype=torch.int32)
+    valid = torch.rand(b, generator=g) > 0.1
+    q, k, v = qkv.unbind(1)
+    exp = oracle.paged_attention(q.float().unsqueeze(2), kc.float(), vc.float(), table, lengths,
+                                 current_key=k.float(), current_value=v.float(),
+                                 current_valid=valid).squeeze(2)
+    qkv_d = qkv.to(dev)
+    qd, kd, vd = qkv_d.unbind(1)
+    out = torch.empty(b, h, 32, device=dev, dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    rc = _causal_abi(dev, qd, kc.to(dev), vc.to(dev), table.to(dev), lengths.to(dev), kd, vd,
+                     valid.to(dev), out, status)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    np.testing.assert_allclose(out.float().cpu().numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+    # beam 3 points one used page at an id past the arena
+    lengths[3] = 40
+    table[3, 1] = cap + 7
+    good = torch.ones(b, dtype=torch.bool)
+    good[3] = False
+    rc = _causal_abi(dev, qd, kc.to(dev), vc.to(dev), table.to(dev), lengths.to(dev), kd, vd,
+                     valid.to(dev), out, status)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == -2                     # GRS_ERR_BAD_PAGE
+    np.testing.assert_allclose(out.float().cpu().numpy()[good.numpy()],
+                               exp.numpy()[good.numpy()], rtol=2e-2, atol=2e-2)
+    assert torch.isfinite(out.float()).all()

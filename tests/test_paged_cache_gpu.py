@@ -74,12 +74,20 @@ def test_exhaustion_and_refcount_errors(cuda_device):
         cache2.block_table([PrefixHandle((1, 2), 1)])
 
 
-def test_bf16_churn_matches_oracle(cuda_device):
-    """Config-3 semantics at small scale, bf16 arenas, device-native API."""
+@pytest.mark.parametrize("beams,depth,checked", [(64, 40, 8), (1000, 64, 40)])
+def test_bf16_churn_matches_oracle(cuda_device, beams, depth, checked):
+    """Cache churn with bf16 arenas through the device-native API, bit-exact
+    against the oracle: each step forks every beam into 5 children with
+    seeded uniform scores, keeps the top `beams` (stable, ties by index),
+    appends one token per survivor in all arenas (COW on partial tail pages)
+    and releases the old handles (refcount reclaim).  The second case is the
+    full churn workload: 1000 beams, 4 layers x 8 heads x 32, page 16, depth
+    64.  Block tables, refcounts and the free list are compared in full, arena
+    rows at every valid position of `checked` handles spread over the beam."""
     from graph_rewrite_system_b200.paged_cache import PagedKVCache
     from oracle.paged_cache import OraclePagedKVCache
 
-    layers, heads, hw, width, page, beams, depth = 4, 8, 32, 256, 16, 64, 40
+    layers, heads, hw, width, page = 4, 8, 32, 256, 16
     cap = beams * (-(-depth // page) + 3)
     dev = PagedKVCache(layers=layers, capacity=cap, page_size=page, heads=heads, head_width=hw,
                        model_width=width, device=cuda_device, dtype=torch.bfloat16)
@@ -112,8 +120,11 @@ def test_bf16_churn_matches_oracle(cuda_device):
     rows = table.cpu()
     for i, h in enumerate(handles):
         assert rows[i, : len(h.blocks)].tolist() == list(h.blocks)
+    assert dev.allocated_pages == ref.allocated_pages
+    assert cl.tolist() == [h.length for h in handles]
     # arena contents at every valid token position
-    for i, h in enumerate(handles[:8]):
+    stride = max(1, len(handles) // checked)
+    for h in handles[::stride][:checked]:
         for pos in range(h.length):
             p, r = h.blocks[pos // page], pos % page
             assert torch.equal(dev.keys[:, p, r].cpu(), ref.keys[:, p, r])

@@ -2,8 +2,8 @@
 
 fp32: the per-level decisions (every accepted child's parent, xfer and
 binding, in order), the accept/duplicate/invalid counts, the proposal and
-expansion metrics and the final 64-bit topology fingerprints must match
-exactly.  bf16 at the rollout model's shape: the search runs, the device
+expansion metrics, the final 64-bit topology fingerprints and the exported
+beam-level history lines must match exactly.  bf16 at the rollout model's shape: the search runs, the device
 topology types equal the model's live-slot types, every invariant holds and
 the cache returns every page.
 """
@@ -36,6 +36,7 @@ SMALL = dict(width=64, retrieval_width=32, graph_layers=1, action_layers=2, acti
 @pytest.mark.parametrize("seed", [3, 4])
 def test_fp32_rollout_matches_oracle(cuda_device, seed):
     from graph_rewrite_system_b200 import synthetic
+    from graph_rewrite_system_b200.history import BeamHistoryRecorder, beam_level_line
     from graph_rewrite_system_b200.rollout import DeviceBeamSearch
     from oracle.rollout import OracleBeamSearch
     from oracle.topology import node_component  # noqa: F401  (same hash family)
@@ -48,6 +49,7 @@ def test_fp32_rollout_matches_oracle(cuda_device, seed):
     oracle.reset()
     search = DeviceBeamSearch(model, rules, circuit, rc, cuda_device)
     search.reset()
+    recorder = BeamHistoryRecorder(search)
     for _ in range(rc.depth):
         exp = oracle.step()
         got = search.step()
@@ -55,6 +57,10 @@ def test_fp32_rollout_matches_oracle(cuda_device, seed):
             assert got is None
             break
         assert got is not None
+        # the exported JSONL line of the level equals the oracle beam's
+        recorder.record()
+        assert beam_level_line(recorder.depth, recorder.states()) == beam_level_line(
+            got.step, [(n.gate_count, n.history) for n in oracle.beam])
         for key in ("accepted_actions", "attempted_actions", "invalid_structural_actions",
                     "duplicate_speculative_successors", "proposals_after_caps",
                     "predicted_actions", "eligible_actions_before_parent_cap"):
