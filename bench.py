@@ -1,7 +1,7 @@
 """Benchmark of the B200 beam-search decode path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload rollout|decode-attention|update-gemm]
+                    [--workload rollout|decode-attention|update-gemm|graph-mlp]
 
 Workloads (seeded synthetic inputs; the reference's hwb6 circuit, rule set
 and checkpoint are not available):
@@ -19,6 +19,9 @@ and checkpoint are not available):
 * ``update-gemm``: the readout graph layers' update projection with its GELU
   as one tcgen05 tensor-core launch, GELU(x [300000, 512] @ W^T + b), against
   the library GEMM + bias+GELU pair on the same inputs.
+* ``graph-mlp``: one readout graph layer's update MLP + residual + LayerNorm
+  as one fused tensor-core launch (the GELU activation never leaves shared
+  memory), M = 300000 rows, against the same layer as two GEMM launches.
 * ``decode-attention``: the shared-prefix paged decode microbenchmark -
   512 beams, one query token each, 8 heads x 32, bf16, 381 shared s0 node
   keys, 64 action K/V entries per beam in pages of 16, block tables from a
@@ -60,14 +63,35 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "beam-state decode steps/s at B=1000,T=64; paged-attn HBM GB/s vs peak"
-PROBE_LEAD_CYCLES = 40_000             # ~20 us at 1.965 GHz
+PROBE_LEAD_US = 15.0                  # device busy time ahead of a probed launch
 DECODE_INPUT_COPIES = 16              # 16 x ~11.2 MB = 180 MB > 126 MB L2
+_SLEEP_RATE: list[float] = []
 
 
-def queue_ahead_cycles(steps: int) -> int:
-    """GPU sleep long enough for the host to enqueue `steps` API calls
-    (~200 us each at 1.965 GHz), at least ~30 ms."""
-    return max(60_000_000, steps * 400_000)
+def sleep_cycles_per_us() -> float:
+    """torch.cuda._sleep counts a device clock whose rate is not the SM
+    clock's; measure it once against CUDA events (cycles per microsecond)."""
+    if not _SLEEP_RATE:
+        cycles = 2_000_000
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        torch.cuda._sleep(cycles)
+        b.record()
+        torch.cuda.synchronize()
+        _SLEEP_RATE.append(cycles / max(a.elapsed_time(b) * 1e3, 1e-3))
+    return _SLEEP_RATE[0]
+
+
+def device_sleep_us(us: float) -> None:
+    """Keep the current stream busy for about `us` microseconds."""
+    torch.cuda._sleep(max(1, int(us * sleep_cycles_per_us())))
+
+
+def queue_ahead_us(steps: int) -> float:
+    """Device sleep long enough for the host to enqueue `steps` API calls
+    (~200 us each), at least 30 ms."""
+    return max(30_000.0, steps * 200.0)
 
 L2_FLUSH_BYTES = 256 << 20
 
@@ -105,7 +129,7 @@ class KernelProbe:
             end = torch.cuda.Event(enable_timing=True)
             # keep the device busy while the host issues the launch, so the
             # events bracket the kernel and not the host call (~20 us)
-            torch.cuda._sleep(PROBE_LEAD_CYCLES)
+            device_sleep_us(PROBE_LEAD_US)
             start.record()
             out = self.original(*a, **kw)
             end.record()
@@ -290,7 +314,7 @@ def run_decode_attention(args, world, rank, device):
     with ClockSampler(device.index) as clocks:
         # hold the device while the host enqueues the timed launches, so the
         # events bracket device time and not the Python call overhead
-        torch.cuda._sleep(queue_ahead_cycles(args.steps))
+        device_sleep_us(queue_ahead_us(args.steps))
         launches0 = launch_count()
         start.record(stream)
         for i in range(args.steps):
@@ -304,7 +328,7 @@ def run_decode_attention(args, world, rank, device):
 
     # the same launch alone after an L2 flush (launch latency included)
     single = []
-    torch.cuda._sleep(queue_ahead_cycles(args.steps))
+    device_sleep_us(queue_ahead_us(args.steps))
     for i in range(args.steps):
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -667,9 +691,9 @@ def run_reference(args, world, rank):
     """--impl reference: the CPU oracle on the same workload (rank 0 only)."""
     if rank != 0:
         return None
-    if args.workload == "update-gemm":
-        return {"impl": "reference", "unavailable": "the update-gemm microbenchmark has no CPU "
-                "arm; the rollout workload's reference arm times the CPU oracle"}
+    if args.workload in ("update-gemm", "graph-mlp"):
+        return {"impl": "reference", "unavailable": f"the {args.workload} microbenchmark has no "
+                "CPU arm; the rollout workload's reference arm times the CPU oracle"}
     if args.workload == "rollout":
         started = time.perf_counter()
         steps, first = rollout_window(args.steps, args.warmup)
@@ -752,7 +776,7 @@ def run_update_gemm(args, world, rank, device):
         barrier(world, device)
         events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(steps)]
-        torch.cuda._sleep(queue_ahead_cycles(steps))
+        device_sleep_us(queue_ahead_us(steps))
         for i, (s0, s1) in enumerate(events):
             s0.record(stream)
             fn(i)
@@ -806,14 +830,112 @@ def run_update_gemm(args, world, rank, device):
     }
 
 
+def run_graph_mlp(args, world, rank, device):
+    """One readout graph layer's update as one tensor-core launch:
+    LayerNorm(x + GELU([x | agg] U0^T + b0) U2^T + b2) * live over
+    M = 300000 rows (beam 1000 x 300 slots), width 256, bf16; the [M, 512]
+    GELU activation stays in shared memory.  Two rotating inputs of 307 MB
+    (larger than L2).  The same layer as two tensor-core GEMMs with fused
+    epilogues (GELU; residual + LayerNorm), which write and re-read the
+    activation, is timed beside it."""
+    from graph_rewrite_system_b200 import kernels as K
+
+    m = 300000
+    gen = torch.Generator(device=device).manual_seed(rank + 11)
+    xs = [torch.randn(m, 512, device=device, generator=gen).to(torch.bfloat16) for _ in range(2)]
+    u0 = (torch.randn(512, 512, device=device, generator=gen) / 512 ** 0.5).to(torch.bfloat16)
+    u2 = (torch.randn(256, 512, device=device, generator=gen) / 512 ** 0.5).to(torch.bfloat16)
+    b0 = torch.randn(512, device=device, generator=gen) * 0.1
+    b2 = torch.randn(256, device=device, generator=gen) * 0.1
+    gamma = 1 + 0.1 * torch.randn(256, device=device, generator=gen)
+    beta = 0.1 * torch.randn(256, device=device, generator=gen)
+    live = torch.rand(m, device=device, generator=gen) > 0.3
+    out = torch.empty(m, 256, device=device, dtype=torch.bfloat16)
+    hidden = torch.empty(m, 512, device=device, dtype=torch.bfloat16)
+    status = torch.zeros(1, device=device, dtype=torch.int32)
+    stream = torch.cuda.current_stream(device)
+    flops = 2.0 * m * 512 * (512 + 256)
+
+    def fused(i):
+        x = xs[i % 2]
+        K.graph_mlp(x, u0, b0, u2, b2, x[:, :256], gamma, beta, zero_row=live, out=out,
+                    status=status)
+
+    def two_gemms(i):
+        x = xs[i % 2]
+        K.gemm(x, u0, b0, gelu=True, out=hidden, status=status)
+        K.gemm_layernorm(hidden, u2, b2, x[:, :256], gamma, beta, zero_row=live, out=out,
+                         status=status)
+
+    def timed(fn, steps):
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(steps)]
+        device_sleep_us(queue_ahead_us(steps))
+        for i, (s0, s1) in enumerate(events):
+            s0.record(stream)
+            fn(i)
+            s1.record(stream)
+        torch.cuda.synchronize(device)
+        return max_over_ranks(sum(a.elapsed_time(z) for a, z in events), world, device) / steps
+
+    launches0 = launch_count()
+    with ClockSampler(device.index) as clocks:
+        ms = timed(fused, args.steps)
+    launches = launch_count() - launches0
+    two_ms = timed(two_gemms, args.steps)
+    if int(status.item()):
+        raise RuntimeError(f"tensor-core kernel reported status {int(status.item())}")
+    host_x = xs[0].cpu().pin_memory()
+    host_out = torch.empty(m, 256, dtype=torch.bfloat16).pin_memory()
+    dev_x = torch.empty_like(xs[0])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(3):
+        dev_x.copy_(host_x, non_blocking=True)
+        K.graph_mlp(dev_x, u0, b0, u2, b2, dev_x[:, :256], gamma, beta, zero_row=live,
+                    out=out, status=status)
+        host_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / 3, world, device)
+    peaks = measured_peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic_ratio = profiled_traffic("graph_mlp_traffic_ratio")
+    algorithmic_bytes = 2.0 * (m * 512 + 512 * 512 + 256 * 512 + m * 256) + m + 4 * 1280
+    return {
+        "metric": "graph-layer update (GELU MLP + residual + LayerNorm) throughput",
+        "value": world * achieved, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "graph-mlp: LayerNorm(x + GELU([x|agg] U0^T + b0) U2^T + b2) * live, "
+                               "M = 300000, width 256, bf16, two rotating 307 MB inputs "
+                               "(larger than L2)",
+                   "two_tensor_core_gemms_ms": two_ms, "speedup_vs_two_gemms": two_ms / ms},
+        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": m * 512 * 2, "d2h_bytes_per_step": m * 256 * 2},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                     "traffic": traffic_ratio * algorithmic_bytes if traffic_ratio else None,
+                     "kernel": "graph_mlp_kernel", "algorithmic_bytes_per_launch": algorithmic_bytes,
+                     "hbm_frac": algorithmic_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                     "peak_source": f"{peaks['source']} bf16_tflops (burst)"},
+        "clocks": clocks.summary(),
+    }
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=60)
     parser.add_argument("--warmup", type=int, default=4)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    parser.add_argument("--workload", choices=("rollout", "decode-attention", "update-gemm"),
-                        default="rollout")
+    parser.add_argument("--workload", choices=("rollout", "decode-attention", "update-gemm",
+                                               "graph-mlp"), default="rollout")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--beam", type=int, default=1000,
                         help="rollout beam size (1000 is the benchmark configuration)")
@@ -835,6 +957,7 @@ def main() -> None:
     world, rank, local = dist_setup(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    sleep_cycles_per_us()            # calibrate the device sleep before any timed region
     if args.workload == "rollout":
         line = run_rollout(args, world, rank, device)
         if not args.no_attention:
@@ -844,6 +967,8 @@ def main() -> None:
                 "value", "unit", "ms_per_step", "roofline", "config")}
     elif args.workload == "update-gemm":
         line = run_update_gemm(args, world, rank, device)
+    elif args.workload == "graph-mlp":
+        line = run_graph_mlp(args, world, rank, device)
     else:
         line = run_decode_attention(args, world, rank, device)
     if rank == 0:

@@ -50,7 +50,9 @@ struct GtShape {
   static constexpr int kStages = BN == 256 ? 3 : BN == 128 ? 4 : 6;
   static constexpr int kEpiWarps = BN >= 64 ? 4 * (BN / 64) : 4;
   static constexpr int kThreads = (2 + kEpiWarps) * 32;
-  static constexpr int kStaging = BN >= 64 ? kEpiWarps * GT_OUT_BYTES : 0;
+  // BN < 64 is the logits epilogue: each warp stages its 32 rows of <= 32
+  // fp32 logits and <= 32 eligibility bytes
+  static constexpr int kStaging = BN >= 64 ? kEpiWarps * GT_OUT_BYTES : kEpiWarps * 32 * 32 * 5;
   static constexpr int kSmem = kStages * kStage + kStaging + 1024;   // + alignment slack
 };
 
@@ -147,6 +149,47 @@ __device__ __forceinline__ void stage_row_chunks(uint8_t* stage, int lane, int c
     *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
         make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
   }
+}
+
+// 64 consecutive bf16 of a row (128 bytes, 16-byte aligned) into registers,
+// or zeros when the row is past the end
+__device__ __forceinline__ void load_row64(const __nv_bfloat16* src, bool in, uint4 r[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    r[j] = in ? *reinterpret_cast<const uint4*>(src + 8 * j) : make_uint4(0, 0, 0, 0);
+}
+
+// v[0..31] += the 32 bf16 held in r[0..3]
+__device__ __forceinline__ void add_regs32(float v[32], const uint4 r[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r[j]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      v[8 * j + 2 * k] += f.x;
+      v[8 * j + 2 * k + 1] += f.y;
+    }
+  }
+}
+
+// exact mean and centred sum of squares of 64 values
+__device__ __forceinline__ void stats64(const float v[64], float& mean, float& m2) {
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 64; j += 2) {
+    s0 += v[j];
+    s1 += v[j + 1];
+  }
+  mean = (s0 + s1) * (1.f / 64.f);
+  float q0 = 0.f, q1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 64; j += 2) {
+    const float d0 = v[j] - mean, d1 = v[j + 1] - mean;
+    q0 = fmaf(d0, d0, q0);
+    q1 = fmaf(d1, d1, q1);
+  }
+  m2 = q0 + q1;
 }
 
 __device__ __forceinline__ void pack_bf16x32(const float v[32], uint32_t packed[16]) {
@@ -260,6 +303,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int m0 = (t / n_tiles) * GT_BM, n0 = (t % n_tiles) * BN;
       const int b = i & 1, u = i >> 1;
+      const int row = m0 + quarter * 32 + lane;
+      const bool in = row < M;
+      const bool zero = in && e.zero_row != nullptr && e.zero_row[row] == 0;
       if (!mbar_wait_warp(&tmem_full[b], u & 1)) {
         failed = 1;
         break;
@@ -267,9 +313,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       tc_fence_after();
       if (lane == 0) tma_store_wait_read();   // this warp's previous block has left smem
       __syncwarp();
-      const int row = m0 + quarter * 32 + lane;
-      const bool in = row < M;
-      const bool zero = in && e.zero_row != nullptr && e.zero_row[row] == 0;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         const int col = cgroup * 64 + c * 32;
@@ -319,15 +362,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       const int b = i & 1, u = i >> 1;
       // after a wait gave up, the warp still runs every named barrier so the
       // other warps of its quarter are not left waiting
-      if (!gave_up && !mbar_wait_warp(&tmem_full[b], u & 1)) {
-        gave_up = true;
-        failed = 1;
-      }
-      tc_fence_after();
-      if (lane == 0) tma_store_wait_read();
-      __syncwarp();
       const int row = m0 + quarter * 32 + lane;
       const bool in = row < M;
+      // the row's residual, scale and masks are read before the wait (their
+      // latency hides behind the tile's MMAs)
+      uint4 res[8];
+      load_row64(e.residual + (int64_t)row * e.ldr + cgroup * 64, in, res);
       const int64_t beam = in ? row / e.rows_per_beam : 0;
       const float sc = (in && e.row_scale) ? e.row_scale[row] : 1.f;
       bool zc = true, wc = true;
@@ -337,6 +377,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
         if (e.where_beam) wc = wc && e.where_beam[beam] != 0;
         if (e.where_len) wc = wc && e.where_len[beam] > 0;
       }
+      if (!gave_up && !mbar_wait_warp(&tmem_full[b], u & 1)) {
+        gave_up = true;
+        failed = 1;
+      }
+      tc_fence_after();
+      if (lane == 0) tma_store_wait_read();
+      __syncwarp();
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN);
       // v = residual + row_scale * (acc + bias) for one 32-column chunk
       const auto load_row = [&](int c, float v[32]) {
@@ -347,7 +394,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] *= sc;
         }
-        if (in) add_row32(v, e.residual + (int64_t)row * e.ldr + col);
+        add_regs32(v, res + 4 * c);
       };
       // this thread's 64 columns: exact mean and centred sum of squares of
       // each 32-column chunk, merged (Chan, Golub & LeVeque's pairwise update)
@@ -408,7 +455,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
         } else if (!wc) {             // the row keeps its input
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = 0.f;
-          add_row32(r, e.residual + (int64_t)row * e.ldr + col);
+          add_regs32(r, res + 4 * c);
         } else {
           const float4* g4 = reinterpret_cast<const float4*>(e.gamma + col);
           const float4* b4 = reinterpret_cast<const float4*>(e.beta + col);
@@ -435,14 +482,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
     }
     if (lane == 0) tma_store_wait_all();
   } else {
-    // LOGITS (BN == 32): one thread per row reads its 32 accumulator columns
-    // and writes the row's fp32 logits and eligibility directly
+    // LOGITS (BN == 32): one thread per row reads its 32 accumulator columns;
+    // a warp's 32 rows of logits (and of eligibility bytes) are contiguous in
+    // the outputs, so they are staged in shared memory row by row and written
+    // with 16-byte stores across the warp
     static_assert(BN == 32, "the logits epilogue reads one 32-column accumulator");
     const int quarter = warp & 3;
+    const int ns = e.num_sources;
+    float* lstage = reinterpret_cast<float*>(smem + S::kStages * S::kStage) + (warp - 2) * 32 * 32;
+    uint8_t* estage = smem + S::kStages * S::kStage + S::kEpiWarps * 32 * 32 * 4 +
+                      (warp - 2) * 32 * 32;
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int m0 = t * GT_BM;
       const int b = i & 1, u = i >> 1;
+      const int r0 = m0 + quarter * 32;             // this warp's first row
+      const int row = r0 + lane;
+      const bool alive = row < M && e.live[row] != 0;
+      const int64_t type = row < M ? e.types[row] : -1;
       if (!mbar_wait_warp(&tmem_full[b], u & 1)) {
         failed = 1;
         break;
@@ -453,21 +510,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[b]);
-      const int row = m0 + quarter * 32 + lane;
-      if (row < M) {
-        const bool alive = e.live[row] != 0;
-        const int64_t type = e.types[row];
-        float* lo = e.logits + (int64_t)row * e.num_sources;
-        uint8_t* el = e.eligible + (int64_t)row * e.num_sources;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (j < e.num_sources) {
-            const bool ok = alive && type == __ldg(e.first_types + j);
-            lo[j] = ok ? v[j] * e.logit_scale + __ldg(e.bias + j) : -1e4f;
-            el[j] = ok;
-          }
+      for (int j = 0; j < 32; ++j) {
+        if (j < ns) {
+          const bool ok = alive && type == __ldg(e.first_types + j);
+          lstage[lane * ns + j] = ok ? v[j] * e.logit_scale + __ldg(e.bias + j) : -1e4f;
+          estage[lane * ns + j] = ok;
         }
       }
+      __syncwarp();
+      const int rows = min(32, M - r0);
+      float* lo = e.logits + (int64_t)r0 * ns;
+      uint8_t* el = e.eligible + (int64_t)r0 * ns;
+      const int nf = rows * ns, nb = rows * ns;
+      if (((reinterpret_cast<uintptr_t>(lo) | reinterpret_cast<uintptr_t>(el)) & 15) == 0) {
+        for (int k = lane; k < nf / 4; k += 32)
+          reinterpret_cast<float4*>(lo)[k] = reinterpret_cast<const float4*>(lstage)[k];
+        for (int k = (nf / 4) * 4 + lane; k < nf; k += 32) lo[k] = lstage[k];
+        for (int k = lane; k < nb / 16; k += 32)
+          reinterpret_cast<uint4*>(el)[k] = reinterpret_cast<const uint4*>(estage)[k];
+        for (int k = (nb / 16) * 16 + lane; k < nb; k += 32) el[k] = estage[k];
+      } else {
+        for (int k = lane; k < nf; k += 32) lo[k] = lstage[k];
+        for (int k = lane; k < nb; k += 32) el[k] = estage[k];
+      }
+      __syncwarp();
     }
   }
   __syncwarp();
@@ -880,17 +947,24 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
         __syncwarp();
         if (lane == 0) mbar_arrive(half == 0 ? h0_done : h1_done);
       }
-      // ---- GEMM 2 epilogue: + b2 + residual, LayerNorm, dead rows, TMA store
+      // ---- GEMM 2 epilogue: + b2 + residual, LayerNorm, dead rows, TMA store.
+      // The row's residual and live flag are read before the wait, so their
+      // latency hides behind the second GEMM; the accumulator is read once.
+      uint4 res[8];
+      load_row64(e.residual + (int64_t)row * e.ldr + cgroup * 64, in, res);
+      const bool keep = !in || e.zero_row == nullptr || e.zero_row[row] != 0;
       if (ok && !mbar_wait_warp(p2_full, i & 1)) {
         ok = false;
         *failed = 1;
       }
       tc_fence_after();
       const uint32_t taddr = x_reg + lane_base + (uint32_t)(cgroup * 64);
+      // v = acc + b2 + residual for one 32-column chunk (the accumulator is
+      // read twice, once for the statistics and once for the output)
       const auto load_row = [&](int c, float v[32]) {
         tmem_load32(taddr + c * 32, v);
         add_bias32(v, e.b2 + cgroup * 64 + c * 32);
-        if (in) add_row32(v, e.residual + (int64_t)row * e.ldr + cgroup * 64 + c * 32);
+        add_regs32(v, res + 4 * c);
       };
       float mean_t = 0.f, m2_t = 0.f;
 #pragma unroll 1
@@ -905,12 +979,12 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float d = v[j] - mc;
-          m2c += d * d;
+          m2c = fmaf(d, d, m2c);
         }
         if (c == 0) {
           mean_t = mc;
           m2_t = m2c;
-        } else {
+        } else {                       // two halves of 32: n_a n_b / n = 16
           const float delta = mc - mean_t;
           mean_t += 0.5f * delta;
           m2_t += m2c + 16.f * delta * delta;
@@ -929,7 +1003,6 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       const float mean = mean01 + 0.5f * dd;
       const float var = (m201 + m223 + 64.f * dd * dd) * (1.f / 256.f);
       const float rstd = rsqrtf(var + e.eps);
-      const bool keep = !in || e.zero_row == nullptr || e.zero_row[row] != 0;
       uint8_t* stage = hid + cgroup * GT_A_BYTES + quarter * 32 * 128;   // this warp's block
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {

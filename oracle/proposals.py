@@ -74,3 +74,94 @@ def rank_proposals(batch_ids, sources, anchors, bindings, probabilities,
         "probability": prob[sel], "next_gate": next_gate[sel], "row": sel,
         "candidate": rows[sel],
     }, {"predicted_actions": predicted, "eligible_actions": expanded}
+
+
+def rank_proposals_exploration(primary: dict, exploration: dict, parent_gate_counts, index, *,
+                               per_parent_cap: int, exploration_per_parent: int,
+                               global_cap: int):
+    """Proposals from a primary and an exploration model's candidates with a
+    per-parent exploration quota: build_legacy_proposals
+    (paged_rollout_benchmark.py:101-210) over candidates expanded like
+    expand_action_rows (:88-98).
+
+    `primary` / `exploration`: dicts of candidate arrays (batch_ids,
+    sources, anchors, bindings [n, P] -1 padded, probabilities), each in its
+    model's candidate order.  Per parent: each model's actions with an
+    allowed gate delta, stably sorted by (next_gate, -probability, xfer); the
+    first cap - quota primary actions, then exploration actions whose
+    (xfer, anchor, binding) is not yet taken, then the remaining primary
+    ones, until the cap; the parent's list stably re-sorted by the same key.
+    All parents' lists, in parent order, stably sorted by (next_gate,
+    -probability, parent gate) and cut at global_cap.  Returned rows index
+    the concatenated candidate table [primary rows | exploration rows]."""
+    pgc = np.asarray(parent_gate_counts, np.int64)
+    quota = min(exploration_per_parent, per_parent_cap)
+    primary_limit = per_parent_cap - quota
+
+    def expand(cand, offset):
+        """Per parent: (next_gate, -prob, xfer, anchor, binding, prob, row, parent) in
+        expansion order, allowed deltas only; plus the predicted count."""
+        per, predicted = {}, 0
+        batch = np.asarray(cand["batch_ids"], np.int64)
+        sources = np.asarray(cand["sources"], np.int64)
+        for r in range(batch.size):
+            s = int(sources[r])
+            predicted += int(index["all_xfer_counts"][s])
+            start, count = int(index["xfer_offsets"][s]), int(index["xfer_counts"][s])
+            b = int(batch[r])
+            binding = tuple(int(v) for v in cand["bindings"][r] if v >= 0)
+            prob = float(np.float32(cand["probabilities"][r]))
+            for x in index["xfer_ids"][start:start + count].tolist():
+                ng = int(pgc[b] + index["gate_deltas"][x])
+                per.setdefault(b, []).append((ng, -prob, x, int(cand["anchors"][r]), binding,
+                                              prob, offset + r, b))
+        for rows in per.values():
+            rows.sort(key=lambda t: (t[0], t[1], t[2]))
+        return per, predicted
+
+    n_primary = np.asarray(primary["batch_ids"]).size
+    p_rows, p_pred = expand(primary, 0)
+    e_rows, e_pred = expand(exploration, n_primary)
+    proposals, eligible, e_eligible, selected_exploration = [], 0, 0, 0
+    for parent in range(pgc.size):
+        prim, expl = p_rows.get(parent, []), e_rows.get(parent, [])
+        eligible += len(prim)
+        e_eligible += len(expl)
+        chosen = list(prim[:primary_limit])
+        keys = {(t[2], t[3], t[4]) for t in chosen}
+        # the cap is checked after an append (:172-180): with no quota and a
+        # full primary list one exploration proposal still joins
+        for t in expl:
+            key = (t[2], t[3], t[4])
+            if key in keys:
+                continue
+            chosen.append(t)
+            keys.add(key)
+            selected_exploration += 1
+            if len(chosen) >= per_parent_cap:
+                break
+        if len(chosen) < per_parent_cap:
+            for t in prim[primary_limit:]:
+                key = (t[2], t[3], t[4])
+                if key in keys:
+                    continue
+                chosen.append(t)
+                keys.add(key)
+                if len(chosen) >= per_parent_cap:
+                    break
+        chosen.sort(key=lambda t: (t[0], t[1], t[2]))
+        proposals.extend(chosen)
+    proposals.sort(key=lambda t: (t[0], t[1], int(pgc[t[7]])))
+    proposals = proposals[:global_cap]
+    sel = {
+        "parent": np.asarray([t[7] for t in proposals], np.int64),
+        "xfer": np.asarray([t[2] for t in proposals], np.int64),
+        "anchor": np.asarray([t[3] for t in proposals], np.int64),
+        "binding": [t[4] for t in proposals],
+        "probability": np.asarray([t[5] for t in proposals], np.float32),
+        "next_gate": np.asarray([t[0] for t in proposals], np.int64),
+        "candidate": np.asarray([t[6] for t in proposals], np.int64),
+    }
+    return sel, {"predicted_actions": p_pred, "exploration_predicted_actions": e_pred,
+                 "eligible_actions": eligible, "exploration_eligible_actions": e_eligible,
+                 "selected_exploration_proposals": selected_exploration}

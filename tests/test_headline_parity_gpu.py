@@ -4,8 +4,9 @@ fp32 oracle on the same beam states.
 The model is the rollout workload's (width 256, 8 heads x 32, 4 causal
 layers, 4 readout graph layers, seeded random weights, bf16) on the 6-qubit
 259-gate synthetic circuit, beam 64, so a level's per-slot GEMMs have
-B x S >= 4096 rows and the tensor-core GEMMs with their GELU and
-residual+LayerNorm epilogues run (the test checks that they did).  After
+B x S >= 4096 rows; every projection runs on the tcgen05 GEMMs (plain and
+LayerNorm epilogues, the fused graph-layer MLP, the match-logits GEMM: the
+test checks that each ran).  After
 three levels of the device search:
 
 * one-token advance of level 3: the children's next states from the
@@ -69,18 +70,18 @@ def rollout(cuda_device):
     rules, cfg = synthetic.synthetic_rules(), synthetic.ROLLOUT_MODEL
     params = synthetic.deterministic_parameters(synthetic.parameter_shapes(cfg, rules), 0)
     oracle = OracleModel({k: torch.from_numpy(v) for k, v in params.items()}, rules, cfg)
-    calls = {"gelu": 0, "layernorm": 0}
-    originals = (K.gemm_bias_gelu, K.gemm_residual_layernorm)
+    names = ("gemm", "gemm_layernorm", "graph_mlp", "match_logits_gemm")
+    calls = dict.fromkeys(names, 0)
+    originals = {n: getattr(K, n) for n in names}
 
-    def gelu(*a, **kw):
-        calls["gelu"] += 1
-        return originals[0](*a, **kw)
+    def counting(name):
+        def call(*a, **kw):
+            calls[name] += 1
+            return originals[name](*a, **kw)
+        return call
 
-    def layernorm(*a, **kw):
-        calls["layernorm"] += 1
-        return originals[1](*a, **kw)
-
-    K.gemm_bias_gelu, K.gemm_residual_layernorm = gelu, layernorm
+    for n in names:
+        setattr(K, n, counting(n))
     try:
         search.reset()
         for _ in range(2):
@@ -96,9 +97,10 @@ def rollout(cuda_device):
         assert search.step() is not None
         search.check()
     finally:
-        K.gemm_bias_gelu, K.gemm_residual_layernorm = originals
+        for n in names:
+            setattr(K, n, originals[n])
     assert search.beams * search.slots >= 4096
-    assert calls["gelu"] > 0 and calls["layernorm"] > 0, calls
+    assert all(calls[n] > 0 for n in names), calls
     return search, oracle, rules, parents
 
 
