@@ -122,6 +122,10 @@ class KernelProbe:
         self.module, self.original = kernels, getattr(kernels, self.name)
 
         def timed(*a, **kw):
+            # launches recorded into a CUDA graph are not timed (and the
+            # probe's own sleep and events must not be captured with them)
+            if torch.cuda.is_current_stream_capturing():
+                return self.original(*a, **kw)
             self.calls += 1
             if self.calls % self.every:
                 return self.original(*a, **kw)
@@ -212,14 +216,23 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
-        time.sleep(0.3)
+        # the sampler's start-up (NVML initialisation) must be over before the
+        # timed region opens: wait for its first sample
+        deadline = time.time() + 10.0
+        while self.proc is not None and time.time() < deadline:
+            if os.path.getsize(self.path) > 0 and open(self.path).read().count("\n") >= 1:
+                break
+            time.sleep(0.02)
+        time.sleep(0.06)
+        self.window_start = time.time()
         return self
 
     def __exit__(self, *exc):
+        self.window_end = time.time()
         if self.proc is not None:
             self.proc.terminate()
             try:

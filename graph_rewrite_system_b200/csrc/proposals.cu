@@ -13,6 +13,7 @@
 // stable LSD radix sort; the expansion size never leaves the device (arrays
 // are sized by the host's upper bound and padded with keys that sort last).
 #include <cub/cub.cuh>
+#include <thrust/iterator/counting_iterator.h>
 
 #include "grs_common.cuh"
 
@@ -658,6 +659,441 @@ extern "C" int grs_proposals_rank_grouped(
     prop_grouped_output_kernel<<<ceil_div(global_cap, 256), 256, 0, grs::counted(s)>>>(
         key_out, val_out, global_cap, sel_row, sel_xfer, sel_next, n, out_row, out_xfer,
         out_next_gate, out_count);
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Proposals from a primary and an exploration model with a per-parent quota
+// (build_legacy_proposals, paged_rollout_benchmark.py:101-210; the search uses
+// it while a second model is loaded, :917-919, 937-961).
+//
+// The candidate table is the primary model's rows [0, c_primary) followed by
+// the exploration model's rows.  Per parent, each model's actions are ranked
+// (next gate, probability desc, xfer, expansion order); the parent keeps the
+// first cap - quota primary actions, then exploration actions whose
+// (xfer, anchor, binding) is not already kept - appending before checking
+// the cap, as the reference does - then the remaining primary actions that
+// are not duplicates, up to the cap.  An xfer fixes its source and both
+// models decode bindings on the same topology, so two actions share
+// (xfer, anchor, binding) exactly when their candidates share (parent,
+// source, anchor): a hash join of the two tables on that key pairs them.
+// The survivors are ordered by (next gate, probability desc, parent gate)
+// with ties in the order the parent's list is sorted by (next gate,
+// probability desc, xfer, position in the kept list) - two stable radix
+// sorts.
+// ---------------------------------------------------------------------------
+namespace grs {
+
+__global__ void prop_count_models_kernel(const int64_t* __restrict__ sources, int64_t c,
+                                         int64_t c_primary, const int32_t* __restrict__ xfer_counts,
+                                         const int32_t* __restrict__ all_counts, int num_sources,
+                                         int32_t* __restrict__ counts, int64_t* __restrict__ metrics,
+                                         int32_t* __restrict__ status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  long long v[4] = {0, 0, 0, 0};   // primary predicted, eligible; exploration predicted, eligible
+  if (i < c) {
+    const int64_t s = sources[i];
+    int cnt = 0, all = 0;
+    if (s >= num_sources) {
+      set_status(status, GRS_ERR_SHAPE);
+    } else if (s >= 0) {
+      cnt = xfer_counts[s];
+      all = all_counts[s];
+    }
+    counts[i] = cnt;
+    const int m = i >= c_primary ? 2 : 0;
+    v[m] = all;
+    v[m + 1] = cnt;
+  }
+  typedef cub::BlockReduce<long long, 256> Reduce;
+  __shared__ typename Reduce::TempStorage t[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const long long sum = Reduce(t[k]).Sum(v[k]);
+    if (threadIdx.x == 0 && sum)
+      atomicAdd(reinterpret_cast<unsigned long long*>(&metrics[k]), (unsigned long long)sum);
+  }
+}
+
+__global__ void prop_model_key_kernel(const int32_t* __restrict__ sorted_e, int64_t n,
+                                      const int32_t* __restrict__ total_ptr,
+                                      const uint32_t* __restrict__ e_parent,
+                                      const int32_t* __restrict__ e_row, int64_t c_primary,
+                                      uint32_t* __restrict__ pkey) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int e = sorted_e[i];
+  pkey[i] = e < *total_ptr ? e_parent[e] * 2u + (e_row[e] >= c_primary ? 1u : 0u) : PAD_PARENT;
+}
+
+// after the (parent, model) sort: every action's position and the bounds
+// of every (parent, model) segment (bounds preset to 0: empty)
+__global__ void prop_positions_kernel(const uint32_t* __restrict__ pkey,
+                                      const int32_t* __restrict__ sorted_e, int64_t n,
+                                      int32_t* __restrict__ pos_of, int32_t* __restrict__ seg_begin,
+                                      int32_t* __restrict__ seg_end) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t k = pkey[i];
+  if (k == PAD_PARENT) return;
+  pos_of[sorted_e[i]] = (int32_t)i;
+  if (i == 0 || pkey[i - 1] != k) seg_begin[k] = (int32_t)i;
+  if (i == n - 1 || pkey[i + 1] != k) seg_end[k] = (int32_t)(i + 1);
+}
+
+__device__ __forceinline__ bool candidate_key(int64_t parent, int64_t source, int64_t anchor,
+                                              uint64_t* key) {
+  if (parent < 0 || parent >= (1ll << 23) || source < 0 || source >= (1ll << 12) || anchor < 0 ||
+      anchor >= (1ll << 28))
+    return false;
+  *key = (((uint64_t)parent << 40) | ((uint64_t)source << 28) | (uint64_t)anchor) + 1;
+  return true;
+}
+
+// primary rows into an open-addressing table keyed by (parent, source, anchor)
+__global__ void prop_join_insert_kernel(const int64_t* __restrict__ batch_ids,
+                                        const int64_t* __restrict__ sources,
+                                        const int64_t* __restrict__ anchors, int64_t c_primary,
+                                        unsigned long long* __restrict__ hkeys,
+                                        int32_t* __restrict__ hvals, int64_t hmask,
+                                        int32_t* __restrict__ match_e, int32_t* __restrict__ status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= c_primary) return;
+  match_e[i] = -1;
+  if (sources[i] < 0) return;
+  uint64_t key;
+  if (!candidate_key(batch_ids[i], sources[i], anchors[i], &key)) {
+    set_status(status, GRS_ERR_SHAPE);
+    return;
+  }
+  int64_t slot = (int64_t)(mix64(key) & (uint64_t)hmask);
+  for (int64_t probe = 0; probe <= hmask; ++probe, slot = (slot + 1) & hmask) {
+    const unsigned long long prev = atomicCAS(&hkeys[slot], 0ull, (unsigned long long)key);
+    if (prev == 0ull) {
+      hvals[slot] = (int32_t)i;
+      return;
+    }
+    if (prev == (unsigned long long)key) return;   // the first row of a repeated key wins
+  }
+  set_status(status, GRS_ERR_WORKSPACE);
+}
+
+// exploration rows look up their primary partner (and tell it theirs)
+__global__ void prop_join_lookup_kernel(const int64_t* __restrict__ batch_ids,
+                                        const int64_t* __restrict__ sources,
+                                        const int64_t* __restrict__ anchors, int64_t c_primary,
+                                        int64_t c, const unsigned long long* __restrict__ hkeys,
+                                        const int32_t* __restrict__ hvals, int64_t hmask,
+                                        int32_t* __restrict__ match_p, int32_t* __restrict__ match_e) {
+  const int64_t i = c_primary + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= c) return;
+  match_p[i - c_primary] = -1;
+  uint64_t key;
+  if (sources[i] < 0 || !candidate_key(batch_ids[i], sources[i], anchors[i], &key)) return;
+  int64_t slot = (int64_t)(mix64(key) & (uint64_t)hmask);
+  for (int64_t probe = 0; probe <= hmask; ++probe, slot = (slot + 1) & hmask) {
+    const unsigned long long k = hkeys[slot];
+    if (k == 0ull) return;
+    if (k == (unsigned long long)key) {
+      const int32_t row = hvals[slot];
+      match_p[i - c_primary] = row;
+      match_e[row] = (int32_t)i;
+      return;
+    }
+  }
+}
+
+constexpr int EXPL_THREADS = 256;
+
+// one CTA per parent: the kept list (positions in spos) of the quota rule
+__global__ void __launch_bounds__(EXPL_THREADS) prop_select_exploration_kernel(
+    const int32_t* __restrict__ sorted_e, const int32_t* __restrict__ pos_of,
+    const int32_t* __restrict__ seg_begin, const int32_t* __restrict__ seg_end,
+    const int32_t* __restrict__ e_row, const int32_t* __restrict__ offsets, int64_t c_primary,
+    const int32_t* __restrict__ match_p, const int32_t* __restrict__ match_e, int cap, int quota,
+    uint8_t* __restrict__ keep, uint8_t* __restrict__ taken_e, int32_t* __restrict__ spos,
+    int64_t* __restrict__ metrics) {
+  typedef cub::BlockScan<int, EXPL_THREADS> Scan;
+  __shared__ typename Scan::TempStorage scan;
+  const int64_t p = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int ps = seg_begin[2 * p], pe = seg_end[2 * p];
+  const int es = seg_begin[2 * p + 1], ee = seg_end[2 * p + 1];
+  const int np = pe - ps, ne = ee - es;
+  const int limit = cap - min(quota, cap);          // primary actions kept first
+  const int n0 = min(limit, np);
+  for (int i = tid; i < n0; i += EXPL_THREADS) {
+    const int e = sorted_e[ps + i];
+    keep[e] = 1;
+    spos[e] = i;
+  }
+  // exploration actions: the reference appends, then checks the cap, so a
+  // full primary head still admits one
+  const int want = n0 >= cap ? 1 : cap - n0;
+  int taken = 0;
+  for (int base = 0; base < ne && taken < want; base += EXPL_THREADS) {
+    const int i = base + tid;
+    int ok = 0, e = -1;
+    if (i < ne) {
+      e = sorted_e[es + i];
+      const int row = e_row[e];
+      const int rp = match_p[row - c_primary];
+      bool dup = false;
+      if (rp >= 0) dup = pos_of[offsets[rp] + (e - offsets[row])] - ps < limit;
+      ok = dup ? 0 : 1;
+    }
+    int prefix, total;
+    Scan(scan).ExclusiveSum(ok, prefix, total);
+    if (ok && taken + prefix < want) {
+      keep[e] = 1;
+      taken_e[e] = 1;
+      spos[e] = n0 + taken + prefix;
+    }
+    taken += min(total, want - taken);
+    __syncthreads();
+  }
+  // the remaining primary actions that no kept exploration action repeats
+  const int kept = n0 + taken;
+  if (kept < cap) {
+    const int need = cap - kept;
+    int filled = 0;
+    for (int base = limit; base < np && filled < need; base += EXPL_THREADS) {
+      const int i = base + tid;
+      int ok = 0, e = -1;
+      if (i < np) {
+        e = sorted_e[ps + i];
+        const int row = e_row[e];
+        const int re = match_e[row];
+        bool dup = false;
+        if (re >= 0) dup = taken_e[offsets[re] + (e - offsets[row])] != 0;
+        ok = dup ? 0 : 1;
+      }
+      int prefix, total;
+      Scan(scan).ExclusiveSum(ok, prefix, total);
+      if (ok && filled + prefix < need) {
+        keep[e] = 1;
+        spos[e] = kept + filled + prefix;
+      }
+      filled += min(total, need - filled);
+      __syncthreads();
+    }
+  }
+  if (tid == 0 && taken)
+    atomicAdd(reinterpret_cast<unsigned long long*>(&metrics[4]), (unsigned long long)taken);
+}
+
+// keys of the final order: secondary (parent, xfer, kept position), primary
+// (next gate, probability desc, parent gate)
+__global__ void prop_exploration_keys_kernel(
+    const int32_t* __restrict__ kept_e, const int32_t* __restrict__ num_kept, int64_t m,
+    const int32_t* __restrict__ e_next, const int32_t* __restrict__ e_row,
+    const int32_t* __restrict__ e_xfer, const uint32_t* __restrict__ e_parent,
+    const int32_t* __restrict__ spos, const float* __restrict__ probs,
+    const int64_t* __restrict__ parent_gates, uint64_t* __restrict__ key2,
+    uint64_t* __restrict__ key1, int32_t* __restrict__ value, int32_t* __restrict__ status) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= m) return;
+  if (j < *num_kept) {
+    const int e = kept_e[j];
+    const uint32_t parent = e_parent[e];
+    const int64_t pg = parent_gates[parent];
+    if (pg < -32768 || pg > 32767 || parent >= (1u << 24) || spos[e] > 0xffff)
+      set_status(status, GRS_ERR_SHAPE);
+    key2[j] = ((uint64_t)parent << 32) | ((uint64_t)(e_xfer[e] & 0xffff) << 16) |
+              (uint64_t)(spos[e] & 0xffff);
+    key1[j] = ((uint64_t)(uint16_t)(e_next[e] + 32768) << 48) |
+              ((uint64_t)desc_float_key(probs[e_row[e]]) << 16) | (uint64_t)(uint16_t)(pg + 32768);
+    value[j] = (int32_t)j;
+  } else {
+    key2[j] = PAD_KEY;
+    key1[j] = PAD_KEY;
+    value[j] = -1;
+  }
+}
+
+// after the tie-order sort (order[i] = kept index): the ranking keys and
+// the action ids in that order
+__global__ void prop_gather_keys_kernel(const int32_t* __restrict__ order, int64_t n,
+                                        const int32_t* __restrict__ kept_e,
+                                        const int32_t* __restrict__ num_kept,
+                                        const uint64_t* __restrict__ key1,
+                                        uint64_t* __restrict__ key_out,
+                                        int32_t* __restrict__ e_out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int j = order[i];
+  if (j >= 0 && j < *num_kept) {
+    key_out[i] = key1[j];
+    e_out[i] = kept_e[j];
+  } else {
+    key_out[i] = PAD_KEY;
+    e_out[i] = -1;
+  }
+}
+
+struct ExplWorkspace {
+  int32_t *counts, *offsets, *total, *num_kept;
+  int32_t *e_row, *e_xfer, *e_next, *pos_of, *spos, *kept;
+  uint32_t *e_parent, *pkey_in, *pkey_out;
+  uint64_t *key_in, *key_out, *key2_in, *key2_out;
+  int32_t *val_in, *val_out;
+  int32_t *seg_begin, *seg_end, *match_p, *match_e, *hvals;
+  unsigned long long* hkeys;
+  uint8_t *keep, *taken_e;
+  int64_t hmask;
+  void* cub_tmp;
+  size_t cub_bytes;
+};
+
+static size_t expl_layout(char* base, int64_t c, int64_t c_primary, int64_t n, int64_t parents,
+                          ExplWorkspace* w) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> char* {
+    char* p = base ? base + off : nullptr;
+    off += align_up(bytes);
+    return p;
+  };
+  const int64_t cc = c > 0 ? c : 1, nn = n > 0 ? n : 1, pp = parents > 0 ? parents : 1;
+  int64_t h = 2;
+  while (h < 2 * (c_primary > 0 ? c_primary : 1)) h <<= 1;
+  w->hmask = h - 1;
+  w->counts = (int32_t*)take(cc * 4);
+  w->offsets = (int32_t*)take(cc * 4);
+  w->total = (int32_t*)take(4);
+  w->num_kept = (int32_t*)take(4);
+  w->e_row = (int32_t*)take(nn * 4);
+  w->e_xfer = (int32_t*)take(nn * 4);
+  w->e_next = (int32_t*)take(nn * 4);
+  w->pos_of = (int32_t*)take(nn * 4);
+  w->spos = (int32_t*)take(nn * 4);
+  w->kept = (int32_t*)take(nn * 4);
+  w->e_parent = (uint32_t*)take(nn * 4);
+  w->pkey_in = (uint32_t*)take(nn * 4);
+  w->pkey_out = (uint32_t*)take(nn * 4);
+  w->key_in = (uint64_t*)take(nn * 8);
+  w->key_out = (uint64_t*)take(nn * 8);
+  w->key2_in = (uint64_t*)take(nn * 8);
+  w->key2_out = (uint64_t*)take(nn * 8);
+  w->val_in = (int32_t*)take(nn * 4);
+  w->val_out = (int32_t*)take(nn * 4);
+  w->seg_begin = (int32_t*)take(2 * pp * 4);
+  w->seg_end = (int32_t*)take(2 * pp * 4);
+  w->match_p = (int32_t*)take(cc * 4);
+  w->match_e = (int32_t*)take(cc * 4);
+  w->hvals = (int32_t*)take(h * 4);
+  w->hkeys = (unsigned long long*)take(h * 8);
+  w->keep = (uint8_t*)take(nn);
+  w->taken_e = (uint8_t*)take(nn);
+  size_t need = 0, t = 0;
+  cub::DeviceScan::ExclusiveSum(nullptr, t, (int32_t*)nullptr, (int32_t*)nullptr, (int)cc);
+  need = t > need ? t : need;
+  cub::DeviceRadixSort::SortPairs(nullptr, t, (uint64_t*)nullptr, (uint64_t*)nullptr,
+                                  (int32_t*)nullptr, (int32_t*)nullptr, (int)nn);
+  need = t > need ? t : need;
+  cub::DeviceRadixSort::SortPairs(nullptr, t, (uint32_t*)nullptr, (uint32_t*)nullptr,
+                                  (int32_t*)nullptr, (int32_t*)nullptr, (int)nn);
+  need = t > need ? t : need;
+  cub::DeviceSelect::Flagged(nullptr, t, thrust::counting_iterator<int32_t>(0),
+                             (uint8_t*)nullptr, (int32_t*)nullptr, (int32_t*)nullptr, (int)nn);
+  need = t > need ? t : need;
+  w->cub_bytes = need;
+  w->cub_tmp = take(need);
+  return off;
+}
+
+}  // namespace grs
+
+extern "C" int64_t grs_proposals_exploration_workspace_bytes(int64_t num_candidates,
+                                                             int64_t num_primary,
+                                                             int64_t max_expanded,
+                                                             int64_t num_parents) {
+  ExplWorkspace w;
+  return (int64_t)expl_layout(nullptr, num_candidates, num_primary, max_expanded, num_parents, &w);
+}
+
+extern "C" int grs_proposals_rank_exploration(
+    const int64_t* batch_ids, const int64_t* sources, const int64_t* anchors,
+    const float* probabilities, int64_t num_candidates, int64_t num_primary,
+    const int64_t* parent_gate_counts, int64_t num_parents, const int32_t* xfer_offsets,
+    const int32_t* xfer_counts, const int32_t* xfer_ids, const int32_t* gate_deltas,
+    const int32_t* all_xfer_counts, int num_sources, int64_t max_expanded, int per_parent_cap,
+    int exploration_per_parent, int64_t global_cap, int64_t* out_row, int64_t* out_xfer,
+    int64_t* out_next_gate, int64_t* out_count, int64_t* out_metrics, void* workspace,
+    int64_t workspace_bytes, int32_t* status, void* stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t c = num_candidates, n = max_expanded, cp = num_primary;
+  if (c < 0 || cp < 0 || cp > c || n < 0 || num_parents < 0 || per_parent_cap < 0 ||
+      per_parent_cap > 0xfffe || exploration_per_parent < 0 || global_cap < 0 ||
+      c > (1ll << 30) || n > (1ll << 30) || num_parents >= (1ll << 23))
+    return GRS_ERR_SHAPE;
+  ExplWorkspace w;
+  const int64_t need = (int64_t)expl_layout((char*)workspace, c, cp, n, num_parents, &w);
+  if (need > workspace_bytes) return GRS_ERR_WORKSPACE;
+  cudaMemsetAsync(out_metrics, 0, 5 * sizeof(int64_t), s);
+  if (c == 0 || n == 0 || num_parents == 0) {
+    cudaMemsetAsync(out_count, 0, sizeof(int64_t), s);
+    GRS_CUDA_CHECK_LAUNCH();
+    return GRS_OK;
+  }
+  const int T = 256;
+  prop_count_models_kernel<<<ceil_div(c, T), T, 0, counted(s)>>>(
+      sources, c, cp, xfer_counts, all_xfer_counts, num_sources, w.counts, out_metrics, status);
+  size_t tb = w.cub_bytes;
+  cub::DeviceScan::ExclusiveSum(w.cub_tmp, tb, w.counts, w.offsets, (int)c, s);
+  prop_total_kernel<<<1, 1, 0, counted(s)>>>(w.counts, w.offsets, c, w.total);
+  prop_expand_kernel<<<ceil_div(c, T), T, 0, counted(s)>>>(
+      batch_ids, sources, probabilities, c, w.counts, w.offsets, xfer_offsets, xfer_ids,
+      gate_deltas, parent_gate_counts, num_parents, w.e_row, w.e_xfer, w.e_next, w.e_parent,
+      w.key_in, w.val_in, n, status);
+  prop_pad_kernel<<<ceil_div(n, T), T, 0, counted(s)>>>(w.total, n, w.key_in, w.val_in);
+  // (next gate, probability desc, xfer), then stably by (parent, model)
+  tb = w.cub_bytes;
+  cub::DeviceRadixSort::SortPairs(w.cub_tmp, tb, w.key_in, w.key_out, w.val_in, w.val_out,
+                                  (int)n, 0, 64, s);
+  prop_model_key_kernel<<<ceil_div(n, T), T, 0, counted(s)>>>(w.val_out, n, w.total, w.e_parent,
+                                                             w.e_row, cp, w.pkey_in);
+  tb = w.cub_bytes;
+  cub::DeviceRadixSort::SortPairs(w.cub_tmp, tb, w.pkey_in, w.pkey_out, w.val_out, w.val_in,
+                                  (int)n, 0, 32, s);
+  cudaMemsetAsync(w.seg_begin, 0, 2 * num_parents * sizeof(int32_t), s);
+  cudaMemsetAsync(w.seg_end, 0, 2 * num_parents * sizeof(int32_t), s);
+  prop_positions_kernel<<<ceil_div(n, T), T, 0, counted(s)>>>(w.pkey_out, w.val_in, n, w.pos_of,
+                                                             w.seg_begin, w.seg_end);
+  // pair the two models' candidates on (parent, source, anchor)
+  cudaMemsetAsync(w.hkeys, 0, (w.hmask + 1) * sizeof(unsigned long long), s);
+  if (cp > 0)
+    prop_join_insert_kernel<<<ceil_div(cp, T), T, 0, counted(s)>>>(
+        batch_ids, sources, anchors, cp, w.hkeys, w.hvals, w.hmask, w.match_e, status);
+  if (c > cp)
+    prop_join_lookup_kernel<<<ceil_div(c - cp, T), T, 0, counted(s)>>>(
+        batch_ids, sources, anchors, cp, c, w.hkeys, w.hvals, w.hmask, w.match_p, w.match_e);
+  cudaMemsetAsync(w.keep, 0, n, s);
+  cudaMemsetAsync(w.taken_e, 0, n, s);
+  prop_select_exploration_kernel<<<(unsigned)num_parents, EXPL_THREADS, 0, counted(s)>>>(
+      w.val_in, w.pos_of, w.seg_begin, w.seg_end, w.e_row, w.offsets, cp, w.match_p, w.match_e,
+      per_parent_cap, exploration_per_parent, w.keep, w.taken_e, w.spos, out_metrics);
+  tb = w.cub_bytes;
+  cub::DeviceSelect::Flagged(w.cub_tmp, tb, thrust::counting_iterator<int32_t>(0), w.keep,
+                             w.kept, w.num_kept, (int)n, s);
+  prop_exploration_keys_kernel<<<ceil_div(n, T), T, 0, counted(s)>>>(
+      w.kept, w.num_kept, n, w.e_next, w.e_row, w.e_xfer, w.e_parent, w.spos, probabilities,
+      parent_gate_counts, w.key2_in, w.key_in, w.val_in, status);
+  // LSD: the tie order first, then the ranking key (both sorts stable)
+  tb = w.cub_bytes;
+  cub::DeviceRadixSort::SortPairs(w.cub_tmp, tb, w.key2_in, w.key2_out, w.val_in, w.val_out,
+                                  (int)n, 0, 64, s);
+  prop_gather_keys_kernel<<<ceil_div(n, T), T, 0, counted(s)>>>(w.val_out, n, w.kept, w.num_kept,
+                                                               w.key_in, w.key_out, w.val_in);
+  tb = w.cub_bytes;
+  cub::DeviceRadixSort::SortPairs(w.cub_tmp, tb, w.key_out, w.key_in, w.val_in, w.val_out,
+                                  (int)n, 0, 64, s);
+  if (global_cap > 0)
+    prop_output_kernel<<<ceil_div(global_cap, T), T, 0, counted(s)>>>(
+        w.val_out, w.num_kept, global_cap, w.e_row, w.e_xfer, w.e_next, out_row, out_xfer,
+        out_next_gate, out_count);
+  else
+    cudaMemsetAsync(out_count, 0, sizeof(int64_t), s);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }

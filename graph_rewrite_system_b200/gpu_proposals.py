@@ -196,3 +196,52 @@ def rank_proposals_grouped(sources: torch.Tensor, probabilities: torch.Tensor, k
         metrics.data_ptr(), ws.data_ptr(), ws.numel(), status.data_ptr(),
         torch.cuda.current_stream(device).cuda_stream), "rank_proposals_grouped")
     return RankedProposals(rows, xfers, nexts, count, metrics, status)
+
+
+def rank_proposals_exploration(primary: dict, exploration: dict,
+                               parent_gate_counts: torch.Tensor, rule_index: GpuRuleIndex, *,
+                               per_parent_cap: int, exploration_per_parent: int,
+                               global_cap: int, status: torch.Tensor | None = None):
+    """Proposals from a primary and an exploration model's candidates with a
+    per-parent exploration quota (build_legacy_proposals,
+    paged_rollout_benchmark.py:101-210), on the device.  `primary` and
+    `exploration` are candidate dicts (batch_ids, sources, anchors,
+    probabilities; source -1 marks an absent row).  Returns
+    (RankedProposals whose rows index the concatenated candidate table
+    [primary rows | exploration rows], metrics int64 [5]: primary predicted,
+    primary eligible, exploration predicted, exploration eligible, selected
+    exploration proposals)."""
+    device = primary["sources"].device
+    cat = lambda k, dt: torch.cat((primary[k], exploration[k])).to(dt).contiguous()
+    batch_ids, sources = cat("batch_ids", torch.int64), cat("sources", torch.int64)
+    anchors, probs = cat("anchors", torch.int64), cat("probabilities", torch.float32)
+    _lib.require_cuda(batch_ids, parent_gate_counts)
+    c, cp = sources.numel(), primary["sources"].numel()
+    parents = parent_gate_counts.numel()
+    expanded_bound = c * max(1, rule_index.max_xfers_per_source)
+    need = int(_lib.lib().grs_proposals_exploration_workspace_bytes(c, cp, expanded_bound,
+                                                                    parents))
+    key = (str(device), "exploration")
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 1), device=device, dtype=torch.uint8)
+        _WORKSPACES[key] = ws
+    i64 = dict(device=device, dtype=torch.int64)
+    rows = torch.empty(max(global_cap, 0), **i64)
+    xfers = torch.empty_like(rows)
+    nexts = torch.empty_like(rows)
+    count = torch.empty(1, **i64)
+    metrics = torch.empty(5, **i64)
+    if status is None:
+        status = torch.zeros(1, device=device, dtype=torch.int32)
+    _lib.check(_lib.lib().grs_proposals_rank_exploration(
+        batch_ids.data_ptr(), sources.data_ptr(), anchors.data_ptr(), probs.data_ptr(), c, cp,
+        parent_gate_counts.to(torch.int64).contiguous().data_ptr(), parents,
+        rule_index.xfer_offsets.data_ptr(), rule_index.xfer_counts.data_ptr(),
+        rule_index.xfer_ids.data_ptr(), rule_index.gate_deltas.data_ptr(),
+        rule_index.all_xfer_counts.data_ptr(), rule_index.xfer_counts.numel(), expanded_bound,
+        per_parent_cap, exploration_per_parent, global_cap, rows.data_ptr(), xfers.data_ptr(),
+        nexts.data_ptr(), count.data_ptr(), metrics.data_ptr(), ws.data_ptr(), ws.numel(),
+        status.data_ptr(), _lib.current_stream()), "rank_proposals_exploration")
+    ranked = RankedProposals(rows, xfers, nexts, count, metrics[:2], status)
+    return ranked, metrics

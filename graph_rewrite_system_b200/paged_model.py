@@ -582,7 +582,9 @@ class PagedActionBindingModel(nn.Module):
 
     # ---- the per-beam token path of one step (CUDA graph per shape) ------------
     USE_GRAPHS = True
-    GRAPH_CACHE_LIMIT = 16   # captured token-step graphs kept (least recently used dropped)
+    # captured token-step graphs kept (least recently used dropped): a 64-level
+    # search meets at most ~64 (beams, block-table width) shapes
+    GRAPH_CACHE_LIMIT = 64
 
     def _token_step_eager(self, ctx_in, active, past_lengths, block_table, key_cache,
                           value_cache):

@@ -32,7 +32,8 @@ import torch
 from . import _lib
 from . import kernels as K
 from .gpu_proposals import (GROUPED_MAX_EXPANSION, GpuRuleIndex, RankedProposals,
-                            rank_proposals_device, rank_proposals_grouped)
+                            rank_proposals_device, rank_proposals_exploration,
+                            rank_proposals_grouped)
 from .paged_cache import PagedKVCache
 from .paged_model import PagedActionBindingModel
 from .synthetic import (Circuit, RolloutConfig, RuleMetadata, SELECT_ALL_THRESHOLDS)
@@ -66,6 +67,9 @@ class StepRow:
     allocated_cache_pages: int
     logical_cache_pages: int
     page_sharing_ratio: float
+    exploration_predicted_actions: int = 0
+    exploration_eligible_actions: int = 0
+    selected_exploration_proposals: int = 0
 
 
 @dataclass
@@ -77,6 +81,7 @@ class Proposed:
     valid: torch.Tensor          # uint8 [global_cap] structurally valid
     fp: torch.Tensor             # int64 [global_cap] child fingerprint
     k: int                       # candidate rows per parent
+    exploration_metrics: torch.Tensor | None = None   # int64 [3] while a second model runs
 
 
 class StageTimer:
@@ -108,10 +113,35 @@ class DeviceBeamSearch:
     """Beam search over rewrite sequences with the state resident in HBM."""
 
     def __init__(self, model: PagedActionBindingModel, rules: RuleMetadata, circuit: Circuit,
-                 config: RolloutConfig, device, thresholds: dict = SELECT_ALL_THRESHOLDS):
+                 config: RolloutConfig, device, thresholds: dict = SELECT_ALL_THRESHOLDS, *,
+                 exploration_model: PagedActionBindingModel | None = None,
+                 exploration_thresholds: dict | None = None, exploration_per_parent: int = 0,
+                 exploration_until_depth: int = 0):
+        """`exploration_model`: a second paged model searched alongside (the
+        reference's --exploration-checkpoint, paged_rollout_benchmark.py
+        :724-758): it reads the same beams from its own paged cache, its
+        candidates fill up to `exploration_per_parent` of every parent's
+        proposals (build_legacy_proposals, :101-210), it advances with every
+        accepted child, and it is dropped from level `exploration_until_depth`
+        on (0: never, :900-911)."""
         self.model, self.rules, self.circuit, self.cfg = model, rules, circuit, config
         self.device = torch.device(device)
         self.thresholds = thresholds
+        if exploration_per_parent < 0 or exploration_until_depth < 0:
+            raise ValueError("the exploration quota and depth must be nonnegative")
+        if exploration_per_parent and exploration_model is None:
+            raise ValueError("an exploration checkpoint is required for an exploration quota")
+        if exploration_per_parent > config.per_parent_cap:
+            raise ValueError("the exploration quota cannot exceed the per-parent cap")
+        if exploration_model is not None and (
+                exploration_model.width != model.width
+                or exploration_model.action_layers_count != model.action_layers_count
+                or exploration_model.action_heads != model.action_heads):
+            raise ValueError("primary and exploration paged-cache shapes differ")
+        self.exploration_model = exploration_model
+        self.exploration_thresholds = exploration_thresholds or thresholds
+        self.exploration_per_parent = exploration_per_parent
+        self.exploration_until_depth = exploration_until_depth
         dev = self.device
         self.s0_slots = max(s for s, _ in circuit.nodes) + 1
         self.max_dst = max(len(d) for d in rules.destination_gate_types)
@@ -135,6 +165,14 @@ class DeviceBeamSearch:
         self.status = torch.zeros(1, device=dev, dtype=torch.int32)
         # the model's tensor-core kernels report into the level's status word
         model.kernel_status = self.status
+        self.exploration_cache = None
+        if exploration_model is not None:
+            exploration_model.kernel_status = self.status
+            self.exploration_cache = PagedKVCache(
+                layers=model.action_layers_count, capacity=config.cache_pages,
+                page_size=config.page_size, heads=model.action_heads, head_width=hd,
+                model_width=model.width, device=dev, dtype=exploration_model.compute_dtype)
+        self.exploring = False
         self.summary = torch.zeros(6, device=dev, dtype=torch.int64)
         self.rows: list[StepRow] = []
         self.timer: StageTimer | None = None
@@ -190,6 +228,13 @@ class DeviceBeamSearch:
                  "edge_src": e[:, 0].to(dev), "edge_dst": e[:, 1].to(dev),
                  "edge_relation": (e[:, 2] * 4 + e[:, 3]).to(dev)}
         self.states, self.live, self.types = model.initialize_incremental(batch)
+        self.exploring = self.exploration_model is not None
+        if self.exploring:
+            self.x_states, self.x_live, self.x_types = \
+                self.exploration_model.initialize_incremental(batch)
+            self.exploration_cache.reset()
+            self.x_block_table = torch.zeros(1, 1, device=dev, dtype=torch.int32)
+            self.x_lengths = torch.zeros(1, device=dev, dtype=torch.int32)
         self.topo = initial_topology(self.topology[0], nodes, edges, s)
         self.cache.reset()
         self.current = 0
@@ -208,9 +253,17 @@ class DeviceBeamSearch:
         with K.pinned_stream():
             return self._step()
 
+    def _drop_exploration(self) -> None:
+        """The second model leaves the search (paged_rollout_benchmark.py:900-911)."""
+        self.exploration_cache.release_device(self.x_block_table, self.x_lengths)
+        self.x_states = self.x_live = self.x_types = None
+        self.exploring = False
+
     def _step(self) -> StepRow | None:
         cfg, dev = self.cfg, self.device
         b, s, depth = self.beams, self.slots, self.depth
+        if self.exploring and self.exploration_until_depth and depth >= self.exploration_until_depth:
+            self._drop_exploration()
         prop = self._propose()
         # 4. accept (first occurrence of unseen valid fingerprints, in rank order)
         gcap = cfg.global_cap
@@ -228,18 +281,24 @@ class DeviceBeamSearch:
             "topology_accept")
         # one synchronisation per level
         self._mark("host_sync")
-        host = torch.cat((self.summary, prop.ranked.count, prop.ranked.metrics,
-                          self.cache.allocated_pages_tensor().long(), self.status.long(),
-                          self.cache.status_tensor().long())).cpu()
+        parts = [self.summary, prop.ranked.count, prop.ranked.metrics,
+                 self.cache.allocated_pages_tensor().long(), self.status.long(),
+                 self.cache.status_tensor().long()]
+        if prop.exploration_metrics is not None:
+            parts += [prop.exploration_metrics, self.exploration_cache.status_tensor().long()]
+        host = torch.cat(parts).cpu().tolist()
         (accepted, attempted, invalid, dup, extent, best, proposals, predicted, eligible_n,
-         allocated, status, cache_status) = host.tolist()
+         allocated, status, cache_status) = host[:12]
+        x_metrics = host[12:15] if prop.exploration_metrics is not None else [0, 0, 0]
+        if prop.exploration_metrics is not None and host[15]:
+            self.exploration_cache.check_status()
         if status:
             self.status.zero_()
             _lib.check(int(status), "beam search step")
         if cache_status:
             self.cache.check_status()
         row = StepRow(depth + 1, b, accepted, best, predicted, eligible_n, proposals, attempted,
-                      accepted, invalid, dup, allocated, 0, 0.0)
+                      accepted, invalid, dup, allocated, 0, 0.0, *x_metrics)
         if not accepted:
             self.rows.append(row)
             return None
@@ -275,11 +334,33 @@ class DeviceBeamSearch:
         self._check_range("candidates", "source", cand["sources"], 0, self.rules.num_sources,
                           allow_negative_one=True)
         self._check_range("candidates", "binding", cand["bindings"], 0, s, allow_negative_one=True)
+        cand_x = None
+        if self.exploring:   # the second model's candidates on the same beams
+            xm = self.exploration_model
+            x_readout, _, _ = xm.readout_incremental(
+                self.x_states, self.x_live, self.x_types,
+                readout_key_cache=self.exploration_cache.readout_keys,
+                readout_value_cache=self.exploration_cache.readout_values,
+                block_table=self.x_block_table, lengths=self.x_lengths, ports=ports)
+            x_logits, x_eligible = xm.match_logits(x_readout, self.x_live, self.x_types)
+            cand_x = select_candidates_device(xm, self.x_types, self.x_live, ports, topo.distance,
+                                              x_logits, x_eligible, self.exploration_thresholds,
+                                              cfg.max_candidates_per_state)
         # 3. proposals (effective parent cap of paged_rollout_benchmark.py:963-966)
         cap = self.parent_cap()
         self._mark("proposals")
         k = cand["sources"].numel() // b
-        if cap <= GROUPED_MAX_EXPANSION:
+        x_metrics = None
+        if cand_x is not None:
+            # build_legacy_proposals with the exploration quota; the ranked
+            # rows index the primary then the exploration candidate rows
+            ranked, m5 = rank_proposals_exploration(
+                cand, cand_x, topo.gate, self.rule_index, per_parent_cap=cap,
+                exploration_per_parent=self.exploration_per_parent, global_cap=cfg.global_cap,
+                status=self.status)
+            x_metrics = m5[2:]
+            cand = {key: torch.cat((cand[key], cand_x[key])) for key in cand}
+        elif cap <= GROUPED_MAX_EXPANSION:
             ranked = rank_proposals_grouped(cand["sources"], cand["probabilities"], k, topo.gate,
                                             self.rule_index, per_parent_cap=cap,
                                             global_cap=cfg.global_cap, status=self.status)
@@ -307,7 +388,7 @@ class DeviceBeamSearch:
             topo.out_port.data_ptr(), topo.in_node.data_ptr(), topo.in_port.data_ptr(), s,
             topo.next_slot.data_ptr(), topo.fingerprint.data_ptr(), valid.data_ptr(), fp.data_ptr(),
             self.status.data_ptr(), K.stream()), "topology_plan")
-        return Proposed(ranked, cand, valid, fp, k)
+        return Proposed(ranked, cand, valid, fp, k, x_metrics)
 
     def global_beams(self) -> int:
         """Beams of the whole search at this level (this GPU's beams here)."""
@@ -366,11 +447,40 @@ class DeviceBeamSearch:
             table_par, lengths_par, new_k, new_v, action, rk, rv, child_cols=child_cols)
         self._check_tables("append", child_table, child_lengths)
         self.cache.release_device(self.block_table, self.lengths)
+        if self.exploring:   # the second model advances with the same children
+            self._advance_exploration(a_parent, a_xfer, a_source, a_src, a_dst, a_dst_types,
+                                      accepted, s_new, child_cols)
         self.states, self.live, self.types = states, live, types
         self.block_table, self.lengths = child_table, child_lengths
         self.topo, self.current = nxt, 1 - self.current
         self.last_actions = (a_parent, a_xfer, a_src, a_dst)
         self.beams, self.slots, self.depth = accepted, s_new, depth + 1
+
+    def _advance_exploration(self, a_parent, a_xfer, a_source, a_src, a_dst, a_dst_types,
+                             n: int, s_new: int, child_cols: int) -> None:
+        """advance_selected for the exploration model (paged_rollout_benchmark.py:1071-1091):
+        its parents' rows, one-token step, append to its cache, release its parents."""
+        xm, dev, w = self.exploration_model, self.device, self.model.width
+        states_par = torch.empty(n, s_new, w, device=dev, dtype=xm.compute_dtype)
+        K.gather_beams(self.x_states, a_parent, states_par)
+        live_par = torch.empty(n, s_new, device=dev, dtype=torch.bool)
+        K.gather_beams(self.x_live, a_parent, live_par)
+        types_par = torch.empty(n, s_new, device=dev, dtype=torch.int64)
+        K.gather_beams(self.x_types, a_parent, types_par, fill_byte=0xFF)
+        table_par = torch.empty(n, self.x_block_table.shape[1], device=dev, dtype=torch.int32)
+        K.gather_beams(self.x_block_table, a_parent, table_par)
+        lengths_par = torch.empty(n, device=dev, dtype=torch.int32)
+        K.gather_beams(self.x_lengths, a_parent, lengths_par)
+        cache = self.exploration_cache
+        states, live, types, new_k, new_v, action, rk, rv = xm.advance_device(
+            states_par, live_par, types_par, a_xfer, a_source, a_src, a_dst, a_dst_types,
+            cache.keys, cache.values, table_par, lengths_par, return_readout_kv=True,
+            graphed=True)
+        child_table, child_lengths = cache.append_device(
+            table_par, lengths_par, new_k, new_v, action, rk, rv, child_cols=child_cols)
+        cache.release_device(self.x_block_table, self.x_lengths)
+        self.x_states, self.x_live, self.x_types = states, live, types
+        self.x_block_table, self.x_lengths = child_table, child_lengths
 
     def _materialize(self, n: int, child_proposal, summary, rows, xfers, next_gate, fp,
                      cand_batch, cand_anchor, cand_bindings, parent, slots: int, nxt,

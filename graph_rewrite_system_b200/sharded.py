@@ -65,6 +65,9 @@ class ShardedBeamSearch(DeviceBeamSearch):
     Requires an initialised default process group."""
 
     def __init__(self, *args, group=None, **kwargs):
+        if kwargs.get("exploration_model") is not None:
+            raise NotImplementedError("the sharded search runs one model; the exploration "
+                                      "model runs on the single-GPU search")
         super().__init__(*args, **kwargs)
         self.group = group
         self.world = dist.get_world_size(group)

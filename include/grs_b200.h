@@ -205,6 +205,37 @@ GRS_API int grs_proposals_rank_grouped(const int64_t* sources, const float* prob
                                        int64_t* out_count, int64_t* out_metrics, void* workspace,
                                        int64_t workspace_bytes, int32_t* status, void* stream);
 
+/* Proposals from two models' candidates with a per-parent exploration quota
+ * (build_legacy_proposals, paged_rollout_benchmark.py:101-210; used while
+ * the search runs a second, exploration model, :917-919, 937-961).  The
+ * candidate table holds the primary model's rows [0, num_primary) then the
+ * exploration model's (source < 0: absent row).  Per parent, each model's
+ * allowed actions are ranked (next gate, probability desc, xfer, expansion
+ * order); the parent keeps the first cap - quota primary actions, then
+ * exploration actions whose (xfer, anchor, binding) is not yet kept
+ * (appending before checking the cap, as the reference), then the other
+ * primary actions that no kept one repeats, up to the cap; all kept actions
+ * are ranked (next gate, probability desc, parent gate) with ties in the
+ * parent's list order (next gate, probability desc, xfer, kept position),
+ * first global_cap.  Outputs as grs_proposals_rank (rows index the
+ * concatenated table); out_metrics int64 [5] = primary predicted, primary
+ * eligible, exploration predicted, exploration eligible, selected
+ * exploration proposals.  Workspace from
+ * grs_proposals_exploration_workspace_bytes. */
+GRS_API int64_t grs_proposals_exploration_workspace_bytes(int64_t num_candidates,
+                                                          int64_t num_primary,
+                                                          int64_t max_expanded,
+                                                          int64_t num_parents);
+GRS_API int grs_proposals_rank_exploration(
+    const int64_t* batch_ids, const int64_t* sources, const int64_t* anchors,
+    const float* probabilities, int64_t num_candidates, int64_t num_primary,
+    const int64_t* parent_gate_counts, int64_t num_parents, const int32_t* xfer_offsets,
+    const int32_t* xfer_counts, const int32_t* xfer_ids, const int32_t* gate_deltas,
+    const int32_t* all_xfer_counts, int num_sources, int64_t max_expanded, int per_parent_cap,
+    int exploration_per_parent, int64_t global_cap, int64_t* out_row, int64_t* out_xfer,
+    int64_t* out_next_gate, int64_t* out_count, int64_t* out_metrics, void* workspace,
+    int64_t workspace_bytes, int32_t* status, void* stream);
+
 /* Allocation-free variant of grs_proposals_rank (no counterpart in the
  * reference).  For callers that cannot allocate device memory when they rank
  * proposals (a runtime whose device memory is all pre-reserved by its own

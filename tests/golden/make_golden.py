@@ -306,6 +306,9 @@ def main() -> None:
         np.savez_compressed(HERE / "model_cpu_equivalence.npz", **model_case(args.reference))
     if not only or "topology" in only:
         np.savez_compressed(HERE / "topology_accept.npz", **topology_case())
+    if not only or "exploration" in only:
+        np.savez_compressed(HERE / "proposals_exploration.npz",
+                            **exploration_cases(ref_prb, ref_bsb))
     if not only or "checkpoint" in only:
         np.savez_compressed(HERE / "checkpoint_tiny.npz", **checkpoint_case(args.reference))
     print("golden fixtures written to", HERE)
@@ -460,6 +463,74 @@ def model_case(reference: Path, *, seed=1, beams=16, actions=8, dag_nodes=64):
         out["decode_bindings"], out["decode_valid"] = bindings.numpy(), valid.numpy()
     out["seed"] = np.int64(seed)
     return out
+
+
+def exploration_cases(ref_prb, ref_bsb):
+    """build_legacy_proposals (paged_rollout_benchmark.py:101-210) with a
+    second model's candidates and an exploration quota, on seeded candidate
+    lists: the exploration model re-predicts about half of the primary
+    (source, anchor, binding) candidates with its own probabilities and adds
+    its own.  Cases: a regular quota, no quota (the cap is checked after an
+    append), a quota equal to the cap, and one wide parent (a search's first
+    level, where the effective cap is 2 x beam)."""
+    import json
+    import random
+
+    from graph_rewrite_system_b200 import synthetic
+
+    rules = synthetic.synthetic_rules()
+    s2x, deltas = rules.source_to_xfers(), rules.gate_deltas()
+    out = {}
+    for name, (seed, parents, per_state, beam_size, cap, quota) in {
+            "regular": (11, 6, 12, 6, 8, 3), "no_quota": (12, 5, 10, 5, 6, 0),
+            "full_quota": (13, 4, 9, 4, 5, 5), "wide": (14, 1, 300, 120, 16, 6)}.items():
+        rng = random.Random(seed)
+        f32 = lambda: float(np.float32(rng.random()))
+        beam = [ref_bsb.BeamState(graph=None, snapshot=None, guid_to_slot={}, next_slot=0,
+                                  last_touched={}, rewrite_distance={}, previous_preferred=set(),
+                                  local_streak=0, gate_count=rng.randrange(90, 96), depth=0,
+                                  history=()) for _ in range(parents)]
+        predicted, explored = [], []
+        for _ in range(parents):
+            rows, seen = [], set()
+            while len(rows) < per_state:
+                source = rng.randrange(rules.num_sources)
+                anchor = rng.randrange(60)
+                if (source, anchor) in seen:
+                    continue
+                seen.add((source, anchor))
+                width = len(rules.source_gate_types[source])
+                binding = tuple([anchor] + [rng.randrange(60) for _ in range(width - 1)])
+                rows.append((source, anchor, binding, f32()))
+            extra = []
+            for source, anchor, binding, _ in rows:
+                if rng.random() < 0.5:
+                    extra.append((source, anchor, binding, f32()))
+            while len(extra) < per_state:
+                source, anchor = rng.randrange(rules.num_sources), 60 + rng.randrange(40)
+                if (source, anchor) in seen:
+                    continue
+                seen.add((source, anchor))
+                width = len(rules.source_gate_types[source])
+                extra.append((source, anchor,
+                              tuple([anchor] + [rng.randrange(60) for _ in range(width - 1)]), f32()))
+            rng.shuffle(extra)
+            predicted.append(rows)
+            explored.append(extra)
+        proposals, metrics = ref_prb.build_legacy_proposals(
+            beam, predicted, explored, s2x, deltas, beam_size=beam_size,
+            max_actions_per_parent=cap, exploration_actions_per_parent=quota,
+            proposal_factor=4, max_gate_increase=1)
+        out[name] = {
+            "gate_counts": [b.gate_count for b in beam],
+            "predicted": [[list(r[:2]) + [list(r[2]), r[3]] for r in rows] for rows in predicted],
+            "exploration_predicted": [[list(r[:2]) + [list(r[2]), r[3]] for r in rows]
+                                      for rows in explored],
+            "beam_size": beam_size, "cap": cap, "quota": quota, "proposal_factor": 4,
+            "proposals": [[q.parent, q.xfer_id, q.anchor_slot, list(q.binding), q.probability,
+                           q.next_gate_count] for q in proposals],
+            "metrics": {k: v for k, v in metrics.items() if not k.endswith("_seconds")}}
+    return {"json": np.array(json.dumps(out))}
 
 
 def checkpoint_case(reference: Path, *, seed=4, beams=3, actions=4):

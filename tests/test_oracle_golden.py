@@ -124,3 +124,56 @@ def test_oracle_proposals():
         np.testing.assert_allclose(sel["probability"], g["out_probability"], rtol=0, atol=1e-7)
         assert metrics == {"predicted_actions": int(g["predicted"]),
                            "eligible_actions": int(g["eligible"])}
+
+
+def exploration_golden():
+    import json
+
+    return json.loads(str(load_golden("proposals_exploration.npz")["json"]))
+
+
+def exploration_inputs(case, max_pattern):
+    """The golden case's per-state candidate lists as padded candidate tables."""
+    import math
+
+    def table(per_state):
+        batch, sources, anchors, bindings, probs = [], [], [], [], []
+        for parent, rows in enumerate(per_state):
+            for source, anchor, binding, prob in rows:
+                batch.append(parent)
+                sources.append(source)
+                anchors.append(anchor)
+                bindings.append(list(binding) + [-1] * (max_pattern - len(binding)))
+                probs.append(prob)
+        return {"batch_ids": np.asarray(batch, np.int64), "sources": np.asarray(sources, np.int64),
+                "anchors": np.asarray(anchors, np.int64),
+                "bindings": np.asarray(bindings, np.int64).reshape(-1, max_pattern),
+                "probabilities": np.asarray(probs, np.float32)}
+
+    parents = len(case["gate_counts"])
+    cap = max(case["cap"], math.ceil(case["beam_size"] / max(1, parents)) * 2)
+    return (table(case["predicted"]), table(case["exploration_predicted"]),
+            np.asarray(case["gate_counts"], np.int64), cap,
+            case["beam_size"] * case["proposal_factor"])
+
+
+def test_oracle_exploration_quota_matches_reference():
+    """build_legacy_proposals with a second model's candidates and an
+    exploration quota (paged_rollout_benchmark.py:101-210): the oracle
+    selects the reference's proposals in the reference's order."""
+    from graph_rewrite_system_b200 import synthetic
+    from oracle import proposals as P
+
+    rules = synthetic.synthetic_rules()
+    index = P.build_rule_index(rules.source_to_xfers(), rules.gate_deltas(), rules.num_sources, 1)
+    maxp = max(map(len, rules.source_gate_types))
+    for name, case in exploration_golden().items():
+        primary, explored, gates, cap, global_cap = exploration_inputs(case, maxp)
+        sel, metrics = P.rank_proposals_exploration(
+            primary, explored, gates, index, per_parent_cap=cap,
+            exploration_per_parent=case["quota"], global_cap=global_cap)
+        got = [[int(p), int(x), int(a), list(b), int(n)] for p, x, a, b, n in zip(
+            sel["parent"], sel["xfer"], sel["anchor"], sel["binding"], sel["next_gate"])]
+        exp = [[p, x, a, b, n] for p, x, a, b, _, n in case["proposals"]]
+        assert got == exp, name
+        assert metrics == case["metrics"], name

@@ -109,3 +109,56 @@ def test_bf16_rollout_model_shape_invariants(cuda_device):
     search.cache.release_device(search.block_table, search.lengths)
     search.check()
     assert search.cache.allocated_pages == 0
+
+
+@pytest.mark.parametrize("quota,until", [(2, 2), (3, 0), (0, 3)])
+def test_fp32_rollout_with_exploration_model_matches_oracle(cuda_device, quota, until):
+    """A second (exploration) model searched alongside the primary one
+    (paged_rollout_benchmark.py:724-758, 917-961, 1071-1091): per level the
+    same children in the same order, the same proposal and exploration
+    metrics and fingerprints as the oracle search; the second model leaves
+    the search at level `until` (0: stays)."""
+    from graph_rewrite_system_b200 import synthetic
+    from graph_rewrite_system_b200.history import BeamHistoryRecorder, beam_level_line
+    from graph_rewrite_system_b200.rollout import DeviceBeamSearch
+    from oracle.model import OracleModel, parameter_shapes
+    from oracle.rollout import OracleBeamSearch
+    from test_paged_model_gpu import build_model
+
+    cfg = synthetic.ModelConfig(**SMALL)
+    rc = synthetic.RolloutConfig(beam_size=12, depth=5, page_size=4, max_candidates_per_state=400,
+                                 per_parent_cap=4, proposal_factor=4)
+    rules, model, oracle_model, circuit = _setup(cuda_device, torch.float32, cfg, 3, 4, 30, rc)
+    x_model = build_model(cuda_device, torch.float32, rules, cfg, 9)
+    x_params = synthetic.deterministic_parameters(parameter_shapes(cfg, rules), 9)
+    x_oracle = OracleModel({k: torch.from_numpy(v) for k, v in x_params.items()}, rules, cfg)
+    oracle = OracleBeamSearch(oracle_model, rules, circuit, rc, synthetic.SELECT_ALL_THRESHOLDS,
+                              exploration_model=x_oracle, exploration_per_parent=quota,
+                              exploration_until_depth=until)
+    oracle.reset()
+    search = DeviceBeamSearch(model, rules, circuit, rc, cuda_device, exploration_model=x_model,
+                              exploration_per_parent=quota, exploration_until_depth=until)
+    search.reset()
+    recorder = BeamHistoryRecorder(search)
+    for level in range(rc.depth):
+        exp = oracle.step()
+        got = search.step()
+        if exp is None:
+            assert got is None
+            break
+        for key in ("accepted_actions", "attempted_actions", "invalid_structural_actions",
+                    "duplicate_speculative_successors", "proposals_after_caps",
+                    "predicted_actions", "eligible_actions_before_parent_cap",
+                    "exploration_predicted_actions", "exploration_eligible_actions",
+                    "selected_exploration_proposals"):
+            assert getattr(got, key) == exp.get(key, 0), (got.step, key)
+        assert search.last_children() == exp["children"], got.step
+        fps = [int(x) & ((1 << 64) - 1) for x in search.topo.fingerprint.tolist()]
+        assert fps == [n.topology.fingerprint for n in oracle.beam]
+        recorder.record()
+        assert beam_level_line(recorder.depth, recorder.states()) == beam_level_line(
+            got.step, [(n.gate_count, n.history) for n in oracle.beam])
+        assert search.exploring == (until == 0 or level < until)
+    if until and rc.depth > until:
+        assert search.exploration_cache.allocated_pages == 0     # released when it left
+    search.check()
