@@ -1,7 +1,7 @@
 """Benchmark of the B200 beam-search decode path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload rollout|decode-attention|update-gemm|graph-mlp]
+                    [--workload rollout|decode-attention|update-gemm|graph-mlp|cache-churn]
 
 Workloads (seeded synthetic inputs; the reference's hwb6 circuit, rule set
 and checkpoint are not available):
@@ -26,6 +26,12 @@ and checkpoint are not available):
   512 beams, one query token each, 8 heads x 32, bf16, 381 shared s0 node
   keys, 64 action K/V entries per beam in pages of 16, block tables from a
   random prefix tree.  A step is one decode-attention launch over all beams.
+* ``cache-churn``: the paged KV cache alone - 1000 live beams, 4 layers x 8
+  heads x 32 bf16 K/V per action, page 16, depth 64; each level forks every
+  beam into 5 children, keeps the top 1000 by seeded uniform scores, appends
+  one token to each (copy-on-write of partial tail pages) and releases the
+  previous level (refcount reclaim).  A step is one level; the L2 is flushed
+  before each timed level.
 
 Timing: each timed step is bracketed by CUDA events on the launching stream,
 with barrier + synchronize around the timed region and the max over ranks.
@@ -662,6 +668,49 @@ def run_rollout(args, world, rank, device):
     return line
 
 
+def run_sharded_config5(args, world, rank, device) -> dict:
+    """The sharded-beam workload: synthetic 24-qubit, 2000-gate circuit, the
+    same model, 1000 beams per GPU (global beam 1000 x GPUs), depth 64; one
+    untimed search, then the last K levels of a second one timed like the
+    headline (CUDA events per level, max over ranks)."""
+    depth = ROLLOUT_DEPTH
+    steps, first = rollout_window(args.steps, args.warmup)
+    search, rc = build_rollout(device, beam_size=1000, depth=depth, seed=0, world=world,
+                               qubits=24, gates=2000)
+    stream = torch.cuda.current_stream(device)
+    search.run(depth)
+    search.reset()
+    for _ in range(first - 1):
+        if search.step() is None:
+            raise RuntimeError(f"the search ended before level {first}")
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+    done = 0
+    with ClockSampler(device.index) as clocks:
+        for a, b in events:
+            a.record(stream)
+            row = search.step()
+            b.record(stream)
+            done += 1
+            if row is None:
+                break
+        torch.cuda.synchronize(device)
+    search.check()
+    total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in events[:done]), world, device)
+    slots = search.slots
+    del search
+    torch.cuda.empty_cache()
+    return {"workload": "sharded beam: synthetic 24-qubit 2000-gate circuit, same model, beam "
+                        f"1000 per GPU ({1000 * world} global), depth {depth}, levels "
+                        f"{first}..{first + done - 1} timed",
+            "value": world * done * 1e3 / total_ms, "unit": "steps/s (B=1000-equivalent)",
+            "ms_per_step": total_ms / done, "timed_levels": f"{first}..{first + done - 1}",
+            "beam_per_gpu": 1000, "global_beam": 1000 * world, "slots": slots,
+            "clocks": clocks.summary()}
+
+
 def cpu_rollout(levels: int, warmup: int, sample_beams: int, full_beams: int = 1000):
     """The oracle beam search (the reference's loop restated on the host,
     fp32) on a bounded beam of the 64-level search: `warmup` untimed levels,
@@ -707,6 +756,25 @@ def run_reference(args, world, rank):
     if args.workload in ("update-gemm", "graph-mlp"):
         return {"impl": "reference", "unavailable": f"the {args.workload} microbenchmark has no "
                 "CPU arm; the rollout workload's reference arm times the CPU oracle"}
+    if args.workload == "cache-churn":
+        started = time.perf_counter()
+        levels = max(1, min(args.steps, CHURN["depth"] - args.warmup))
+        base = cpu_cache_churn(levels)
+        value = base["value"]
+        return {
+            "metric": "paged-cache churn levels/s (1000 beams, fork x5, top 1000, append, release)",
+            "impl": "reference", "value": value, "unit": "levels/s", "n_gpus": world,
+            "steps": levels, "warmup": CHURN["depth"] - levels, "ms_per_step": 1e3 / value,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "cache churn (the oracle's sequential PagedKVCache): 1000 "
+                                   "beams, 4 layers x 8 heads x 32, page 16, depth 64, 5 children",
+                       "timed_levels": f"{CHURN['depth'] - levels + 1}..{CHURN['depth']}"},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": value, "unit": "levels/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "wall_seconds": time.perf_counter() - started,
+        }
     if args.workload == "rollout":
         started = time.perf_counter()
         steps, first = rollout_window(args.steps, args.warmup)
@@ -941,6 +1009,226 @@ def run_graph_mlp(args, world, rank, device):
     }
 
 
+# cache-churn workload: 1000 live beams, 4 causal layers x 8 heads x 32 bf16
+# K/V per action, page 16, depth 64, 5 children per beam
+CHURN = dict(beams=1000, children=5, depth=64, layers=4, heads=8, head_width=32, width=256,
+             page=16)
+
+
+def churn_token_bytes(c=CHURN) -> int:
+    """Bytes of one token row across every arena: K and V of each layer, the
+    action state, the readout K and V (bf16)."""
+    hd = c["heads"] * c["head_width"]
+    return 2 * (2 * c["layers"] * hd + c["width"] + 2 * hd)
+
+
+def churn_plan(seed: int, c=CHURN) -> list[torch.Tensor]:
+    """Per level, the surviving children's parent rows: every beam forks into
+    `children`, each child draws a seeded uniform score, the top `beams`
+    (stable sort, ties by index) survive."""
+    gen = torch.Generator().manual_seed(seed)
+    plan, n = [], 1
+    for _ in range(c["depth"]):
+        scores = torch.rand(n * c["children"], generator=gen)
+        parents = torch.sort(scores, descending=True, stable=True).indices[:c["beams"]]
+        plan.append(parents // c["children"])
+        n = plan[-1].numel()
+    return plan
+
+
+def churn_level_bytes(parent_lengths: list[int], parent_cols: int, n_prev: int,
+                      c=CHURN) -> int:
+    """Algorithmic HBM bytes of one churn level: every child writes its new
+    token row; a child whose parent ends in a partial page copies that page's
+    `length % page` rows to its own page (read + write); the parent block-table
+    rows and lengths are read and the child rows written; the released rows
+    are read once."""
+    token = churn_token_bytes(c)
+    rows = sum(1 + 2 * (length % c["page"]) for length in parent_lengths)
+    n = len(parent_lengths)
+    tables = 4 * (n * (parent_cols + 1) + n * (parent_cols + 2) + n_prev * (parent_cols + 1))
+    return token * rows + tables
+
+
+def cpu_cache_churn(levels: int, seed: int = 0) -> dict:
+    """The oracle's PagedKVCache (the reference's sequential append/release
+    loop restated) over the same churn: all 64 levels run, the last `levels`
+    timed."""
+    from oracle.paged_cache import OraclePagedKVCache
+
+    c = CHURN
+    cap = c["beams"] * (-(-c["depth"] // c["page"]) + 3)
+    ref = OraclePagedKVCache(layers=c["layers"], capacity=cap, page_size=c["page"],
+                             heads=c["heads"], head_width=c["head_width"],
+                             model_width=c["width"], dtype=torch.bfloat16)
+    gen = torch.Generator().manual_seed(seed + 1)
+    handles = [ref.empty_handle()]
+    first = c["depth"] - levels
+    seconds = 0.0
+    for level, parents in enumerate(churn_plan(seed)):
+        n = parents.numel()
+        kv = torch.randn(c["layers"], n, c["heads"], c["head_width"], generator=gen).bfloat16()
+        act = torch.randn(n, c["width"], generator=gen).bfloat16()
+        rk = torch.randn(n, c["heads"], c["head_width"], generator=gen).bfloat16()
+        t0 = time.perf_counter()
+        new = ref.append_batch([handles[p] for p in parents.tolist()], kv, kv, act, rk, rk)
+        for h in handles:
+            ref.release(h)
+        handles = new
+        if level >= first:
+            seconds += time.perf_counter() - t0
+    return {"value": levels / seconds, "unit": "levels/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"the oracle cache (sequential per-handle loop) over the "
+                                      f"whole 64-level churn at 1000 beams, levels "
+                                      f"{first + 1}..{c['depth']} timed, unscaled"}
+
+
+def run_cache_churn(args, world, rank, device):
+    """The paged-cache churn workload (1000 live beams, 4 layers x 8 heads x
+    32 bf16 K/V per action, page 16, depth 64, 5 children per beam with
+    seeded uniform scores, the top 1000 kept).  A step is one level on the
+    device: the survivors' parent block-table rows are gathered, one token is
+    appended to each (grs_cache_append: fork with copy-on-write of partial
+    tail pages, then the token rows in every arena) and the previous level's
+    rows are released (grs_cache_release: refcount reclaim in release order).
+    The survivor choice (the search's ranking, not the cache's work) and the
+    token contents are drawn before timing.  All 64 levels run; the last
+    `steps` are timed, each after an L2 flush."""
+    from graph_rewrite_system_b200.paged_cache import PagedKVCache
+
+    c = CHURN
+    levels = max(1, min(args.steps, c["depth"] - args.warmup))
+    first = c["depth"] - levels
+    cap = c["beams"] * (-(-c["depth"] // c["page"]) + 3)
+    cache = PagedKVCache(layers=c["layers"], capacity=cap, page_size=c["page"],
+                         heads=c["heads"], head_width=c["head_width"], model_width=c["width"],
+                         device=device, dtype=torch.bfloat16)
+    plan = [p.to(device) for p in churn_plan(rank)]
+    gen = torch.Generator(device=device).manual_seed(rank + 1)
+    hd = (c["heads"], c["head_width"])
+    tokens = []
+    for p in plan:
+        n = p.numel()
+        tokens.append(tuple(torch.randn(shape, device=device, generator=gen).bfloat16() for shape in
+                            ((c["layers"], n) + hd, (c["layers"], n) + hd, (n, c["width"]),
+                             (n,) + hd, (n,) + hd)))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def level(state, i):
+        table, lengths = state
+        pt, pl = table.index_select(0, plan[i]), lengths.index_select(0, plan[i])
+        ct, cl = cache.append_device(pt, pl, *tokens[i])
+        cache.release_device(table, lengths)
+        return ct, cl
+
+    def start():
+        cache.reset()
+        return (torch.zeros(1, 1, dtype=torch.int32, device=device),
+                torch.zeros(1, dtype=torch.int32, device=device))
+
+    # untimed pass: warm-up, and the algorithmic bytes of every timed level
+    state = start()
+    level_bytes = []
+    for i in range(c["depth"]):
+        if i >= first:
+            lengths = state[1].index_select(0, plan[i]).tolist()
+            level_bytes.append(churn_level_bytes(lengths, state[0].shape[1], state[1].numel()))
+        state = level(state, i)
+    cache.check_status()
+    # timed pass
+    state = start()
+    for i in range(first):
+        state = level(state, i)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(levels)]
+    launches0 = launch_count()
+    with ClockSampler(device.index) as clocks:
+        for j, i in enumerate(range(first, c["depth"])):
+            flush.fill_(j & 0xFF)
+            events[j][0].record(stream)
+            state = level(state, i)
+            events[j][1].record(stream)
+        torch.cuda.synchronize(device)
+    launches = launch_count() - launches0
+    cache.check_status()
+    level_ms = [a.elapsed_time(b) for a, b in events]
+    ms = max_over_ranks(sum(level_ms), world, device) / levels
+    avg_bytes = sum(level_bytes) / levels
+    # end to end: each level's token rows and survivor indices copied in from
+    # pinned host memory, the child lengths and the status word read back
+    host_tokens = [tuple(t.cpu().pin_memory() for t in tokens[i]) for i in range(first, c["depth"])]
+    host_plan = [plan[i].to(torch.int32).cpu().pin_memory() for i in range(first, c["depth"])]
+    host_lengths = torch.empty(c["beams"], dtype=torch.int32).pin_memory()
+    host_status = torch.empty(1, dtype=torch.int32).pin_memory()
+    dev_tokens = [torch.empty(t.shape, dtype=t.dtype, device=device) for t in host_tokens[0]]
+    dev_plan = torch.empty(c["beams"], dtype=torch.int32, device=device)
+    state = start()
+    for i in range(first):
+        state = level(state, i)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h2d = d2h = 0
+    e0.record(stream)
+    for j in range(levels):
+        for dst, src in zip(dev_tokens, host_tokens[j]):
+            dst.copy_(src, non_blocking=True)
+            h2d += src.numel() * src.element_size()
+        n = host_plan[j].numel()
+        dev_plan[:n].copy_(host_plan[j], non_blocking=True)
+        h2d += 4 * n
+        table, lengths = state
+        pidx = dev_plan[:n]
+        ct, cl = cache.append_device(table.index_select(0, pidx), lengths.index_select(0, pidx),
+                                     *dev_tokens)
+        cache.release_device(table, lengths)
+        state = (ct, cl)
+        host_lengths[:n].copy_(cl, non_blocking=True)
+        host_status.copy_(cache.status_tensor(), non_blocking=True)
+        d2h += 4 * n + 4
+        stream.synchronize()
+        if int(host_status[0]):
+            raise RuntimeError(f"cache kernel reported status {int(host_status[0])}")
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device) / levels
+    peaks = measured_peaks()
+    achieved = avg_bytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "paged-cache churn levels/s (1000 beams, fork x5, top 1000, append, release)",
+        "value": world * 1e3 / ms, "unit": "levels/s", "n_gpus": world, "steps": levels,
+        "warmup": first, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cache churn: 1000 live beams, 4 causal layers x 8 heads x 32 bf16 "
+                               "K/V per action (+ action state, readout K/V), page 16, depth 64, "
+                               "each level forks every beam into 5 children with seeded uniform "
+                               "scores and keeps the top 1000; levels "
+                               f"{first + 1}..{c['depth']} timed",
+                   "timed_levels": f"{first + 1}..{c['depth']}", "beams_per_gpu": c["beams"],
+                   "l2": "L2 flushed (256 MB write) before every timed level",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "e2e": {"value": world * 1e3 / e2e_ms, "unit": "levels/s",
+                "h2d_bytes_per_step": h2d // levels, "d2h_bytes_per_step": d2h // levels,
+                "scope": "PagedKVCache.append_device / release_device per level with the token "
+                         "rows and survivor indices copied from pinned host memory and the "
+                         "child lengths and status read back"},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "traffic": None, "kernel": "one churn level (append + release)",
+                     "algorithmic_bytes_per_level": avg_bytes,
+                     "level_ms": [round(x, 4) for x in level_ms],
+                     "peak_source": f"{peaks['source']} hbm_gbs"},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_cache_churn(levels)
+    return line
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -948,12 +1236,14 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=4)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--workload", choices=("rollout", "decode-attention", "update-gemm",
-                                               "graph-mlp"), default="rollout")
+                                               "graph-mlp", "cache-churn"), default="rollout")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--beam", type=int, default=1000,
                         help="rollout beam size (1000 is the benchmark configuration)")
     parser.add_argument("--no-attention", action="store_true",
                         help="rollout only: skip the paged-attention sub-benchmark")
+    parser.add_argument("--no-config5", action="store_true",
+                        help="rollout only: skip the sharded-beam (24-qubit, 2000-gate) block")
     parser.add_argument("--qubits", type=int, default=6,
                         help="rollout circuit qubits (24 with --gates 2000: the sharded config)")
     parser.add_argument("--gates", type=int, default=259, help="rollout circuit gates")
@@ -973,6 +1263,9 @@ def main() -> None:
     sleep_cycles_per_us()            # calibrate the device sleep before any timed region
     if args.workload == "rollout":
         line = run_rollout(args, world, rank, device)
+        if not args.no_config5 and (args.qubits, args.gates) != (24, 2000):
+            torch.cuda.empty_cache()
+            line["sharded_config5"] = run_sharded_config5(args, world, rank, device)
         if not args.no_attention:
             attn_args = argparse.Namespace(steps=20, warmup=5, no_cpu_baseline=True)
             attention = run_decode_attention(attn_args, world, rank, device)
@@ -982,6 +1275,8 @@ def main() -> None:
         line = run_update_gemm(args, world, rank, device)
     elif args.workload == "graph-mlp":
         line = run_graph_mlp(args, world, rank, device)
+    elif args.workload == "cache-churn":
+        line = run_cache_churn(args, world, rank, device)
     else:
         line = run_decode_attention(args, world, rank, device)
     if rank == 0:

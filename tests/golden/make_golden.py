@@ -311,6 +311,8 @@ def main() -> None:
                             **exploration_cases(ref_prb, ref_bsb))
     if not only or "checkpoint" in only:
         np.savez_compressed(HERE / "checkpoint_tiny.npz", **checkpoint_case(args.reference))
+    if not only or "rollout" in only:
+        np.savez_compressed(HERE / "rollout_reference_loop.npz", **rollout_case())
     print("golden fixtures written to", HERE)
 
 
@@ -576,6 +578,143 @@ def checkpoint_case(reference: Path, *, seed=4, beams=3, actions=4):
         "destination_slots", "destination_types")}
     out.update(encode_states=states.numpy(), encode_live=live.numpy(), encode_types=types.numpy())
     return out
+
+
+def rollout_case(*, seed=7, beam_size=12, depth=6, qubits=4, gates=30):
+    """Six levels of the reference's own search loop on the CPU (fp32):
+    paged_model_matches with tensorized state batches and threshold candidate
+    tensors, build_gpu_proposals with the effective parent cap, the lazy_child
+    accept loop (indexed topology, raw dedup), the gate-count sort and
+    advance_selected over a PagedKVCache (paged_rollout_benchmark.py:243-556,
+    898-1093).  Seeded weights (synthetic.deterministic_parameters), the
+    synthetic rule set and a seeded random circuit."""
+    import json
+    import math
+    from collections import defaultdict
+
+    import beam_search_benchmark as bsb
+    import dataset as ref_dataset
+    import gpu_proposals as gp
+    import incremental_graph as ig
+    import lazy_rollout_benchmark as lrb
+    import paged_cache as ref_cache
+    import paged_model as ref_model
+    import paged_rollout_benchmark as prb
+    from graph_rewrite_system_b200 import synthetic
+    from oracle.model import parameter_shapes
+
+    cfg = synthetic.ModelConfig(**ROLLOUT_GOLDEN_MODEL)
+    rc = synthetic.RolloutConfig(**ROLLOUT_GOLDEN_SEARCH)
+    assert (rc.beam_size, rc.depth) == (beam_size, depth)
+    rules = synthetic.synthetic_rules()
+    ref_rules = ref_dataset.RuleMetadata.from_payload({
+        "source_patterns": list(rules.source_patterns),
+        "xfer_to_source": list(rules.xfer_to_source),
+        "xfer_sources": list(rules.xfer_sources),
+        "xfer_destinations": list(rules.xfer_destinations)})
+    model = ref_model.PagedActionBindingModel(
+        ref_rules, num_xfers=rules.num_xfers, width=cfg.width,
+        retrieval_width=cfg.retrieval_width, graph_layers=cfg.graph_layers,
+        action_layers=cfg.action_layers, action_heads=cfg.action_heads,
+        max_sequence_length=cfg.max_sequence_length,
+        readout_graph_layers=cfg.readout_graph_layers, readout_attention_backend="paged",
+        dropout=0.0).eval()
+    state = model.state_dict()
+    for k, v in synthetic.deterministic_parameters(parameter_shapes(cfg, rules), seed).items():
+        assert tuple(state[k].shape) == v.shape, k
+        state[k] = torch.from_numpy(v)
+    model.load_state_dict(state)
+    device = torch.device("cpu")
+
+    source_to_xfers = defaultdict(list)
+    for xfer, source in enumerate(ref_rules.xfer_to_source):
+        source_to_xfers[source].append(xfer)
+    gate_deltas = [len(ref_rules.destination_gate_types[x])
+                   - len(ref_rules.source_gate_types[ref_rules.xfer_to_source[x]])
+                   for x in range(len(ref_rules.xfer_to_source))]
+    rule_index = gp.GpuRuleIndex.build(source_to_xfers, gate_deltas,
+                                       len(ref_rules.source_gate_types), rc.max_gate_increase,
+                                       device)
+    src_pat = tuple(ig.parse_pattern(p) for p in ref_rules.xfer_sources)
+    dst_pat = tuple(ig.parse_pattern(p) for p in ref_rules.xfer_destinations)
+
+    circuit = synthetic.random_circuit(qubits, gates, seed + 1)
+    snapshot = circuit.snapshot()
+    beam = [bsb.BeamState(graph=None, snapshot=snapshot, guid_to_slot={}, next_slot=gates,
+                          last_touched={}, rewrite_distance={n[0]: 5 for n in snapshot["nodes"]},
+                          previous_preferred=set(), local_streak=0, gate_count=gates, depth=0,
+                          history=(), topology_index=lrb.indexed_topology(snapshot))]
+    with torch.no_grad():
+        slot_states, live, gate_types = model.initialize_incremental(prb.initial_batch(snapshot))
+        source_vectors = model.retrieval_source(model.source_representations())
+    arena = ref_cache.PagedKVCache(layers=cfg.action_layers, capacity=rc.cache_pages,
+                                   page_size=rc.page_size, heads=cfg.action_heads,
+                                   head_width=cfg.width // cfg.action_heads,
+                                   model_width=cfg.width, device=device, dtype=torch.float32)
+    handles = [arena.empty_handle()]
+    seen = {lrb.raw_topology_hash(snapshot)}
+    out = {"circuit_nodes": [list(n) for n in circuit.nodes],
+           "circuit_edges": [list(e) for e in circuit.edges], "levels": [],
+           "model": ROLLOUT_GOLDEN_MODEL, "search": ROLLOUT_GOLDEN_SEARCH, "seed": seed,
+           "qubits": qubits, "gates": gates}
+    states_out = {}
+    for step in range(depth):
+        with torch.no_grad():
+            candidates, _, _ = prb.paged_model_matches(
+                beam, slot_states, live, gate_types, handles, arena, model, device,
+                synthetic.SELECT_ALL_THRESHOLDS, source_vectors, rc.microbatch,
+                rc.max_candidates_per_state, "tensorized", "gpu")
+        cap = max(rc.per_parent_cap, math.ceil(rc.beam_size / max(1, len(beam))) * 2)
+        proposals, metrics, _ = gp.build_gpu_proposals(candidates, beam, rule_index,
+                                                       per_parent_cap=cap,
+                                                       global_cap=rc.global_cap)
+        records = []
+        attempted = invalid = duplicates = 0
+        for proposal in proposals:
+            if len(records) >= rc.beam_size:
+                break
+            attempted += 1
+            child, fingerprint, is_dup = lrb.lazy_child(beam[proposal.parent], proposal, src_pat,
+                                                        dst_pat, False, "raw", seen, "indexed")
+            if is_dup:
+                duplicates += 1
+                continue
+            if child is None:
+                invalid += 1
+                continue
+            seen.add(fingerprint)
+            records.append((child, proposal))
+        level = {"input_states": len(beam), "proposals_after_caps": len(proposals),
+                 "predicted_actions": int(metrics["predicted_actions"]),
+                 "eligible_actions": int(metrics["eligible_actions"]),
+                 "attempted": attempted, "invalid": invalid, "duplicates": duplicates}
+        if not records:
+            out["levels"].append(level | {"children": []})
+            break
+        records.sort(key=lambda row: (row[0].gate_count, len(row[0].history)))
+        records = records[:rc.beam_size]
+        with torch.no_grad():
+            slot_states, live, gate_types, handles, _, _ = prb.advance_selected(
+                slot_states, live, gate_types, handles, records, ref_rules, arena, model,
+                device, rc.microbatch)
+        beam = [r[0] for r in records]
+        level["children"] = [[int(p.parent), int(p.xfer_id), int(p.anchor_slot),
+                              [int(x) for x in p.binding], int(c.gate_count)]
+                             for c, p in records]
+        level["candidate_count"] = int(candidates.batch_ids.numel())
+        out["levels"].append(level)
+        states_out[f"states_{step}"] = slot_states.numpy()
+        states_out[f"live_{step}"] = live.numpy()
+        states_out[f"types_{step}"] = gate_types.numpy()
+    return {"json": np.array(json.dumps(out)), **states_out}
+
+
+# The model and search settings of the reference-loop fixture (rollout_case);
+# the oracle test rebuilds the same model from the same seed.
+ROLLOUT_GOLDEN_MODEL = dict(width=32, retrieval_width=16, graph_layers=1, action_layers=2,
+                            action_heads=2, max_sequence_length=16, readout_graph_layers=1)
+ROLLOUT_GOLDEN_SEARCH = dict(beam_size=12, depth=6, page_size=4, max_candidates_per_state=400,
+                             per_parent_cap=4, proposal_factor=4)
 
 
 if __name__ == "__main__":

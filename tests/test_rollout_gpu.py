@@ -162,3 +162,47 @@ def test_fp32_rollout_with_exploration_model_matches_oracle(cuda_device, quota, 
     if until and rc.depth > until:
         assert search.exploration_cache.allocated_pages == 0     # released when it left
     search.check()
+
+
+def test_fp32_device_search_matches_reference_loop(cuda_device):
+    """The device search against the reference's own loop, recorded in
+    tests/golden/rollout_reference_loop.npz (six CPU fp32 levels of
+    paged_model_matches -> build_gpu_proposals -> lazy_child -> advance_selected,
+    paged_rollout_benchmark.py:243-556, 898-1093): every level's children,
+    counts and metrics equal, slot states within 1e-4."""
+    import json
+
+    from conftest import load_golden
+    from graph_rewrite_system_b200 import synthetic
+    from graph_rewrite_system_b200.rollout import DeviceBeamSearch
+    from test_paged_model_gpu import build_model
+
+    g = load_golden("rollout_reference_loop.npz")
+    spec = json.loads(str(g["json"]))
+    cfg = synthetic.ModelConfig(**spec["model"])
+    rc = synthetic.RolloutConfig(**spec["search"])
+    rules = synthetic.synthetic_rules()
+    model = build_model(cuda_device, torch.float32, rules, cfg, spec["seed"])
+    circuit = synthetic.random_circuit(spec["qubits"], spec["gates"], spec["seed"] + 1)
+    search = DeviceBeamSearch(model, rules, circuit, rc, cuda_device)
+    search.reset()
+    for step, level in enumerate(spec["levels"]):
+        got = search.step()
+        assert got is not None
+        assert got.input_states == level["input_states"]
+        assert got.proposals_after_caps == level["proposals_after_caps"]
+        assert got.predicted_actions == level["predicted_actions"]
+        assert got.eligible_actions_before_parent_cap == level["eligible_actions"]
+        assert got.attempted_actions == level["attempted"]
+        assert got.invalid_structural_actions == level["invalid"]
+        assert got.duplicate_speculative_successors == level["duplicates"]
+        assert search.last_children() == [(c[0], c[1], tuple(c[3])) for c in level["children"]]
+        assert search.topo.gate.tolist() == [c[4] for c in level["children"]]
+        live = g[f"live_{step}"]
+        s = live.shape[1]
+        assert np.array_equal(search.live[:, :s].cpu().numpy(), live)
+        assert not search.live[:, s:].any()
+        assert np.array_equal(search.types[:, :s].cpu().numpy(), g[f"types_{step}"])
+        got_states = search.states[:, :s].float().cpu().numpy() * live[..., None]
+        np.testing.assert_allclose(got_states, g[f"states_{step}"] * live[..., None],
+                                   rtol=1e-4, atol=1e-4)
