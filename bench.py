@@ -419,7 +419,7 @@ def run_decode_attention(args, world, rank, device):
                      "logical_bytes": logical,
                      "logical_gbs": logical / (kernel_ms * 1e-3) / 1e9,
                      "peak_source": f"{peaks['source']} hbm_gbs",
-                     "kernel": "decode_cluster_kernel"},
+                     "kernel": "decode_shared_kernel"},
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -629,6 +629,7 @@ def run_rollout(args, world, rank, device):
                                f"{depth}-level search timed",
                    "beam": rc.beam_size, "depth": depth, "timed_levels": window,
                    "untimed_levels_before_window": first - 1, "page_size": rc.page_size,
+                   "level_ms": [round(x, 3) for x in step_ms],
                    "l2": "inputs larger than L2 (beam state ~0.2 GB bf16 per activation)",
                    "circuit": f"{args.qubits} qubits, {args.gates} gates",
                    "beam_per_gpu": args.beam,
@@ -1094,6 +1095,7 @@ def run_cache_churn(args, world, rank, device):
     The survivor choice (the search's ranking, not the cache's work) and the
     token contents are drawn before timing.  All 64 levels run; the last
     `steps` are timed, each after an L2 flush."""
+    from graph_rewrite_system_b200 import kernels as K
     from graph_rewrite_system_b200.paged_cache import PagedKVCache
 
     c = CHURN
@@ -1115,10 +1117,17 @@ def run_cache_churn(args, world, rank, device):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
 
-    def level(state, i):
+    def level(state, i, index=None):
+        # every child of level i holds i + 1 tokens: its table row is exactly
+        # ceil((i + 1) / page) pages wide
         table, lengths = state
-        pt, pl = table.index_select(0, plan[i]), lengths.index_select(0, plan[i])
-        ct, cl = cache.append_device(pt, pl, *tokens[i])
+        index = plan[i] if index is None else index
+        n = index.numel()
+        pt = torch.empty(n, table.shape[1], dtype=torch.int32, device=device)
+        pl = torch.empty(n, dtype=torch.int32, device=device)
+        K.gather_beams(table, index, pt)
+        K.gather_beams(lengths, index, pl)
+        ct, cl = cache.append_device(pt, pl, *tokens[i], child_cols=-(-(i + 1) // c["page"]))
         cache.release_device(table, lengths)
         return ct, cl
 
@@ -1160,11 +1169,11 @@ def run_cache_churn(args, world, rank, device):
     # end to end: each level's token rows and survivor indices copied in from
     # pinned host memory, the child lengths and the status word read back
     host_tokens = [tuple(t.cpu().pin_memory() for t in tokens[i]) for i in range(first, c["depth"])]
-    host_plan = [plan[i].to(torch.int32).cpu().pin_memory() for i in range(first, c["depth"])]
+    host_plan = [plan[i].cpu().pin_memory() for i in range(first, c["depth"])]
     host_lengths = torch.empty(c["beams"], dtype=torch.int32).pin_memory()
     host_status = torch.empty(1, dtype=torch.int32).pin_memory()
     dev_tokens = [torch.empty(t.shape, dtype=t.dtype, device=device) for t in host_tokens[0]]
-    dev_plan = torch.empty(c["beams"], dtype=torch.int32, device=device)
+    dev_plan = torch.empty(c["beams"], dtype=torch.int64, device=device)
     state = start()
     for i in range(first):
         state = level(state, i)
@@ -1179,13 +1188,12 @@ def run_cache_churn(args, world, rank, device):
             h2d += src.numel() * src.element_size()
         n = host_plan[j].numel()
         dev_plan[:n].copy_(host_plan[j], non_blocking=True)
-        h2d += 4 * n
-        table, lengths = state
-        pidx = dev_plan[:n]
-        ct, cl = cache.append_device(table.index_select(0, pidx), lengths.index_select(0, pidx),
-                                     *dev_tokens)
-        cache.release_device(table, lengths)
-        state = (ct, cl)
+        h2d += 8 * n
+        i = first + j
+        tokens_i, tokens[i] = tokens[i], tuple(dev_tokens)
+        state = level(state, i, dev_plan[:n])
+        tokens[i] = tokens_i
+        ct, cl = state
         host_lengths[:n].copy_(cl, non_blocking=True)
         host_status.copy_(cache.status_tensor(), non_blocking=True)
         d2h += 4 * n + 4

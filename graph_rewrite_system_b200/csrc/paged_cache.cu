@@ -154,6 +154,91 @@ __global__ void cache_write_kernel(CacheArenas ar, const int32_t* __restrict__ p
   }
 }
 
+// The same as cache_write_kernel when every row is a whole number of 16-byte
+// vectors and every base is 16-byte aligned (the layouts the model uses):
+// one CTA per child treats its segments (K and V of each layer, actions,
+// readout K and V) as one flat list of 16-byte vectors - the COW rows of the
+// parent's tail page, then the new row - and moves WV_BATCH of them per
+// thread per round, all loads before the stores, so each round costs one
+// memory latency instead of one per vector.
+constexpr int WV_THREADS = 256;
+constexpr int WV_BATCH = 8;
+__global__ void __launch_bounds__(WV_THREADS) cache_write_vec_kernel(
+    CacheArenas ar, const int32_t* __restrict__ ptable, int64_t pstride,
+    const int32_t* __restrict__ plengths, const int32_t* __restrict__ ctable, int64_t cstride,
+    int n, const char* __restrict__ new_keys, const char* __restrict__ new_values,
+    const char* __restrict__ new_actions, const char* __restrict__ new_rkeys,
+    const char* __restrict__ new_rvalues, int32_t* __restrict__ free_count,
+    const int32_t* __restrict__ status) {
+  const int i = blockIdx.x;
+  if (i == 0 && threadIdx.x == 0) {
+    const int fc = *free_count;
+    *free_count = fc >= n ? fc - n : 0;
+  }
+  if (*status != 0) return;
+  const int len = plengths[i];
+  const int offset = len % ar.page;
+  const int nb = blocks_for(len, ar.page);
+  const int dst = ctable[(int64_t)i * cstride + (offset == 0 ? nb : nb - 1)];
+  if (dst < 0 || dst >= ar.capacity) return;
+  int src = dst;
+  if (offset != 0) {
+    src = ptable[(int64_t)i * pstride + nb - 1];
+    if (src < 0 || src >= ar.capacity) return;
+  }
+  const int rows = offset + 1;                       // COW rows, then the new row
+  const int kv_vecs = ar.hd * ar.elem / 16, act_vecs = ar.width * ar.elem / 16;
+  const int64_t kv_row = (int64_t)ar.hd * ar.elem, act_row = (int64_t)ar.width * ar.elem;
+  const int64_t kv_page = kv_row * ar.page, act_page = act_row * ar.page;
+  const int64_t kv_layer = kv_page * ar.capacity;
+  const int per_kv = rows * kv_vecs, per_act = rows * act_vecs;
+  const int kv_segs = 2 * ar.layers;
+  const int total = kv_segs * per_kv + per_act + (new_rkeys ? 2 * per_kv : 0);
+  for (int base = threadIdx.x; base < total; base += WV_THREADS * WV_BATCH) {
+    uint4 val[WV_BATCH];
+    uint4* out[WV_BATCH];
+#pragma unroll
+    for (int k = 0; k < WV_BATCH; ++k) {
+      const int idx = base + k * WV_THREADS;
+      out[k] = nullptr;
+      if (idx >= total) continue;
+      const char* seg;                               // arena segment
+      const char* fresh;                             // the new row of this child
+      int64_t page_bytes, row_bytes;
+      int vecs, rem;
+      if (idx < kv_segs * per_kv) {
+        const int sgi = idx / per_kv;
+        rem = idx - sgi * per_kv;
+        const int l = sgi < ar.layers ? sgi : sgi - ar.layers;
+        seg = (const char*)(sgi < ar.layers ? ar.keys : ar.values) + l * kv_layer;
+        fresh = (sgi < ar.layers ? new_keys : new_values) + ((int64_t)l * n + i) * kv_row;
+        page_bytes = kv_page, row_bytes = kv_row, vecs = kv_vecs;
+      } else if (idx < kv_segs * per_kv + per_act) {
+        rem = idx - kv_segs * per_kv;
+        seg = (const char*)ar.actions;
+        fresh = new_actions + (int64_t)i * act_row;
+        page_bytes = act_page, row_bytes = act_row, vecs = act_vecs;
+      } else {
+        const int r0 = idx - kv_segs * per_kv - per_act;
+        const bool second = r0 >= per_kv;
+        rem = second ? r0 - per_kv : r0;
+        seg = (const char*)(second ? ar.rvalues : ar.rkeys);
+        fresh = (second ? new_rvalues : new_rkeys) + (int64_t)i * kv_row;
+        page_bytes = kv_page, row_bytes = kv_row, vecs = kv_vecs;
+      }
+      const int r = rem / vecs, v = rem - r * vecs;
+      const char* from = r < offset ? seg + src * page_bytes + r * row_bytes + v * 16
+                                    : fresh + v * 16;
+      val[k] = __ldg(reinterpret_cast<const uint4*>(from));
+      out[k] = reinterpret_cast<uint4*>(const_cast<char*>(seg) + dst * page_bytes +
+                                        r * row_bytes + v * 16);
+    }
+#pragma unroll
+    for (int k = 0; k < WV_BATCH; ++k)
+      if (out[k]) *out[k] = val[k];
+  }
+}
+
 // Release pass 1: decrement every page of every handle; remember for each
 // page the last scan position (handle-major) that decremented it.
 __global__ void cache_release_decrement_kernel(int32_t* __restrict__ refcounts,
@@ -327,11 +412,24 @@ extern "C" int grs_cache_append(int elem_bytes, int32_t* refcounts, int32_t* fre
   GRS_CUDA_CHECK_LAUNCH();
   CacheArenas ar{keys, values, actions, readout_keys, readout_values, layers, capacity,
                  page_size, heads_x_width, model_width, elem_bytes};
-  cache_write_kernel<<<n, 128, 0, grs::counted(s)>>>(ar, parent_table, parent_stride, parent_lengths,
-                                       child_table, child_stride, n, (const char*)new_keys,
-                                       (const char*)new_values, (const char*)new_actions,
-                                       (const char*)new_readout_keys,
-                                       (const char*)new_readout_values, free_count, status);
+  const bool vec16 =
+      ((int64_t)heads_x_width * elem_bytes) % 16 == 0 &&
+      ((int64_t)model_width * elem_bytes) % 16 == 0 &&
+      ((uintptr_t)keys | (uintptr_t)values | (uintptr_t)actions | (uintptr_t)new_keys |
+       (uintptr_t)new_values | (uintptr_t)new_actions | (uintptr_t)readout_keys |
+       (uintptr_t)readout_values | (uintptr_t)new_readout_keys |
+       (uintptr_t)new_readout_values) % 16 == 0;
+  if (vec16)
+    cache_write_vec_kernel<<<n, WV_THREADS, 0, grs::counted(s)>>>(
+        ar, parent_table, parent_stride, parent_lengths, child_table, child_stride, n,
+        (const char*)new_keys, (const char*)new_values, (const char*)new_actions,
+        (const char*)new_readout_keys, (const char*)new_readout_values, free_count, status);
+  else
+    cache_write_kernel<<<n, 128, 0, grs::counted(s)>>>(ar, parent_table, parent_stride, parent_lengths,
+                                         child_table, child_stride, n, (const char*)new_keys,
+                                         (const char*)new_values, (const char*)new_actions,
+                                         (const char*)new_readout_keys,
+                                         (const char*)new_readout_values, free_count, status);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
