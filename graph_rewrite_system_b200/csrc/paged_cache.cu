@@ -51,8 +51,14 @@ __global__ void cache_fork_kernel(int32_t* __restrict__ refcounts,
       crow[j] = 0;
       continue;
     }
-    const int old = atomicAdd(&refcounts[p], 1);
-    if (old <= 0) set_status(status, GRS_ERR_BAD_PAGE);
+    // children of one parent (and siblings sharing ancestors) retain the
+    // same pages: one atomic per distinct page among the active lanes
+    const unsigned active = __activemask();
+    const unsigned peers = __match_any_sync(active, p);
+    if ((threadIdx.x & 31) == __ffs(peers) - 1) {
+      const int old = atomicAdd(&refcounts[p], __popc(peers));
+      if (old <= 0) set_status(status, GRS_ERR_BAD_PAGE);
+    }
     crow[j] = p;
   }
   const int fc = *free_count;
@@ -259,7 +265,11 @@ __global__ void cache_release_decrement_kernel(int32_t* __restrict__ refcounts,
 
 // Release pass 2 (one CTA): pages whose count reached zero are appended to
 // the free list in order of their last decrement; last_pos is then reset.
+// Each thread takes REL_PER consecutive scan positions per round, so a round
+// is three memory round trips (lengths, table, refcount + last position) and
+// one block scan.
 constexpr int REL_THREADS = 1024;
+constexpr int REL_PER = 8;
 __global__ void __launch_bounds__(REL_THREADS) cache_release_collect_kernel(
     const int32_t* __restrict__ refcounts, int32_t* __restrict__ last_pos,
     int32_t* __restrict__ free_list, int32_t* __restrict__ free_count, int capacity,
@@ -271,21 +281,34 @@ __global__ void __launch_bounds__(REL_THREADS) cache_release_collect_kernel(
   __syncthreads();
   const int64_t total = (int64_t)n * cols;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t base = 0; base < total; base += REL_THREADS) {
-    const int64_t idx = base + threadIdx.x;
-    int p = -1;
-    if (idx < total) {
-      const int i = (int)(idx / cols), j = (int)(idx % cols);
-      if (j < blocks_for(lengths[i], page)) {
-        const int cand = table[(int64_t)i * stride + j];
-        if (cand >= 0 && cand < capacity && refcounts[cand] == 0 && last_pos[cand] == (int)idx)
-          p = cand;
+  int held[REL_PER];                   // pages of this thread's last round
+  for (int64_t base = 0; base < total; base += (int64_t)REL_THREADS * REL_PER) {
+    const int64_t first = base + (int64_t)threadIdx.x * REL_PER;
+#pragma unroll
+    for (int e = 0; e < REL_PER; ++e) {
+      const int64_t idx = first + e;
+      held[e] = -1;
+      if (idx < total) {
+        const int i = (int)(idx / cols), j = (int)(idx % cols);
+        if (j < blocks_for(lengths[i], page)) {
+          const int cand = table[(int64_t)i * stride + j];
+          if (cand >= 0 && cand < capacity) held[e] = cand;
+        }
       }
     }
-    const int flag = p >= 0 ? 1 : 0;
-    const unsigned ballot = __ballot_sync(0xffffffffu, flag);
-    const int in_warp = __popc(ballot & ((1u << lane) - 1u));
-    if (lane == 0) warp_sums[warp] = __popc(ballot);
+    unsigned flags = 0;
+#pragma unroll
+    for (int e = 0; e < REL_PER; ++e)
+      if (held[e] >= 0 && refcounts[held[e]] == 0 && last_pos[held[e]] == (int)(first + e))
+        flags |= 1u << e;
+    const int count = __popc(flags);
+    int incl = count;                  // block exclusive scan of the counts
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
     __syncthreads();
     if (warp == 0) {
       int v = warp_sums[lane];
@@ -294,25 +317,33 @@ __global__ void __launch_bounds__(REL_THREADS) cache_release_collect_kernel(
         const int y = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += y;
       }
-      warp_sums[lane] = v;  // inclusive
+      warp_sums[lane] = v;             // inclusive over warps
     }
     __syncthreads();
-    const int warp_base = warp == 0 ? 0 : warp_sums[warp - 1];
-    if (flag) {
-      const int pos = running + warp_base + in_warp;
-      if (pos < capacity) free_list[pos] = p;
-    }
+    int pos = running + (warp == 0 ? 0 : warp_sums[warp - 1]) + incl - count;
+#pragma unroll
+    for (int e = 0; e < REL_PER; ++e)
+      if ((flags >> e) & 1u) {
+        if (pos < capacity) free_list[pos] = held[e];
+        ++pos;
+      }
     __syncthreads();
     if (threadIdx.x == 0) running += warp_sums[REL_THREADS / 32 - 1];
     __syncthreads();
   }
   if (threadIdx.x == 0) *free_count = min(running, capacity);
-  __syncthreads();
-  for (int64_t idx = threadIdx.x; idx < total; idx += REL_THREADS) {
-    const int i = (int)(idx / cols), j = (int)(idx % cols);
-    if (j < blocks_for(lengths[i], page)) {
-      const int p = table[(int64_t)i * stride + j];
-      if (p >= 0 && p < capacity) last_pos[p] = -1;
+  // every flag check has read last_pos (the barrier above): reset it
+  if (total <= (int64_t)REL_THREADS * REL_PER) {
+#pragma unroll
+    for (int e = 0; e < REL_PER; ++e)
+      if (held[e] >= 0) last_pos[held[e]] = -1;
+  } else {
+    for (int64_t idx = threadIdx.x; idx < total; idx += REL_THREADS) {
+      const int i = (int)(idx / cols), j = (int)(idx % cols);
+      if (j < blocks_for(lengths[i], page)) {
+        const int p = table[(int64_t)i * stride + j];
+        if (p >= 0 && p < capacity) last_pos[p] = -1;
+      }
     }
   }
 }
