@@ -49,6 +49,7 @@ oracle (the reference's algorithm restated on the host) on the same workload.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 from pathlib import Path
@@ -419,7 +420,7 @@ def run_decode_attention(args, world, rank, device):
                      "logical_bytes": logical,
                      "logical_gbs": logical / (kernel_ms * 1e-3) / 1e9,
                      "peak_source": f"{peaks['source']} hbm_gbs",
-                     "kernel": "decode_shared_kernel"},
+                     "kernel": "decode_cluster_kernel"},
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -649,8 +650,11 @@ def run_rollout(args, world, rank, device):
                             "scope": "DeviceBeamSearch.run(): s0 circuit upload, all 64 "
                                      "levels, beam summary download"},
         "gpu_launches": launches,
+        # traffic: the DRAM / algorithmic byte ratio ncu measured for the
+        # store-epilogue GEMM on the update-projection shape (M = 300000),
+        # applied to the probed launches' algorithmic bytes
         "roofline": probe.roofline(measured_peaks(), "gemm_tc_kernel (store epilogue)",
-                                   profiled_traffic("gemm_store_traffic_ratio")),
+                                   profiled_traffic("update_gemm_traffic_ratio")),
         "search": {"last_level": {k: getattr(last, k) for k in (
                        "step", "input_states", "output_states", "best_speculative_gate_count",
                        "predicted_actions", "eligible_actions_before_parent_cap",
@@ -1269,6 +1273,11 @@ def main() -> None:
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     sleep_cycles_per_us()            # calibrate the device sleep before any timed region
+    # no cyclic-garbage collection pauses inside the measured levels (the
+    # reference's benchmark loop disables the collector the same way,
+    # paged_rollout_benchmark.py:886-887); reference counting still frees
+    gc.collect()
+    gc.disable()
     if args.workload == "rollout":
         line = run_rollout(args, world, rank, device)
         if not args.no_config5 and (args.qubits, args.gates) != (24, 2000):

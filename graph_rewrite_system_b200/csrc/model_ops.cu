@@ -449,11 +449,19 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) graph_aggregate_vec_kernel(
 #pragma unroll
   for (int j = 0; j < VPL; ++j) acc[j] = 0.f;
   int deg = 0;
+  // the slot's four in- and four out-ports in one 16-byte load per array
+  const int4 inn = __ldg(reinterpret_cast<const int4*>(in_node) + prow);
+  const int4 inp = __ldg(reinterpret_cast<const int4*>(in_port) + prow);
+  const int4 outn = __ldg(reinterpret_cast<const int4*>(out_node) + prow);
+  const int4 outp = __ldg(reinterpret_cast<const int4*>(out_port) + prow);
+  const int in_n[4] = {inn.x, inn.y, inn.z, inn.w}, in_p[4] = {inp.x, inp.y, inp.z, inp.w};
+  const int out_n[4] = {outn.x, outn.y, outn.z, outn.w};
+  const int out_p[4] = {outp.x, outp.y, outp.z, outp.w};
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const int src = in_node[prow * 4 + p];
+    const int src = in_n[p];
     if (src >= 0) {
-      const int r = in_port[prow * 4 + p] * 4 + p;
+      const int r = in_p[p] * 4 + p;
       float f[VPL], e[VPL];
       load_vec<VPL>(fb + (beam_base + src) * fb_stride + c0, f);
       load_vec<VPL>(rel + (int64_t)r * width + c0, e);
@@ -461,9 +469,9 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) graph_aggregate_vec_kernel(
       for (int j = 0; j < VPL; ++j) acc[j] += f[j] + e[j];
       ++deg;
     }
-    const int dst = out_node[prow * 4 + p];
+    const int dst = out_n[p];
     if (dst >= 0) {
-      const int r = 16 + p * 4 + out_port[prow * 4 + p];
+      const int r = 16 + p * 4 + out_p[p];
       float f[VPL], e[VPL];
       load_vec<VPL>(fb + (beam_base + dst) * fb_stride + width + c0, f);
       load_vec<VPL>(rel + (int64_t)r * width + c0, e);
@@ -867,7 +875,10 @@ extern "C" int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride,
                    reinterpret_cast<uintptr_t>(fb) % vbytes == 0 &&
                    (fb_stride * esize) % vbytes == 0 && (width * esize) % vbytes == 0 &&
                    reinterpret_cast<uintptr_t>(agg) % vbytes == 0 &&
-                   (agg_stride * esize) % vbytes == 0 && reinterpret_cast<uintptr_t>(rel) % 16 == 0;
+                   (agg_stride * esize) % vbytes == 0 && reinterpret_cast<uintptr_t>(rel) % 16 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(in_node) | reinterpret_cast<uintptr_t>(in_port) |
+                     reinterpret_cast<uintptr_t>(out_node) | reinterpret_cast<uintptr_t>(out_port)) &
+                    15) == 0;
   if (vec) {
     GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
         graph_aggregate_vec_kernel<T, V><<<grid, ROW_WARPS * 32, 0,
