@@ -151,6 +151,23 @@ __device__ __forceinline__ void stage_row_chunks(uint8_t* stage, int lane, int c
   }
 }
 
+// v[0..31] += chunk c (32 columns) of row `lane` of a warp's staging block
+// (the residual, landed there by a TMA load in the output's swizzled layout)
+__device__ __forceinline__ void add_staged32(float v[32], const uint8_t* stage, int lane, int c) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int chunk = c * 4 + j;
+    const uint4 w = *reinterpret_cast<const uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      v[8 * j + 2 * k] += f.x;
+      v[8 * j + 2 * k + 1] += f.y;
+    }
+  }
+}
+
 // 64 consecutive bf16 of a row (128 bytes, 16-byte aligned) into registers,
 // or zeros when the row is past the end
 __device__ __forceinline__ void load_row64(const __nv_bfloat16* src, bool in, uint4 r[8]) {
@@ -203,11 +220,14 @@ __device__ __forceinline__ void pack_bf16x32(const float v[32], uint32_t packed[
 template <int BN, int MODE>
 __global__ void __launch_bounds__(GtShape<BN>::kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-               const __grid_constant__ CUtensorMap tm_out, int M, int N, int K, GemmEpilogue e) {
+               const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_res,
+               int M, int N, int K, GemmEpilogue e) {
   using namespace sm100;
   using S = GtShape<BN>;
   extern __shared__ uint8_t gt_smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[S::kStages], empty_bar[S::kStages];
+  // per epilogue warp: its residual block landed in its staging block
+  __shared__ __align__(8) uint64_t res_bar[S::kEpiWarps];
   __shared__ __align__(8) uint64_t tmem_full[GT_ACC], tmem_empty[GT_ACC];
   __shared__ __align__(8) uint64_t drain_bar;   // completes when every issued MMA is done
   __shared__ uint32_t tmem_slot;
@@ -229,6 +249,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       mbar_init(&tmem_empty[b], S::kEpiWarps);
     }
     mbar_init(&drain_bar, 1);
+    for (int w = 0; w < S::kEpiWarps; ++w) mbar_init(&res_bar[w], 1);
     failed = 0;
     drain_failed = 0;
     mbar_init_fence();
@@ -299,6 +320,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
     // TMEM -> registers -> bias, residual, GELU, mask -> bf16 -> smem -> TMA store
     const int quarter = warp & 3, cgroup = (warp - 2) >> 2;   // 64 columns per warp
     uint8_t* stage = smem + S::kStages * S::kStage + (warp - 2) * GT_OUT_BYTES;
+    uint64_t* rbar = &res_bar[warp - 2];
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int m0 = (t / n_tiles) * GT_BM, n0 = (t % n_tiles) * BN;
@@ -306,20 +328,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       const int row = m0 + quarter * 32 + lane;
       const bool in = row < M;
       const bool zero = in && e.zero_row != nullptr && e.zero_row[row] == 0;
-      if (!mbar_wait_warp(&tmem_full[b], u & 1)) {
+      // the warp's residual block goes into its staging block (once the
+      // previous output block has left it) while the MMAs run; rows past
+      // the end read as zeros
+      if (lane == 0) {
+        tma_store_wait_read();
+        if (e.residual) {
+          mbar_arrive_expect_tx(rbar, GT_OUT_BYTES);
+          tma_load_2d(stage, &tm_res, n0 + cgroup * 64, m0 + quarter * 32, rbar);
+        }
+      }
+      __syncwarp();
+      if (!mbar_wait_warp(&tmem_full[b], u & 1) ||
+          (e.residual && !mbar_wait_warp(rbar, i & 1))) {
         failed = 1;
+        // a residual load still in flight lands before the warp leaves
+        if (lane == 0 && e.residual) mbar_wait(rbar, i & 1);
         break;
       }
       tc_fence_after();
-      if (lane == 0) tma_store_wait_read();   // this warp's previous block has left smem
-      __syncwarp();
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         const int col = cgroup * 64 + c * 32;
         float v[32];
         tmem_load32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN + col), v);
         if (e.bias) add_bias32(v, e.bias + n0 + col);
-        if (e.residual && in) add_row32(v, e.residual + (int64_t)row * e.ldr + n0 + col);
+        if (e.residual) add_staged32(v, stage, lane, c);
         if (e.gelu) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -355,7 +389,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
     __shared__ float ln_part[4][4][32], ln_m2[4][4][32];
     const int quarter = warp & 3, cgroup = (warp - 2) >> 2;
     uint8_t* stage = smem + S::kStages * S::kStage + (warp - 2) * GT_OUT_BYTES;
-    int i = 0;
+    uint64_t* rbar = &res_bar[warp - 2];
+    int i = 0, res_issued = 0, res_landed = 0;   // residual loads of this warp
     bool gave_up = false;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int m0 = t * GT_BM;                                 // N == BN: one tile per row block
@@ -364,10 +399,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
       // other warps of its quarter are not left waiting
       const int row = m0 + quarter * 32 + lane;
       const bool in = row < M;
-      // the row's residual, scale and masks are read before the wait (their
-      // latency hides behind the tile's MMAs)
-      uint4 res[8];
-      load_row64(e.residual + (int64_t)row * e.ldr + cgroup * 64, in, res);
+      // the warp's residual block goes into its staging block (once the
+      // previous output block has left it) and the row's scale and masks are
+      // read before the wait: their latency hides behind the tile's MMAs
+      const bool res_here = e.residual && !gave_up;
+      if (lane == 0) {
+        tma_store_wait_read();
+        if (res_here) {
+          mbar_arrive_expect_tx(rbar, GT_OUT_BYTES);
+          tma_load_2d(stage, &tm_res, cgroup * 64, m0 + quarter * 32, rbar);
+        }
+      }
+      res_issued += res_here ? 1 : 0;
+      __syncwarp();
       const int64_t beam = in ? row / e.rows_per_beam : 0;
       const float sc = (in && e.row_scale) ? e.row_scale[row] : 1.f;
       bool zc = true, wc = true;
@@ -377,13 +421,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
         if (e.where_beam) wc = wc && e.where_beam[beam] != 0;
         if (e.where_len) wc = wc && e.where_len[beam] > 0;
       }
+      if (res_here) {
+        if (mbar_wait_warp(rbar, (res_issued - 1) & 1)) {
+          ++res_landed;
+        } else {
+          gave_up = true;
+          failed = 1;
+        }
+      }
       if (!gave_up && !mbar_wait_warp(&tmem_full[b], u & 1)) {
         gave_up = true;
         failed = 1;
       }
       tc_fence_after();
-      if (lane == 0) tma_store_wait_read();
-      __syncwarp();
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN);
       // v = residual + row_scale * (acc + bias) for one 32-column chunk
       const auto load_row = [&](int c, float v[32]) {
@@ -394,7 +444,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] *= sc;
         }
-        add_regs32(v, res + 4 * c);
+        if (e.residual) add_staged32(v, stage, lane, c);
       };
       // this thread's 64 columns: exact mean and centred sum of squares of
       // each 32-column chunk, merged (Chan, Golub & LeVeque's pairwise update)
@@ -455,7 +505,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
         } else if (!wc) {             // the row keeps its input
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = 0.f;
-          add_regs32(r, res + 4 * c);
+          if (e.residual) add_staged32(r, stage, lane, c);
         } else {
           const float4* g4 = reinterpret_cast<const float4*>(e.gamma + col);
           const float4* b4 = reinterpret_cast<const float4*>(e.beta + col);
@@ -480,6 +530,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
         tma_store_2d(&tm_out, stage, cgroup * 64, m0 + quarter * 32);
       }
     }
+    // a residual load that was not seen to land lands before the warp leaves
+    if (lane == 0 && res_issued > res_landed) mbar_wait(rbar, (res_issued - 1) & 1);
     if (lane == 0) tma_store_wait_all();
   } else {
     // LOGITS (BN == 32): one thread per row reads its 32 accumulator columns;
@@ -616,13 +668,19 @@ int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, int M, i
   if (!aligned16(a) || !aligned16(b) || !aligned16(e.bias)) return GRS_ERR_SHAPE;
   if (MODE != GT_EPI_LOGITS && (ldo % 8 || ldo < N || !aligned16(out))) return GRS_ERR_SHAPE;
   if (e.residual && (e.ldr % 8 || e.ldr < N || !aligned16(e.residual))) return GRS_ERR_SHAPE;
-  CUtensorMap tm_a, tm_b, tm_out;
+  CUtensorMap tm_a, tm_b, tm_out, tm_res;
   if (!gemm_map(&tm_a, a, M, K, lda, GT_BM) || !gemm_map(&tm_b, b, N, K, ldb, BN))
     return GRS_ERR_SHAPE;
   if (MODE != GT_EPI_LOGITS) {
     if (!gemm_map(&tm_out, out, M, N, ldo, 32)) return GRS_ERR_SHAPE;
   } else {
     std::memset(&tm_out, 0, sizeof(tm_out));
+  }
+  // the residual is loaded in the output's 32-row x 64-column blocks
+  if (MODE != GT_EPI_LOGITS && e.residual) {
+    if (!gemm_map(&tm_res, e.residual, M, N, e.ldr, 32)) return GRS_ERR_SHAPE;
+  } else {
+    std::memset(&tm_res, 0, sizeof(tm_res));
   }
   static bool attr[64] = {};
   static int sms[64] = {};
@@ -636,8 +694,8 @@ int launch_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, int M, i
   if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int64_t tiles = (int64_t)((M + GT_BM - 1) / GT_BM) * (N / BN);
   const int grid = (int)std::min<int64_t>(tiles, dev < 64 && sms[dev] ? sms[dev] : 148);
-  gemm_tc_kernel<BN, MODE><<<grid, S::kThreads, S::kSmem, counted(stream)>>>(tm_a, tm_b, tm_out,
-                                                                           M, N, K, e);
+  gemm_tc_kernel<BN, MODE><<<grid, S::kThreads, S::kSmem, counted(stream)>>>(
+      tm_a, tm_b, tm_out, tm_res, M, N, K, e);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
@@ -750,24 +808,28 @@ extern "C" int grs_match_logits_bf16(const void* x, int64_t ldx, const void* w, 
 // with A = [x | agg] bf16 [M, 512], U0 [512, 512], U2 [256, 512] K-major.
 // The [M, 512] GELU activation never leaves the SM: per 128-row tile the
 // first GEMM runs as two 256-column halves into the two halves of TMEM, the
-// epilogue warps drain each half (bias, GELU, bf16) into a 128 KB
+// epilogue warps drain each half (bias, GELU, bf16) into a 64 KB
 // shared-memory tile written in the 128-byte-swizzled K-major layout a TMA
-// load would produce, and that tile is the A operand of the second GEMM,
-// whose epilogue adds b2 and the residual, normalises the 256-column row,
-// zeroes dead rows and writes the result with TMA stores (staged in the
-// first half of the hidden tile, free by then).  TMEM halves alternate roles
+// load would produce, and that tile is the A operand of the second GEMM:
+// its first K half is consumed before the epilogue writes the second half
+// into the same 64 KB, so the operand ring keeps three stages in flight.
+// The second GEMM's epilogue adds b2 and the residual, normalises the
+// 256-column row, zeroes dead rows and writes the result with TMA stores
+// (staged in the hidden tile, free by then).  TMEM halves alternate roles
 // from tile to tile so the next tile's first GEMM overlaps this tile's
 // LayerNorm.
 // ---------------------------------------------------------------------------
 namespace grs {
 
-constexpr int GM_STAGES = 2;
+constexpr int GM_STAGES = 3;
 constexpr int GM_B_BYTES = 256 * GT_BK * 2;                  // 32 KB: 256 weight rows x 64
 constexpr int GM_STAGE = GT_A_BYTES + GM_B_BYTES;            // 48 KB
-constexpr int GM_H_BYTES = 8 * GT_A_BYTES;                   // 128 KB: 128 x 512 bf16
+constexpr int GM_H_BYTES = 4 * GT_A_BYTES;                   // 64 KB: 128 x 256 bf16, one K half
+constexpr int GM_LN_BYTES = 2 * 4 * 4 * 32 * 4;              // LayerNorm partials: 4 KB
 constexpr int GM_EPI_WARPS = 16, GM_THREADS = (2 + GM_EPI_WARPS) * 32;
 constexpr int GM_CTRL = 1024;                                // barriers, flags
-constexpr int GM_SMEM = GM_CTRL + GM_STAGES * GM_STAGE + GM_H_BYTES + 1024;   // + alignment slack
+constexpr int GM_SMEM =
+    GM_CTRL + GM_STAGES * GM_STAGE + GM_H_BYTES + GM_LN_BYTES + 1024;   // + alignment slack
 
 struct GraphMlpArgs {
   const float* b0;                  // [512]
@@ -800,7 +862,8 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   uint64_t* p1a_full = empty_bar + GM_STAGES;   // first half of GEMM 1 done
   uint64_t* p1b_full = p1a_full + 1;            // second half of GEMM 1 done
   uint64_t* p2_full = p1b_full + 1;             // GEMM 2 done
-  uint64_t* h0_done = p2_full + 1;              // first hidden half written (16 warps)
+  uint64_t* g2a_done = p2_full + 1;             // GEMM 2's first K half done (hidden free)
+  uint64_t* h0_done = g2a_done + 1;             // first hidden half written (16 warps)
   uint64_t* h1_done = h0_done + 1;              // second hidden half written (16 warps)
   uint64_t* out_done = h1_done + 1;             // GEMM 2 accumulator drained (16 warps)
   uint64_t* drain_bar = out_done + 1;
@@ -808,9 +871,9 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   int* failed = reinterpret_cast<int*>(tmem_slot + 1);
   int* drain_failed = failed + 1;
   uint8_t* ring = base + GM_CTRL;
-  uint8_t* hid = ring + GM_STAGES * GM_STAGE;                           // 8 slices of 16 KB
-  float* ln_part = reinterpret_cast<float*>(hid + 4 * GT_A_BYTES);     // [4][4][32], slice 4
-  float* ln_m2 = ln_part + 4 * 4 * 32;                                  // during the LayerNorm
+  uint8_t* hid = ring + GM_STAGES * GM_STAGE;                           // 4 slices of 16 KB
+  float* ln_part = reinterpret_cast<float*>(hid + GM_H_BYTES);          // [4][4][32]
+  float* ln_m2 = ln_part + 4 * 4 * 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = (M + GT_BM - 1) / GT_BM;
   constexpr int KI = 512 / GT_BK;                                       // 8 K slices
@@ -823,6 +886,7 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     mbar_init(p1a_full, 1);
     mbar_init(p1b_full, 1);
     mbar_init(p2_full, 1);
+    mbar_init(g2a_done, 1);
     mbar_init(h0_done, GM_EPI_WARPS);
     mbar_init(h1_done, GM_EPI_WARPS);
     mbar_init(out_done, GM_EPI_WARPS);
@@ -877,11 +941,21 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
           // the accumulator (and for GEMM 2 the hidden tile) must be free
           if (phase == 0 && i > 0) ok = mbar_wait(h1_done, (i - 1) & 1);
           if (phase == 1 && i > 0) ok = mbar_wait(out_done, (i - 1) & 1);
-          if (phase == 2) ok = mbar_wait(h0_done, i & 1) && mbar_wait(h1_done, i & 1);
+          if (phase == 2) ok = mbar_wait(h0_done, i & 1);
           if (!ok) break;
           tc_fence_after();
           const uint32_t acc = phase == 1 ? y_reg : x_reg;
           for (int k = 0; k < KI; ++k, ++g) {
+            if (phase == 2 && k == KI / 2) {
+              // the first hidden half is consumed: the epilogue may write
+              // the second half over it once these MMAs are done
+              mma_commit(g2a_done);
+              if (!mbar_wait(h1_done, i & 1)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
             const int s = g % GM_STAGES, r = g / GM_STAGES;
             if (!mbar_wait(&full_bar[s], r & 1)) {
               ok = false;
@@ -889,7 +963,8 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
             }
             tc_fence_after();
             const uint8_t* st = ring + s * GM_STAGE;
-            const uint64_t ad = smem_desc_k128(phase < 2 ? st : hid + k * GT_A_BYTES);
+            const uint64_t ad =
+                smem_desc_k128(phase < 2 ? st : hid + (k % (KI / 2)) * GT_A_BYTES);
             const uint64_t bd = smem_desc_k128(st + GT_A_BYTES);
 #pragma unroll
             for (int kk = 0; kk < GT_BK / 16; ++kk)
@@ -924,9 +999,14 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
           ok = false;
           *failed = 1;
         }
+        // the second half overwrites the first once GEMM 2 has consumed it
+        if (half == 1 && ok && !mbar_wait_warp(g2a_done, i & 1)) {
+          ok = false;
+          *failed = 1;
+        }
         tc_fence_after();
         const uint32_t src = (half == 0 ? x_reg : y_reg) + (uint32_t)(cgroup * 64);
-        uint8_t* dst = hid + (half * 4 + cgroup) * GT_A_BYTES + quarter * 32 * 128;
+        uint8_t* dst = hid + cgroup * GT_A_BYTES + quarter * 32 * 128;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           float v[32];
@@ -1028,8 +1108,8 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       fence_async_shared();
       __syncwarp();
       if (lane == 0) tma_store_2d(&tm_out, stage, cgroup * 64, m0 + quarter * 32);
-      // every warp is past its statistics before the next tile's second
-      // hidden half (which holds them) is written
+      // every warp is past its statistics before the next tile writes the
+      // LayerNorm partials again
       epilogue_sync();
     }
     if (lane == 0) tma_store_wait_all();
