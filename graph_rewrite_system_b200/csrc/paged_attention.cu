@@ -279,7 +279,118 @@ __device__ __forceinline__ void readout_stage(const ReadoutArgs& a, int b, int t
   }
 }
 
-// Histories of at most 64 tokens: one staged tile serves every task.
+// The query fragments of one task (16 queries of head h from q0): rows
+// past Q read as zeros
+__device__ __forceinline__ void readout_load_q(const ReadoutArgs& a, int b, int h, int q0, int g,
+                                               int tig, uint32_t qa[2][4]) {
+  const __nv_bfloat16* qb = a.q + (int64_t)b * a.q_sb + (int64_t)h * a.q_sh;
+  const int r0 = q0 + g, r1 = q0 + g + 8;
+#pragma unroll
+  for (int kq = 0; kq < 2; ++kq) {
+    const int c = kq * 16 + tig * 2;
+    qa[kq][0] = r0 < a.Q ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)r0 * a.q_sq + c) : 0u;
+    qa[kq][1] = r1 < a.Q ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)r1 * a.q_sq + c) : 0u;
+    qa[kq][2] = r0 < a.Q ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)r0 * a.q_sq + c + 8) : 0u;
+    qa[kq][3] = r1 < a.Q ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)r1 * a.q_sq + c + 8) : 0u;
+  }
+}
+
+__device__ __forceinline__ void ro_ldsm_x4(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((unsigned)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ro_ldsm_x4_trans(uint32_t r[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"((unsigned)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ float ro_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// readout_tile for one staged tile with the query fragments already loaded:
+// K fragments by ldmatrix (rows of 80 bytes: conflict-free), V fragments by
+// ldmatrix.trans, key blocks past `valid` skipped, exponentials on the
+// hardware ex2 (the probabilities are rounded to bf16 for the value product)
+__device__ __forceinline__ void readout_tile_q(const ReadoutArgs& a, int h, const uint32_t qa[2][4],
+                                               const __nv_bfloat16* ks, const __nv_bfloat16* vs,
+                                               int valid, float o[4][4], float lrow[2], int lane) {
+  const int g = lane >> 2, tig = lane & 3, mi = lane >> 3, ri = lane & 7;
+  const __nv_bfloat16* kh = ks + (size_t)h * RO_TILE * RO_PAD;
+  const __nv_bfloat16* vh = vs + (size_t)h * RO_TILE * RO_PAD;
+  const int nblocks = (valid + 7) / 8;            // 8-key blocks holding valid keys
+  float s[8][4];
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb) {
+    s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = -INFINITY;
+    if (nb < nblocks) {
+      // keys nb*8 .. +7; matrices: dims 0-7, 8-15, 16-23, 24-31
+      uint32_t kf[4];
+      ro_ldsm_x4(kf, kh + (size_t)(nb * 8 + ri) * RO_PAD + mi * 8);
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t b0[2] = {kf[0], kf[1]}, b1[2] = {kf[2], kf[3]};
+      mma_bf16_16816(c, qa[0], b0);
+      mma_bf16_16816(c, qa[1], b1);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool ok = nb * 8 + tig * 2 + e < valid;
+        s[nb][e] = ok ? c[e] * a.scale_log2 : -INFINITY;
+        s[nb][2 + e] = ok ? c[2 + e] * a.scale_log2 : -INFINITY;
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[nb][0], s[nb][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[nb][2], s[nb][3]));
+    }
+  }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  const float e0 = mx0 == -INFINITY ? 0.f : mx0, e1 = mx1 == -INFINITY ? 0.f : mx1;
+  float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      s[nb][e] = ro_exp2(s[nb][e] - e0);
+      s[nb][2 + e] = ro_exp2(s[nb][2 + e] - e1);
+      sum0 += s[nb][e];
+      sum1 += s[nb][2 + e];
+    }
+  }
+  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+  lrow[0] = sum0;
+  lrow[1] = sum1;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    if (2 * kk < nblocks) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        // matrices: keys kk*16 + 0-7 / 8-15, dims (2 np) * 8 and (2 np + 1) * 8
+        uint32_t vf[4];
+        ro_ldsm_x4_trans(vf, vh + (size_t)(kk * 16 + (mi & 1) * 8 + ri) * RO_PAD +
+                                 (2 * np + (mi >> 1)) * 8);
+        const uint32_t b0[2] = {vf[0], vf[1]}, b1[2] = {vf[2], vf[3]};
+        mma_bf16_16816(o[2 * np], pa, b0);
+        mma_bf16_16816(o[2 * np + 1], pa, b1);
+      }
+    }
+  }
+}
+
+// Histories of at most 64 tokens: one staged tile serves every task; each
+// warp loads its next task's queries while it computes the current one.
 __global__ void __launch_bounds__(RO_WARPS * 32) readout_single_tile_kernel(ReadoutArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);
@@ -293,11 +404,21 @@ __global__ void __launch_bounds__(RO_WARPS * 32) readout_single_tile_kernel(Read
     readout_stage(a, b, 0, length, ks, vs);
     __syncthreads();
   }
+  uint32_t qn[2][4] = {};
+  if (warp < tasks && length > 0) readout_load_q(a, b, warp % a.H, (warp / a.H) * 16, g, tig, qn);
   for (int task = warp; task < tasks; task += RO_WARPS) {
     const int h = task % a.H, q0 = (task / a.H) * 16;
+    uint32_t qa[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) qa[i][j] = qn[i][j];
+    const int next = task + RO_WARPS;
+    if (next < tasks && length > 0)
+      readout_load_q(a, b, next % a.H, (next / a.H) * 16, g, tig, qn);
     float o[4][4] = {};
-    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-    if (length > 0) readout_tile(a, b, h, q0, ks, vs, length, o, mrow, lrow, g, tig);
+    float lrow[2] = {0.f, 0.f};
+    if (length > 0) readout_tile_q(a, h, qa, ks, vs, length, o, lrow, lane);
     readout_store(a, b, h, q0, o, lrow, g, tig);
   }
 }
