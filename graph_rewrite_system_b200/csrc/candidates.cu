@@ -66,14 +66,25 @@ __global__ void __launch_bounds__(SEL_THREADS) select_candidates_kernel(SelectAr
   uint32_t prefix = 0, mask = 0;
   int remaining = a.k;
   bool take_all = false;
+  if (tid == 0) s_count = 0;
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
     for (int i = tid; i < 256; i += SEL_THREADS) hist[i] = 0;
     __syncthreads();
     for (int idx = tid; idx < n; idx += SEL_THREADS) {
       uint32_t key;
-      if (item_key(a, row, idx, &key) && (key & mask) == prefix)
+      if (item_key(a, row, idx, &key) && (key & mask) == prefix) {
         atomicAdd(&hist[(key >> shift) & 255], 1);
+        // the first pass also keeps every item it sees: when they are no
+        // more than k (the usual case), that is the whole selection and no
+        // collect pass is needed (the sort below orders them)
+        if (pass == 0) {
+          const int slot = atomicAdd(&s_count, 1);
+          if (slot < SEL_MAX_K)
+            sel[slot] = ((unsigned long long)key << 32) |
+                        (unsigned long long)(0xffffffffu - (uint32_t)idx);
+        }
+      }
     }
     __syncthreads();
     if (tid == 0) {
@@ -93,10 +104,12 @@ __global__ void __launch_bounds__(SEL_THREADS) select_candidates_kernel(SelectAr
     __syncthreads();
   }
   // Collect: keys above the threshold key, plus the first `remaining` keys
-  // equal to it in index order (block scan over the index-ordered chunks).
-  if (tid == 0) { s_count = 0; s_eq_base = 0; }
+  // equal to it in index order (block scan over the index-ordered chunks);
+  // when every item is taken the first pass already collected them
   __syncthreads();
-  for (int base = 0; base < n; base += SEL_THREADS) {
+  if (!take_all && tid == 0) { s_count = 0; s_eq_base = 0; }
+  __syncthreads();
+  for (int base = 0; !take_all && base < n; base += SEL_THREADS) {
     const int idx = base + tid;
     uint32_t key = 0;
     const bool valid = idx < n && item_key(a, row, idx, &key);

@@ -439,51 +439,60 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) graph_aggregate_vec_kernel(
     const T* fb, int64_t fb_stride, const float* rel, const int32_t* in_node,
     const int32_t* in_port, const int32_t* out_node, const int32_t* out_port, int64_t rows,
     int slots, int port_slots, int width, T* agg, int64_t agg_stride) {
+  // grid-stride over rows, one warp per row: the next row's port arrays are
+  // requested before this row's neighbour rows, so the index round trip of a
+  // row overlaps the previous row's gathers
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int64_t beam_base = (row / slots) * slots;
-  const int64_t prow = (row / slots) * port_slots + row % slots;
+  const int64_t stride = (int64_t)gridDim.x * ROW_WARPS;
+  int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   const int c0 = lane * VPL;
-  float acc[VPL];
+  const auto ports = [&](int64_t r, int4& inn, int4& inp, int4& outn, int4& outp) {
+    const int64_t prow = (r / slots) * port_slots + r % slots;
+    inn = __ldg(reinterpret_cast<const int4*>(in_node) + prow);
+    inp = __ldg(reinterpret_cast<const int4*>(in_port) + prow);
+    outn = __ldg(reinterpret_cast<const int4*>(out_node) + prow);
+    outp = __ldg(reinterpret_cast<const int4*>(out_port) + prow);
+  };
+  int4 inn, inp, outn, outp;
+  if (row < rows) ports(row, inn, inp, outn, outp);
+  for (; row < rows; row += stride) {
+    const int in_n[4] = {inn.x, inn.y, inn.z, inn.w}, in_p[4] = {inp.x, inp.y, inp.z, inp.w};
+    const int out_n[4] = {outn.x, outn.y, outn.z, outn.w};
+    const int out_p[4] = {outp.x, outp.y, outp.z, outp.w};
+    if (row + stride < rows) ports(row + stride, inn, inp, outn, outp);
+    const int64_t beam_base = (row / slots) * slots;
+    float acc[VPL];
 #pragma unroll
-  for (int j = 0; j < VPL; ++j) acc[j] = 0.f;
-  int deg = 0;
-  // the slot's four in- and four out-ports in one 16-byte load per array
-  const int4 inn = __ldg(reinterpret_cast<const int4*>(in_node) + prow);
-  const int4 inp = __ldg(reinterpret_cast<const int4*>(in_port) + prow);
-  const int4 outn = __ldg(reinterpret_cast<const int4*>(out_node) + prow);
-  const int4 outp = __ldg(reinterpret_cast<const int4*>(out_port) + prow);
-  const int in_n[4] = {inn.x, inn.y, inn.z, inn.w}, in_p[4] = {inp.x, inp.y, inp.z, inp.w};
-  const int out_n[4] = {outn.x, outn.y, outn.z, outn.w};
-  const int out_p[4] = {outp.x, outp.y, outp.z, outp.w};
+    for (int j = 0; j < VPL; ++j) acc[j] = 0.f;
+    int deg = 0;
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const int src = in_n[p];
-    if (src >= 0) {
-      const int r = in_p[p] * 4 + p;
-      float f[VPL], e[VPL];
-      load_vec<VPL>(fb + (beam_base + src) * fb_stride + c0, f);
-      load_vec<VPL>(rel + (int64_t)r * width + c0, e);
+    for (int p = 0; p < 4; ++p) {
+      const int src = in_n[p];
+      if (src >= 0) {
+        const int r = in_p[p] * 4 + p;
+        float f[VPL], e[VPL];
+        load_vec<VPL>(fb + (beam_base + src) * fb_stride + c0, f);
+        load_vec<VPL>(rel + (int64_t)r * width + c0, e);
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) acc[j] += f[j] + e[j];
-      ++deg;
+        for (int j = 0; j < VPL; ++j) acc[j] += f[j] + e[j];
+        ++deg;
+      }
+      const int dst = out_n[p];
+      if (dst >= 0) {
+        const int r = 16 + p * 4 + out_p[p];
+        float f[VPL], e[VPL];
+        load_vec<VPL>(fb + (beam_base + dst) * fb_stride + width + c0, f);
+        load_vec<VPL>(rel + (int64_t)r * width + c0, e);
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) acc[j] += f[j] + e[j];
+        ++deg;
+      }
     }
-    const int dst = out_n[p];
-    if (dst >= 0) {
-      const int r = 16 + p * 4 + out_p[p];
-      float f[VPL], e[VPL];
-      load_vec<VPL>(fb + (beam_base + dst) * fb_stride + width + c0, f);
-      load_vec<VPL>(rel + (int64_t)r * width + c0, e);
+    const float inv = 1.f / (float)(deg > 0 ? deg : 1);
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) acc[j] += f[j] + e[j];
-      ++deg;
-    }
+    for (int j = 0; j < VPL; ++j) acc[j] *= inv;
+    store_vec<VPL>(agg + row * agg_stride + c0, acc);
   }
-  const float inv = 1.f / (float)(deg > 0 ? deg : 1);
-#pragma unroll
-  for (int j = 0; j < VPL; ++j) acc[j] *= inv;
-  store_vec<VPL>(agg + row * agg_stride + c0, acc);
 }
 
 // add_ln_kernel with each lane owning VPL contiguous elements of the row
@@ -880,8 +889,14 @@ extern "C" int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride,
                      reinterpret_cast<uintptr_t>(out_node) | reinterpret_cast<uintptr_t>(out_port)) &
                     15) == 0;
   if (vec) {
+    // one wave of CTAs (four per SM at this kernel's register count); the
+    // rows are a grid-stride loop
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int vgrid = (int)std::min<int64_t>(grid, (int64_t)(sms > 0 ? sms : 148) * 4);
     GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
-        graph_aggregate_vec_kernel<T, V><<<grid, ROW_WARPS * 32, 0,
+        graph_aggregate_vec_kernel<T, V><<<vgrid, ROW_WARPS * 32, 0,
                                            grs::counted((cudaStream_t)stream)>>>(
             (const T*)fb, fb_stride, rel, in_node, in_port, out_node, out_port, rows, slots,
             port_slots, width, (T*)agg, agg_stride)))

@@ -251,13 +251,25 @@ class ShardedBeamSearch(DeviceBeamSearch):
             offset += _round_up(nbytes * cols, 16)
         return fields, pages, cols, _round_up(offset, 16)
 
+    def _staging(self, name: str, nbytes: int) -> torch.Tensor:
+        """A persistent byte buffer of at least `nbytes` (grown by half again
+        when too small): the packed rows change size with the slot count, and
+        a fresh multi-hundred-megabyte allocation per level can stall a level
+        while the allocator maps memory."""
+        buf = getattr(self, name, None)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, int(1.5 * buf.numel()) if buf is not None else 0)
+            buf = torch.empty(size, device=self.device, dtype=torch.uint8)
+            setattr(self, name, buf)
+        return buf[:nbytes]
+
     def _pack_outgoing(self, prop, out_local: torch.Tensor, n_out: torch.Tensor,
                        max_out: int):
         """Before the level's host read: copy the rows of this GPU's leaving
         children (out_local, device count n_out <= max_out) into send rows
         with one grs_rows_copy launch."""
         fields, pages, cols, row_size = self._row_layout()
-        send = torch.empty(max_out, row_size, device=self.device, dtype=torch.uint8)
+        send = self._staging("_send_buf", max_out * row_size).view(max_out, row_size)
         if max_out == 0:
             return send
         ranked_index = out_local[:max_out]
@@ -291,7 +303,7 @@ class ShardedBeamSearch(DeviceBeamSearch):
         recv_counts = [pairs[r][me] if r != me else 0 for r in range(world)]
         n_out, n_in = sum(send_counts), sum(recv_counts)
         self.moved_bytes += n_out * row_size
-        recv = torch.empty(n_in, row_size, device=dev, dtype=torch.uint8)
+        recv = self._staging("_recv_buf", n_in * row_size).view(n_in, row_size)
         if send is None:
             send = torch.empty(0, row_size, device=dev, dtype=torch.uint8)
         if world > 1 and any_moves:                # collective: every rank alike
