@@ -565,12 +565,16 @@ def run_rollout(args, world, rank, device):
     d2h_actions = 0
     e2e_done = 0
     with ClockSampler(device.index):      # the same host conditions as the timed window
+        search.level_actions_host()        # its pinned host buffers exist before the window
         e2e_start.record(stream)
+        e2e_level_ms = []                  # host wall time per level (each ends in a host read)
         for _ in range(done):
+            t_level = time.perf_counter()
             if search.step() is None:
                 break
             d2h_actions += search.level_actions_host()["nbytes"]
             e2e_done += 1
+            e2e_level_ms.append(round((time.perf_counter() - t_level) * 1e3, 3))
         e2e_end.record(stream)
         torch.cuda.synchronize(device)
     e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world, device)
@@ -639,6 +643,7 @@ def run_rollout(args, world, rank, device):
                                    f"value counts B=1000-equivalent levels")
                                   if world > 1 else "single GPU"},
         "e2e": {"value": scale * e2e_done * 1e3 / e2e_ms, "unit": "steps/s",
+                "level_ms": e2e_level_ms,
                 "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": summary_bytes + d2h_actions // max(1, e2e_done),
                 "timed_levels": f"{first}..{first + e2e_done - 1}",
