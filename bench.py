@@ -500,6 +500,14 @@ def rollout_window(steps: int, warmup: int) -> tuple[int, int]:
     return steps, ROLLOUT_DEPTH - steps + 1
 
 
+def warm_searches(search, depth: int, count: int = 2) -> None:
+    """Untimed full searches until the caching allocator holds every block a
+    search needs: the searches after them make no new device allocation."""
+    for _ in range(count):
+        search.run(depth)           # run() starts from reset()
+    torch.cuda.synchronize()
+
+
 def run_rollout(args, world, rank, device):
     from graph_rewrite_system_b200.rollout import StageTimer
 
@@ -508,9 +516,12 @@ def run_rollout(args, world, rank, device):
     search, rc = build_rollout(device, beam_size=args.beam, depth=depth, seed=0, world=world,
                                qubits=args.qubits, gates=args.gates)
     stream = torch.cuda.current_stream(device)
-    # one full untimed search first (module load; the caching allocator and
-    # NCCL meet every buffer size of the timed levels once)
-    search.run(depth)
+    # two full untimed searches first (module load; the caching allocator and
+    # NCCL meet every buffer size of the timed levels).  One is not enough:
+    # the allocator's free blocks after it are split differently, and a search
+    # that follows it still made one new device allocation at level 63, which
+    # took 52 ms while the clock sampler's nvidia-smi was querying the driver
+    warm_searches(search, depth)
     # the timed search: levels 1 .. first-1 untimed (they include the
     # warm-up), levels first .. 64 timed one by one
     search.reset()
@@ -688,7 +699,7 @@ def run_sharded_config5(args, world, rank, device) -> dict:
     search, rc = build_rollout(device, beam_size=1000, depth=depth, seed=0, world=world,
                                qubits=24, gates=2000)
     stream = torch.cuda.current_stream(device)
-    search.run(depth)
+    warm_searches(search, depth)
     search.reset()
     for _ in range(first - 1):
         if search.step() is None:

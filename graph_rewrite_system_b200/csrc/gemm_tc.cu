@@ -813,11 +813,14 @@ extern "C" int grs_match_logits_bf16(const void* x, int64_t ldx, const void* w, 
 // load would produce, and that tile is the A operand of the second GEMM:
 // its first K half is consumed before the epilogue writes the second half
 // into the same 64 KB, so the operand ring keeps three stages in flight.
-// The second GEMM's epilogue adds b2 and the residual, normalises the
-// 256-column row, zeroes dead rows and writes the result with TMA stores
-// (staged in the hidden tile, free by then).  TMEM halves alternate roles
-// from tile to tile so the next tile's first GEMM overlaps this tile's
-// LayerNorm.
+// The residual enters the second GEMM's accumulator on the tensor cores:
+// its 64-column slices ride in the otherwise unused A halves of the second
+// GEMM's first four ring stages and are multiplied by a 16 x 16 identity
+// held in shared memory (exact: bf16 x 1.0, fp32 accumulate), so the
+// epilogue never loads it.  The epilogue adds b2, normalises the 256-column
+// row, zeroes dead rows and writes the result with TMA stores (staged in the
+// hidden tile, free by then).  TMEM halves alternate roles from tile to tile
+// so the next tile's first GEMM overlaps this tile's LayerNorm.
 // ---------------------------------------------------------------------------
 namespace grs {
 
@@ -826,16 +829,18 @@ constexpr int GM_B_BYTES = 256 * GT_BK * 2;                  // 32 KB: 256 weigh
 constexpr int GM_STAGE = GT_A_BYTES + GM_B_BYTES;            // 48 KB
 constexpr int GM_H_BYTES = 4 * GT_A_BYTES;                   // 64 KB: 128 x 256 bf16, one K half
 constexpr int GM_LN_BYTES = 2 * 4 * 4 * 32 * 4;              // LayerNorm partials: 4 KB
+// B operand of the residual MMAs: 16 rows x 64 K bf16 in the 128-byte
+// swizzled K-major layout, row n holding 1.0 at the K columns k with
+// k % 16 == n, so each 16-column K chunk of it is the 16 x 16 identity
+constexpr int GM_ID_BYTES = 16 * 128;
 constexpr int GM_EPI_WARPS = 16, GM_THREADS = (2 + GM_EPI_WARPS) * 32;
 constexpr int GM_CTRL = 1024;                                // barriers, flags
-constexpr int GM_SMEM =
-    GM_CTRL + GM_STAGES * GM_STAGE + GM_H_BYTES + GM_LN_BYTES + 1024;   // + alignment slack
+constexpr int GM_SMEM = GM_CTRL + GM_STAGES * GM_STAGE + GM_H_BYTES + GM_LN_BYTES + GM_ID_BYTES +
+                        1024;                                // + alignment slack
 
 struct GraphMlpArgs {
   const float* b0;                  // [512]
   const float* b2;                  // [256]
-  const __nv_bfloat16* residual;    // x: [M, 256] rows, stride ldr
-  int64_t ldr;
   const float* gamma;
   const float* beta;
   const uint8_t* zero_row;          // live rows (0 = dead: written as zeros), or null
@@ -850,7 +855,7 @@ __device__ __forceinline__ void epilogue_sync() {
 
 __global__ void __launch_bounds__(GM_THREADS, 1)
 graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_u0,
-                 const __grid_constant__ CUtensorMap tm_u2,
+                 const __grid_constant__ CUtensorMap tm_u2, const __grid_constant__ CUtensorMap tm_res,
                  const __grid_constant__ CUtensorMap tm_out, int M, GraphMlpArgs e) {
   using namespace sm100;
   extern __shared__ uint8_t gm_smem_raw[];
@@ -874,9 +879,23 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   uint8_t* hid = ring + GM_STAGES * GM_STAGE;                           // 4 slices of 16 KB
   float* ln_part = reinterpret_cast<float*>(hid + GM_H_BYTES);          // [4][4][32]
   float* ln_m2 = ln_part + 4 * 4 * 32;
+  uint8_t* ident = hid + GM_H_BYTES + GM_LN_BYTES;                      // 1024-aligned
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = (M + GT_BM - 1) / GT_BM;
   constexpr int KI = 512 / GT_BK;                                       // 8 K slices
+
+  if (threadIdx.x < GM_ID_BYTES / 16) {
+    // 16-byte piece p of row n holds the K columns of logical piece p ^ (n % 8)
+    const int n = threadIdx.x >> 3, piece = (threadIdx.x & 7) ^ (n & 7);
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k0 = piece * 8 + 2 * j;
+      w[j] = (((k0 & 15) == n) ? 0x3F80u : 0u) | (((k0 + 1) & 15) == n ? 0x3F800000u : 0u);
+    }
+    *reinterpret_cast<uint4*>(ident + threadIdx.x * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    fence_async_shared();                  // visible to the tensor cores
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < GM_STAGES; ++s) {
@@ -902,7 +921,8 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {  // TMA producer: per tile 8 (A, U0 rows 0-255) + 8 (A, U0 rows 256-511) + 8 U2 slices
+    if (lane == 0) {  // TMA producer: per tile 8 (A, U0 rows 0-255) + 8 (A, U0 rows 256-511) +
+                      // 8 U2 slices, the first four with a 64-column residual slice
       int g = 0;
       int armed[GM_STAGES] = {};
       for (int t = blockIdx.x; t < tiles && !*failed; t += gridDim.x) {
@@ -919,6 +939,10 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
             mbar_arrive_expect_tx(&full_bar[s], GM_STAGE);
             tma_load_2d(st, &tm_a, k * GT_BK, m0, &full_bar[s]);
             tma_load_2d(st + GT_A_BYTES, &tm_u0, k * GT_BK, phase * 256, &full_bar[s]);
+          } else if (k < 4) {
+            mbar_arrive_expect_tx(&full_bar[s], GM_STAGE);
+            tma_load_2d(st, &tm_res, k * GT_BK, m0, &full_bar[s]);
+            tma_load_2d(st + GT_A_BYTES, &tm_u2, k * GT_BK, 0, &full_bar[s]);
           } else {
             mbar_arrive_expect_tx(&full_bar[s], GM_B_BYTES);
             tma_load_2d(st + GT_A_BYTES, &tm_u2, k * GT_BK, 0, &full_bar[s]);
@@ -932,6 +956,8 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
       constexpr uint32_t idesc = idesc_bf16_f32(GT_BM, 256);
+      constexpr uint32_t idesc_res = idesc_bf16_f32(GT_BM, 16);
+      const uint64_t id_desc = smem_desc_k128(ident);
       int g = 0, i = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
@@ -969,6 +995,14 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 #pragma unroll
             for (int kk = 0; kk < GT_BK / 16; ++kk)
               mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, idesc, k > 0 || kk > 0);
+            if (phase == 2 && k < 4) {
+              // residual columns 64k + 16kk.. += residual slice . identity
+              const uint64_t rd = smem_desc_k128(st);
+#pragma unroll
+              for (int kk = 0; kk < GT_BK / 16; ++kk)
+                mma_bf16(acc + (uint32_t)(k * GT_BK + kk * 16), rd + 2 * kk, id_desc + 2 * kk,
+                         idesc_res, true);
+            }
             mma_commit(&empty_bar[s]);
           }
           if (!ok) break;
@@ -1027,11 +1061,9 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
         __syncwarp();
         if (lane == 0) mbar_arrive(half == 0 ? h0_done : h1_done);
       }
-      // ---- GEMM 2 epilogue: + b2 + residual, LayerNorm, dead rows, TMA store.
-      // The row's residual and live flag are read before the wait, so their
-      // latency hides behind the second GEMM; the accumulator is read once.
-      uint4 res[8];
-      load_row64(e.residual + (int64_t)row * e.ldr + cgroup * 64, in, res);
+      // ---- GEMM 2 epilogue (the accumulator holds the residual already):
+      // + b2, LayerNorm, dead rows, TMA store.  The live flag is read before
+      // the wait, so its latency hides behind the second GEMM.
       const bool keep = !in || e.zero_row == nullptr || e.zero_row[row] != 0;
       if (ok && !mbar_wait_warp(p2_full, i & 1)) {
         ok = false;
@@ -1039,12 +1071,11 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       }
       tc_fence_after();
       const uint32_t taddr = x_reg + lane_base + (uint32_t)(cgroup * 64);
-      // v = acc + b2 + residual for one 32-column chunk (the accumulator is
-      // read twice, once for the statistics and once for the output)
+      // v = acc + b2 for one 32-column chunk (the accumulator is read twice,
+      // once for the statistics and once for the output)
       const auto load_row = [&](int c, float v[32]) {
         tmem_load32(taddr + c * 32, v);
         add_bias32(v, e.b2 + cgroup * 64 + c * 32);
-        add_regs32(v, res + 4 * c);
       };
       float mean_t = 0.f, m2_t = 0.f;
 #pragma unroll 1
@@ -1139,9 +1170,10 @@ extern "C" int grs_graph_mlp_bf16(const void* a, int64_t lda, const void* u0, in
       !aligned16(residual) || !aligned16(gamma) || !aligned16(beta) || !aligned16(out) ||
       !b0 || !b2 || !residual || !gamma || !beta)
     return GRS_ERR_SHAPE;
-  CUtensorMap tm_a, tm_u0, tm_u2, tm_out;
+  CUtensorMap tm_a, tm_u0, tm_u2, tm_res, tm_out;
   if (!gemm_map(&tm_a, a, M, 512, lda, GT_BM) || !gemm_map(&tm_u0, u0, 512, 512, ldu0, 256) ||
-      !gemm_map(&tm_u2, u2, 256, 512, ldu2, 256) || !gemm_map(&tm_out, out, M, 256, ldo, 32))
+      !gemm_map(&tm_u2, u2, 256, 512, ldu2, 256) || !gemm_map(&tm_res, residual, M, 256, ldr, GT_BM) ||
+      !gemm_map(&tm_out, out, M, 256, ldo, 32))
     return GRS_ERR_SHAPE;
   static bool attr[64] = {};
   static int sms[64] = {};
@@ -1156,10 +1188,9 @@ extern "C" int grs_graph_mlp_bf16(const void* a, int64_t lda, const void* u0, in
   if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int tiles = (M + GT_BM - 1) / GT_BM;
   const int grid = std::min(tiles, dev < 64 && sms[dev] ? sms[dev] : 148);
-  GraphMlpArgs e{b0, b2, static_cast<const __nv_bfloat16*>(residual), ldr, gamma, beta,
-                 zero_row, eps, status};
+  GraphMlpArgs e{b0, b2, gamma, beta, zero_row, eps, status};
   graph_mlp_kernel<<<grid, GM_THREADS, GM_SMEM, counted((cudaStream_t)stream)>>>(
-      tm_a, tm_u0, tm_u2, tm_out, M, e);
+      tm_a, tm_u0, tm_u2, tm_res, tm_out, M, e);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;
 }
