@@ -867,10 +867,12 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   uint64_t* p1a_full = empty_bar + GM_STAGES;   // first half of GEMM 1 done
   uint64_t* p1b_full = p1a_full + 1;            // second half of GEMM 1 done
   uint64_t* p2_full = p1b_full + 1;             // GEMM 2 done
-  uint64_t* g2a_done = p2_full + 1;             // GEMM 2's first K half done (hidden free)
-  uint64_t* h0_done = g2a_done + 1;             // first hidden half written (16 warps)
-  uint64_t* h1_done = h0_done + 1;              // second hidden half written (16 warps)
-  uint64_t* out_done = h1_done + 1;             // GEMM 2 accumulator drained (16 warps)
+  // per 64-column hidden slice c (written by the 4 epilogue warps of column
+  // group c, read by GEMM 2's K slices c and c + 4):
+  uint64_t* g2a_done = p2_full + 1;             // [4] GEMM 2 K slice c done (slice free)
+  uint64_t* h0_done = g2a_done + 4;             // [4] first-half slice c written
+  uint64_t* h1_done = h0_done + 4;              // [4] second-half slice c written
+  uint64_t* out_done = h1_done + 4;             // GEMM 2 accumulator drained (16 warps)
   uint64_t* drain_bar = out_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   int* failed = reinterpret_cast<int*>(tmem_slot + 1);
@@ -905,9 +907,11 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     mbar_init(p1a_full, 1);
     mbar_init(p1b_full, 1);
     mbar_init(p2_full, 1);
-    mbar_init(g2a_done, 1);
-    mbar_init(h0_done, GM_EPI_WARPS);
-    mbar_init(h1_done, GM_EPI_WARPS);
+    for (int c = 0; c < 4; ++c) {
+      mbar_init(&g2a_done[c], 1);
+      mbar_init(&h0_done[c], GM_EPI_WARPS / 4);
+      mbar_init(&h1_done[c], GM_EPI_WARPS / 4);
+    }
     mbar_init(out_done, GM_EPI_WARPS);
     mbar_init(drain_bar, 1);
     *failed = 0;
@@ -964,19 +968,19 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
         const uint32_t x_reg = tmem + (uint32_t)((i & 1) * 256);        // GEMM 1a and GEMM 2
         const uint32_t y_reg = tmem + (uint32_t)(((i + 1) & 1) * 256);  // GEMM 1b
         for (int phase = 0; phase < 3 && ok; ++phase) {
-          // the accumulator (and for GEMM 2 the hidden tile) must be free
-          if (phase == 0 && i > 0) ok = mbar_wait(h1_done, (i - 1) & 1);
+          // the accumulator must be free: the last tile's second GELU half
+          // drained (all four slices) or its LayerNorm done
+          if (phase == 0 && i > 0)
+            for (int c = 0; c < 4 && ok; ++c) ok = mbar_wait(&h1_done[c], (i - 1) & 1);
           if (phase == 1 && i > 0) ok = mbar_wait(out_done, (i - 1) & 1);
-          if (phase == 2) ok = mbar_wait(h0_done, i & 1);
           if (!ok) break;
           tc_fence_after();
           const uint32_t acc = phase == 1 ? y_reg : x_reg;
           for (int k = 0; k < KI; ++k, ++g) {
-            if (phase == 2 && k == KI / 2) {
-              // the first hidden half is consumed: the epilogue may write
-              // the second half over it once these MMAs are done
-              mma_commit(g2a_done);
-              if (!mbar_wait(h1_done, i & 1)) {
+            if (phase == 2) {
+              // GEMM 2's K slice k reads hidden slice k % 4 of half k / 4,
+              // as soon as its four warps have written it
+              if (!mbar_wait(k < KI / 2 ? &h0_done[k] : &h1_done[k - KI / 2], i & 1)) {
                 ok = false;
                 break;
               }
@@ -1004,6 +1008,9 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
                          idesc_res, true);
             }
             mma_commit(&empty_bar[s]);
+            // the first-half slice is consumed: its warps may write their
+            // second-half slice over it once these MMAs are done
+            if (phase == 2 && k < KI / 2) mma_commit(&g2a_done[k]);
           }
           if (!ok) break;
           mma_commit(phase == 0 ? p1a_full : phase == 1 ? p1b_full : p2_full);
@@ -1034,7 +1041,7 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
           *failed = 1;
         }
         // the second half overwrites the first once GEMM 2 has consumed it
-        if (half == 1 && ok && !mbar_wait_warp(g2a_done, i & 1)) {
+        if (half == 1 && ok && !mbar_wait_warp(&g2a_done[cgroup], i & 1)) {
           ok = false;
           *failed = 1;
         }
@@ -1059,7 +1066,7 @@ graph_mlp_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
         fence_async_shared();                  // hidden tile visible to the tensor cores
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(half == 0 ? h0_done : h1_done);
+        if (lane == 0) mbar_arrive(half == 0 ? &h0_done[cgroup] : &h1_done[cgroup]);
       }
       // ---- GEMM 2 epilogue (the accumulator holds the residual already):
       // + b2, LayerNorm, dead rows, TMA store.  The live flag is read before

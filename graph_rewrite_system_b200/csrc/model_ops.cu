@@ -6,6 +6,7 @@
 // computes in fp32.  Rows are processed one warp per row; each lane owns the
 // row elements lane, lane + 32, ... (coalesced 32-lane accesses).
 #include <algorithm>
+#include <type_traits>
 
 #include "grs_common.cuh"
 
@@ -557,7 +558,27 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) add_ln_vec_kernel(AddLnArgs a)
   store_vec<VPL>(reinterpret_cast<T*>(a.ln_out) + row * a.ln_stride + c0, r);
 }
 
-// elements read and written with vector accesses.
+// R 16-byte pieces of 8 bf16 each into 8 R floats
+template <int R>
+__device__ __forceinline__ void unpack_bf16x8(const uint4 (&r)[R], float* v) {
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[8 * i + 2 * j] = f.x;
+      v[8 * i + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+// _update_live_nodes (paged_model.py:223-238) for every slot row: the
+// bound-key attention of the row's query over the beam's `pattern` bound
+// keys, then the action_delta hidden layer GELU(x + cvec + sum_k p_k vw_k).
+// One CTA per (beam, ULH_ROWS slots) with the beam's keys, vw and cvec staged
+// in shared memory as fp32; one warp per row, each lane owning VPLQ query
+// and VPLH hidden elements, read and written with vector accesses.
 template <typename T, int VPLQ, int VPLH>
 __global__ void __launch_bounds__(ROW_WARPS * 32, 4) update_live_hidden_kernel(
     const T* qxa, int64_t qxa_stride, const T* keys, const T* vw, const T* cvec,
@@ -592,15 +613,38 @@ __global__ void __launch_bounds__(ROW_WARPS * 32, 4) update_live_hidden_kernel(
   const bool q_on = q0 < width, h_on = h0 < hw;
   const float scale = rsqrtf((float)width);
   const int end = min(slots, (blockIdx.x + 1) * ULH_ROWS);
+  // bf16 rows in 16-byte pieces: the next row's query and input pieces are
+  // requested before this row's attention, so each warp has two rows' loads
+  // in flight instead of one
+  constexpr bool kAhead = std::is_same<T, __nv_bfloat16>::value && VPLQ % 8 == 0 && VPLH % 8 == 0;
+  constexpr int RQ = kAhead ? VPLQ / 8 : 1, RH = kAhead ? VPLH / 8 : 1;
+  uint4 rq[RQ], rh[RH];
+  const auto fetch = [&](int slot) {
+    const T* q = qxa + (b * slots + slot) * qxa_stride;
+#pragma unroll
+    for (int i = 0; i < RQ; ++i)
+      rq[i] = q_on ? __ldg(reinterpret_cast<const uint4*>(q + q0) + i) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < RH; ++i)
+      rh[i] = h_on ? __ldg(reinterpret_cast<const uint4*>(q + width + h0) + i)
+                   : make_uint4(0, 0, 0, 0);
+  };
+  if (kAhead && blockIdx.x * ULH_ROWS + warp < end) fetch(blockIdx.x * ULH_ROWS + warp);
   for (int s = blockIdx.x * ULH_ROWS + warp; s < end; s += ROW_WARPS) {
     const int64_t row = b * slots + s;
-    const T* q = qxa + row * qxa_stride;
     float qv[VPLQ], xv[VPLH];
-    if (q_on) load_vec<VPLQ>(q + q0, qv);
-    else
+    if constexpr (kAhead) {
+      unpack_bf16x8<RQ>(rq, qv);
+      unpack_bf16x8<RH>(rh, xv);
+      if (s + ROW_WARPS < end) fetch(s + ROW_WARPS);
+    } else {
+      const T* q = qxa + row * qxa_stride;
+      if (q_on) load_vec<VPLQ>(q + q0, qv);
+      else
 #pragma unroll
-      for (int j = 0; j < VPLQ; ++j) qv[j] = 0.f;
-    if (h_on) load_vec<VPLH>(q + width + h0, xv);
+        for (int j = 0; j < VPLQ; ++j) qv[j] = 0.f;
+      if (h_on) load_vec<VPLH>(q + width + h0, xv);
+    }
     float logit[8];
     float mx = -INFINITY;
 #pragma unroll
