@@ -1,9 +1,9 @@
 // Row-wise fused kernels of the paged action model (reference paged_model.py,
-// model.py).  GEMMs are plain cuBLAS calls made by the host; every other
-// operation of the one-token step, the node readout and the readout graph is
-// one of the kernels below.  Each kernel is templated on the activation type
-// (fp32 for the CPU-equivalence configuration, bf16 for the rollout) and
-// computes in fp32.  Rows are processed one warp per row; each lane owns the
+// model.py).  The projections are the tensor-core GEMMs of gemm_tc.cu (fp32
+// path: cuBLAS); every other operation of the one-token step, the node
+// readout and the readout graph is one of the kernels below.  Each kernel is
+// templated on the activation type (fp32 for the CPU-equivalence
+// configuration, bf16 for the rollout) and computes in fp32.  Rows are processed one warp per row; each lane owns the
 // row elements lane, lane + 32, ... (coalesced 32-lane accesses).
 #include <algorithm>
 #include <type_traits>
@@ -167,6 +167,21 @@ __device__ __forceinline__ void load8(const float* p, float v[8]) {
   const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
+// R 16-byte pieces of 8 bf16 each into 8 R floats
+template <int R>
+__device__ __forceinline__ void unpack_bf16x8(const uint4 (&r)[R], float* v) {
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[8 * i + 2 * j] = f.x;
+      v[8 * i + 2 * j + 1] = f.y;
+    }
+  }
+}
+
 __device__ __forceinline__ void store8(__nv_bfloat16* p, const float v[8]) {
   uint4 x;
   __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&x);
@@ -421,22 +436,14 @@ __device__ __forceinline__ void stage_interleaved(float* dst, const T* src, int 
   }
 }
 
-// _update_live_nodes hidden layer (paged_model.py:223-238), per slot row:
-//   logits_k = q . key[b,k] / sqrt(W) (masked -1e4), attn = softmax_k,
-//   affinity = sigmoid(max_k logits),
-//   h = GELU(xa + sum_k attn_k * vw[b,k] + c[b])
-// with q = states W_query^T, xa = states W1[:, :W]^T (one GEMM, qxa row =
-// [q | xa]), vw[b,k] = (bound W_value^T) W1[:, W:2W]^T, c[b] = ctx W1[:, 2W:]^T + b1.
-// A CTA takes up to 64 slot rows of one beam (grid = row blocks x beams) and
-// stages that beam's keys, vw and c in shared memory (fp32) once; a warp
-// handles a row, each lane a contiguous chunk of VPLQ (q) and VPLH (xa, h)
+constexpr int AGG_CTAS_PER_SM = 4;   // resident CTAs of graph_aggregate_vec_kernel
 
 // graph_aggregate_kernel with each lane owning VPL contiguous elements
 // (width == 32 * VPL): 16-byte row accesses instead of 2-byte ones.  Every
 // element accumulates the same terms in the same order, so results are
 // bit-identical to the strided kernel.
 template <typename T, int VPL>
-__global__ void __launch_bounds__(ROW_WARPS * 32) graph_aggregate_vec_kernel(
+__global__ void __launch_bounds__(ROW_WARPS * 32, AGG_CTAS_PER_SM) graph_aggregate_vec_kernel(
     const T* fb, int64_t fb_stride, const float* rel, const int32_t* in_node,
     const int32_t* in_port, const int32_t* out_node, const int32_t* out_port, int64_t rows,
     int slots, int port_slots, int width, T* agg, int64_t agg_stride) {
@@ -558,27 +565,16 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) add_ln_vec_kernel(AddLnArgs a)
   store_vec<VPL>(reinterpret_cast<T*>(a.ln_out) + row * a.ln_stride + c0, r);
 }
 
-// R 16-byte pieces of 8 bf16 each into 8 R floats
-template <int R>
-__device__ __forceinline__ void unpack_bf16x8(const uint4 (&r)[R], float* v) {
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r[i]);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(h[j]);
-      v[8 * i + 2 * j] = f.x;
-      v[8 * i + 2 * j + 1] = f.y;
-    }
-  }
-}
-
-// _update_live_nodes (paged_model.py:223-238) for every slot row: the
-// bound-key attention of the row's query over the beam's `pattern` bound
-// keys, then the action_delta hidden layer GELU(x + cvec + sum_k p_k vw_k).
-// One CTA per (beam, ULH_ROWS slots) with the beam's keys, vw and cvec staged
-// in shared memory as fp32; one warp per row, each lane owning VPLQ query
-// and VPLH hidden elements, read and written with vector accesses.
+// _update_live_nodes hidden layer (paged_model.py:223-238), per slot row:
+//   logits_k = q . key[b,k] / sqrt(W) (masked -1e4), attn = softmax_k,
+//   affinity = sigmoid(max_k logits),
+//   h = GELU(xa + sum_k attn_k * vw[b,k] + c[b])
+// with q = states W_query^T, xa = states W1[:, :W]^T (one GEMM, qxa row =
+// [q | xa]), vw[b,k] = (bound W_value^T) W1[:, W:2W]^T, c[b] = ctx W1[:, 2W:]^T + b1.
+// A CTA takes up to ULH_ROWS slot rows of one beam (grid = row blocks x
+// beams) and stages that beam's keys, vw and c in shared memory (fp32) once;
+// a warp handles a row, each lane a contiguous chunk of VPLQ (q) and VPLH
+// (xa, h) elements, read and written with vector accesses.
 template <typename T, int VPLQ, int VPLH>
 __global__ void __launch_bounds__(ROW_WARPS * 32, 4) update_live_hidden_kernel(
     const T* qxa, int64_t qxa_stride, const T* keys, const T* vw, const T* cvec,
@@ -933,12 +929,13 @@ extern "C" int grs_graph_aggregate(int dtype, const void* fb, int64_t fb_stride,
                      reinterpret_cast<uintptr_t>(out_node) | reinterpret_cast<uintptr_t>(out_port)) &
                     15) == 0;
   if (vec) {
-    // one wave of CTAs (four per SM at this kernel's register count); the
-    // rows are a grid-stride loop
+    // one wave of CTAs (AGG_CTAS_PER_SM per SM, the kernel's launch bound);
+    // the rows are a grid-stride loop
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int vgrid = (int)std::min<int64_t>(grid, (int64_t)(sms > 0 ? sms : 148) * 4);
+    const int vgrid =
+        (int)std::min<int64_t>(grid, (int64_t)(sms > 0 ? sms : 148) * AGG_CTAS_PER_SM);
     GRS_DTYPE_SWITCH(T, dtype, GRS_VPL_SWITCH(V, width,
         graph_aggregate_vec_kernel<T, V><<<vgrid, ROW_WARPS * 32, 0,
                                            grs::counted((cudaStream_t)stream)>>>(
