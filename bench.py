@@ -538,6 +538,9 @@ def run_rollout(args, world, rank, device):
     moved0 = (getattr(search, "moved_children", 0), getattr(search, "moved_bytes", 0))
     probe = KernelProbe("gemm", gemm_work)
     with ClockSampler(device.index) as clocks, probe:
+        # every rank's sampler is up (their start-up times differ) before
+        # any rank opens the window
+        barrier(world, device)
         # NVTX range "timed_levels": lets a profiler restrict itself to the
         # timed window (ncu --nvtx --nvtx-include "timed_levels/")
         torch.cuda.nvtx.range_push("timed_levels")
@@ -577,6 +580,7 @@ def run_rollout(args, world, rank, device):
     e2e_done = 0
     with ClockSampler(device.index):      # the same host conditions as the timed window
         search.level_actions_host()        # its pinned host buffers exist before the window
+        barrier(world, device)             # all ranks open the window together
         e2e_start.record(stream)
         e2e_level_ms = []                  # host wall time per level (each ends in a host read)
         for _ in range(done):
@@ -710,6 +714,7 @@ def run_sharded_config5(args, world, rank, device) -> dict:
               for _ in range(steps)]
     done = 0
     with ClockSampler(device.index) as clocks:
+        barrier(world, device)             # all ranks open the window together
         for a, b in events:
             a.record(stream)
             row = search.step()
