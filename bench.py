@@ -157,27 +157,40 @@ class KernelProbe:
         setattr(self.module, self.name, self.original)
 
     def roofline(self, peaks: dict, kernel: str, traffic_ratio) -> dict | None:
-        """Tensor-pipe roofline (FLOPs) with the HBM fraction beside it.
-        `traffic_ratio`: DRAM bytes / algorithmic bytes of this kernel from a
-        committed ncu capture (None when absent)."""
+        """Roofline of the sampled launches: their arithmetic intensity
+        (algorithmic FLOPs / algorithmic bytes) against the ridge point of the
+        measured peaks (sustained bf16 FLOP/s / HBM bytes/s) decides the
+        bound, so `frac` is achieved / attainable; the other resource's
+        fraction is reported beside it.  `traffic_ratio`: DRAM bytes /
+        algorithmic bytes of this kernel from a committed ncu capture (None
+        when absent)."""
         if not self.events:
             return None
         torch.cuda.synchronize()
         n = len(self.events)
         ms = sum(s.elapsed_time(e) for s, e in self.events) / n
         flops, nbytes = self.flops / n, self.bytes / n
-        achieved = flops / (ms * 1e-3) / 1e12
-        peak = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
-        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak,
+        tflops = flops / (ms * 1e-3) / 1e12
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        peak_tf = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
+        peak_gbs = peaks["hbm_gbs"]
+        intensity = flops / nbytes
+        ridge = peak_tf * 1e12 / (peak_gbs * 1e9)
+        memory_bound = intensity < ridge
+        achieved, peak, unit = (gbs, peak_gbs, "GB/s") if memory_bound else \
+            (tflops, peak_tf, "TFLOP/s")
+        return {"bound": "hbm" if memory_bound else "tensor", "achieved": achieved,
+                "peak": peak, "unit": unit, "frac": achieved / peak,
                 "traffic": traffic_ratio * nbytes if traffic_ratio else None,
                 "kernel": kernel, "launches": n, "sampled_every": self.every,
                 "avg_launch_ms": ms, "algorithmic_flops_per_launch": flops,
                 "algorithmic_bytes_per_launch": nbytes,
-                "hbm_achieved_gbs": nbytes / (ms * 1e-3) / 1e9,
-                "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside "
-                               f"the long search step); HBM: {peaks['source']} hbm_gbs"}
+                "intensity_flop_per_byte": intensity, "ridge_flop_per_byte": ridge,
+                "tensor_achieved_tflops": tflops, "tensor_frac": tflops / peak_tf,
+                "hbm_achieved_gbs": gbs, "hbm_frac": gbs / peak_gbs,
+                "peak_source": f"{peaks['source']} hbm_gbs; tensor: {peaks['source']} "
+                               f"bf16_tflops_sustained (kernel timed inside the long search "
+                               f"step)"}
 
 
 def gemm_work(x, weight, bias=None, *, gelu=False, residual=None, zero_row=None, out=None,

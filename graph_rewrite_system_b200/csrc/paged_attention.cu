@@ -115,7 +115,8 @@ __global__ void __launch_bounds__(256) paged_attention_rows_kernel(RowsArgs<T, D
 // Tensor-core readout: bf16, head width 32, no current token, no shared prefix.
 // ---------------------------------------------------------------------------
 constexpr int RO_TILE = 64;       // keys per shared-memory tile
-constexpr int RO_PAD = 40;        // bf16 elements per staged (key, head) row
+constexpr int RO_PAD = 40;        // bf16 elements per staged (key, head) row, padded layout
+constexpr int RO_ROW = 32;        // the same row unpadded, 16-byte pieces swizzled
 constexpr int RO_WARPS = 8;
 
 __device__ __forceinline__ void mma_bf16_16816(float c[4], const uint32_t a[4],
@@ -257,6 +258,10 @@ __device__ __forceinline__ void readout_store(const ReadoutArgs& a, int b, int h
 }
 
 // Stage keys/values [t0, t0 + 64) of every head of beam b (16-byte vectors).
+// kSwizzled: 64-byte rows whose 16-byte piece v sits at v ^ ((t >> 1) & 3),
+// so the 8 rows an ldmatrix reads cover all 32 banks without padding;
+// otherwise rows padded to RO_PAD elements.
+template <bool kSwizzled>
 __device__ __forceinline__ void readout_stage(const ReadoutArgs& a, int b, int t0, int length,
                                               __nv_bfloat16* ks, __nv_bfloat16* vs) {
   const int total_vec = RO_TILE * a.H * 4;
@@ -273,7 +278,8 @@ __device__ __forceinline__ void readout_stage(const ReadoutArgs& a, int b, int t
       kv = __ldg(reinterpret_cast<const uint4*>(a.kc + off));
       vv = __ldg(reinterpret_cast<const uint4*>(a.vc + off));
     }
-    const size_t soff = ((size_t)h * RO_TILE + t) * RO_PAD + v * 8;
+    const size_t soff = kSwizzled ? ((size_t)h * RO_TILE + t) * RO_ROW + ((v ^ ((t >> 1) & 3)) * 8)
+                                  : ((size_t)h * RO_TILE + t) * RO_PAD + v * 8;
     *reinterpret_cast<uint4*>(ks + soff) = kv;
     *reinterpret_cast<uint4*>(vs + soff) = vv;
   }
@@ -311,16 +317,18 @@ __device__ __forceinline__ float ro_exp2(float x) {
   return y;
 }
 
-// readout_tile for one staged tile with the query fragments already loaded:
-// K fragments by ldmatrix (rows of 80 bytes: conflict-free), V fragments by
-// ldmatrix.trans, key blocks past `valid` skipped, exponentials on the
-// hardware ex2 (the probabilities are rounded to bf16 for the value product)
+// readout_tile for one staged tile (swizzled layout) with the query
+// fragments already loaded: K fragments by ldmatrix, V fragments by
+// ldmatrix.trans (both conflict-free through the piece swizzle), key blocks
+// past `valid` skipped, exponentials on the hardware ex2 (the probabilities
+// are rounded to bf16 for the value product)
 __device__ __forceinline__ void readout_tile_q(const ReadoutArgs& a, int h, const uint32_t qa[2][4],
                                                const __nv_bfloat16* ks, const __nv_bfloat16* vs,
                                                int valid, float o[4][4], float lrow[2], int lane) {
   const int g = lane >> 2, tig = lane & 3, mi = lane >> 3, ri = lane & 7;
-  const __nv_bfloat16* kh = ks + (size_t)h * RO_TILE * RO_PAD;
-  const __nv_bfloat16* vh = vs + (size_t)h * RO_TILE * RO_PAD;
+  const __nv_bfloat16* kh = ks + (size_t)h * RO_TILE * RO_ROW;
+  const __nv_bfloat16* vh = vs + (size_t)h * RO_TILE * RO_ROW;
+  const int sw = (ri >> 1) & 3;                   // piece swizzle of this lane's rows
   const int nblocks = (valid + 7) / 8;            // 8-key blocks holding valid keys
   float s[8][4];
   float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -330,7 +338,7 @@ __device__ __forceinline__ void readout_tile_q(const ReadoutArgs& a, int h, cons
     if (nb < nblocks) {
       // keys nb*8 .. +7; matrices: dims 0-7, 8-15, 16-23, 24-31
       uint32_t kf[4];
-      ro_ldsm_x4(kf, kh + (size_t)(nb * 8 + ri) * RO_PAD + mi * 8);
+      ro_ldsm_x4(kf, kh + (size_t)(nb * 8 + ri) * RO_ROW + ((mi ^ sw) * 8));
       float c[4] = {0.f, 0.f, 0.f, 0.f};
       const uint32_t b0[2] = {kf[0], kf[1]}, b1[2] = {kf[2], kf[3]};
       mma_bf16_16816(c, qa[0], b0);
@@ -379,8 +387,8 @@ __device__ __forceinline__ void readout_tile_q(const ReadoutArgs& a, int h, cons
       for (int np = 0; np < 2; ++np) {
         // matrices: keys kk*16 + 0-7 / 8-15, dims (2 np) * 8 and (2 np + 1) * 8
         uint32_t vf[4];
-        ro_ldsm_x4_trans(vf, vh + (size_t)(kk * 16 + (mi & 1) * 8 + ri) * RO_PAD +
-                                 (2 * np + (mi >> 1)) * 8);
+        ro_ldsm_x4_trans(vf, vh + (size_t)(kk * 16 + (mi & 1) * 8 + ri) * RO_ROW +
+                                 (((2 * np + (mi >> 1)) ^ sw) * 8));
         const uint32_t b0[2] = {vf[0], vf[1]}, b1[2] = {vf[2], vf[3]};
         mma_bf16_16816(o[2 * np], pa, b0);
         mma_bf16_16816(o[2 * np + 1], pa, b1);
@@ -394,14 +402,14 @@ __device__ __forceinline__ void readout_tile_q(const ReadoutArgs& a, int h, cons
 __global__ void __launch_bounds__(RO_WARPS * 32) readout_single_tile_kernel(ReadoutArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-  __nv_bfloat16* vs = ks + (size_t)a.H * RO_TILE * RO_PAD;
+  __nv_bfloat16* vs = ks + (size_t)a.H * RO_TILE * RO_ROW;
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
   const int length = min(a.lengths[b], RO_TILE);
   const int tasks = ((a.Q + 15) / 16) * a.H;
   if (length > 0) {
-    readout_stage(a, b, 0, length, ks, vs);
+    readout_stage<true>(a, b, 0, length, ks, vs);
     __syncthreads();
   }
   uint32_t qn[2][4] = {};
@@ -445,7 +453,7 @@ __global__ void __launch_bounds__(RO_WARPS * 32) readout_multi_tile_kernel(Reado
     }
     for (int t0 = 0; t0 < length; t0 += RO_TILE) {
       __syncthreads();
-      readout_stage(a, b, t0, length, ks, vs);
+      readout_stage<false>(a, b, t0, length, ks, vs);
       __syncthreads();
 #pragma unroll
       for (int i = 0; i < MAXT; ++i) {
@@ -532,19 +540,22 @@ extern "C" int grs_paged_attention(
                   kc_sp, kc_st, kc_sh, block_table, bt_stride, lengths, num_pages,
                   (__nv_bfloat16*)output, o_sb, o_sh, o_sq, batch, heads, query_len,
                   page_size, 1.4426950408889634f / sqrtf(32.f)};
+    // the single-tile kernel stages unpadded swizzled rows (64 KB at 8
+    // heads: three CTAs per SM), the multi-tile kernel padded ones
+    const size_t smem_single = (size_t)2 * heads * RO_TILE * RO_ROW * sizeof(__nv_bfloat16);
     const size_t smem = (size_t)2 * heads * RO_TILE * RO_PAD * sizeof(__nv_bfloat16);
     int dev = 0;
     cudaGetDevice(&dev);
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev]) {
       cudaFuncSetAttribute(readout_single_tile_kernel,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
       cudaFuncSetAttribute(readout_multi_tile_kernel<4>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
       attr_set[dev] = true;
     }
     if ((int64_t)max_blocks * page_size <= RO_TILE)
-      readout_single_tile_kernel<<<batch, RO_WARPS * 32, smem, grs::counted(stream)>>>(a);
+      readout_single_tile_kernel<<<batch, RO_WARPS * 32, smem_single, grs::counted(stream)>>>(a);
     else
       readout_multi_tile_kernel<4><<<batch, RO_WARPS * 32, smem, grs::counted(stream)>>>(a);
     GRS_CUDA_CHECK_LAUNCH();

@@ -87,6 +87,14 @@ def test_readout_mma_bf16(cuda_device):
     assert not out[0].any()  # zero-length history row
 
 
+@pytest.mark.parametrize("heads,max_len", [(3, 64), (16, 64), (16, 100)])
+def test_readout_mma_head_counts_bf16(cuda_device, heads, max_len):
+    # odd and the largest head counts of the tensor-core readout, one staged
+    # tile (swizzled rows) and several (padded rows)
+    out, exp = _random_case(5, 11, heads, 32, 16, 60, 40, max_len, torch.bfloat16, cuda_device)
+    np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
+
+
 def test_readout_mma_multi_tile_bf16(cuda_device):
     out, exp = _random_case(3, 9, 6, 32, 8, 90, 45, 150, torch.bfloat16, cuda_device)
     np.testing.assert_allclose(out.numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
