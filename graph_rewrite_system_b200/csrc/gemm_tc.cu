@@ -727,7 +727,11 @@ extern "C" int grs_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t 
                              int64_t ldr, const uint8_t* zero_row, void* out, int64_t ldo,
                              int32_t* status, void* stream) {
   const GemmEpilogue e = store_epilogue(bias, gelu, out, ldo, residual, ldr, zero_row, status);
-  if (N % 256 == 0)
+  // short GEMMs (the per-beam token path: M = beams) are latency-bound and
+  // fill few SMs with 256-column tiles; 128-column tiles give twice the CTAs,
+  // each with half the operand bytes and MMAs
+  const int64_t tiles256 = (int64_t)((M + GT_BM - 1) / GT_BM) * (N / 256);
+  if (N % 256 == 0 && tiles256 >= 64)
     return launch_gemm<256, GT_EPI_STORE>(a, lda, b, ldb, M, N, K, out, ldo, e,
                                           (cudaStream_t)stream);
   if (N % 128 == 0)
