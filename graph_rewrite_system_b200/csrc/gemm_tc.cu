@@ -601,6 +601,181 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
   if (threadIdx.x == 0 && (failed || drain_failed)) set_status(e.status, GRS_ERR_TIMEOUT);
 }
 
+// ---------------------------------------------------------------------------
+// B-stationary store GEMM for K = 256: C[M, N] = A[M, 256] B[N, 256]^T
+// (+ bias), rows with zero_row == 0 zeroed.  The model's K = 256 projections
+// (node queries, the graph layers' fb, the update's query) are HBM-bound:
+// their 256 x 256 weight tile is 2/3 of what the streaming kernel pulls
+// into shared memory per output tile.  Here each CTA keeps its weight tile
+// (all four K slices, 128 KB) resident for every tile it computes - the grid
+// is a multiple of N / 256, so a CTA's tiles all share one column block -
+// and only A streams through a four-stage ring.  Eight epilogue warps (two
+// per TMEM lane quarter, 128 columns each) store 32 x 64 blocks with TMA.
+// ---------------------------------------------------------------------------
+constexpr int BS_STAGES = 4;
+constexpr int BS_K = 256;
+constexpr int BS_KI = BS_K / GT_BK;                        // 4 K slices
+constexpr int BS_B_SLICE = 256 * GT_BK * 2;                // 32 KB: 256 weight rows x 64
+constexpr int BS_EPI_WARPS = 8, BS_THREADS = (2 + BS_EPI_WARPS) * 32;
+constexpr int BS_SMEM = BS_KI * BS_B_SLICE + BS_STAGES * GT_A_BYTES +
+                        BS_EPI_WARPS * GT_OUT_BYTES + 1024;   // + alignment slack
+
+__global__ void __launch_bounds__(BS_THREADS, 1)
+gemm_bstat_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                  const __grid_constant__ CUtensorMap tm_out, int M, int N, GemmEpilogue e) {
+  using namespace sm100;
+  extern __shared__ uint8_t bs_smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[BS_STAGES], empty_bar[BS_STAGES];
+  __shared__ __align__(8) uint64_t b_bar;                 // the weight tile has landed
+  __shared__ __align__(8) uint64_t tmem_full[GT_ACC], tmem_empty[GT_ACC];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int failed, drain_failed;
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(bs_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* bsm = smem;                                     // 4 x 32 KB weight slices
+  uint8_t* ring = bsm + BS_KI * BS_B_SLICE;                // 4 x 16 KB A stages
+  uint8_t* stg = ring + BS_STAGES * GT_A_BYTES;            // 8 x 4 KB output blocks
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = N / 256;
+  const int tiles = ((M + GT_BM - 1) / GT_BM) * n_tiles;
+  const int n0 = (blockIdx.x % n_tiles) * 256;            // gridDim.x % n_tiles == 0
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BS_STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < GT_ACC; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], BS_EPI_WARPS);
+    }
+    mbar_init(&b_bar, 1);
+    mbar_init(&drain_bar, 1);
+    failed = 0;
+    drain_failed = 0;
+    mbar_init_fence();
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, GT_ACC * 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer: the weight tile once, then A slices
+      mbar_arrive_expect_tx(&b_bar, BS_KI * BS_B_SLICE);
+      for (int k = 0; k < BS_KI; ++k)
+        tma_load_2d(bsm + k * BS_B_SLICE, &tm_b, k * GT_BK, n0, &b_bar);
+      int g = 0;
+      int armed[BS_STAGES] = {};
+      for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+        const int m0 = (t / n_tiles) * GT_BM;
+        for (int it = 0; it < BS_KI; ++it, ++g) {
+          const int s = g % BS_STAGES, r = g / BS_STAGES;
+          if (r > 0 && !mbar_wait(&empty_bar[s], (r - 1) & 1)) {
+            failed = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[s], GT_A_BYTES);
+          tma_load_2d(ring + s * GT_A_BYTES, &tm_a, it * GT_BK, m0, &full_bar[s]);
+          armed[s] = r + 1;
+        }
+      }
+      // every load in flight lands before the CTA exits
+      if (!mbar_wait(&b_bar, 0)) drain_failed = 1;
+      for (int s = 0; s < BS_STAGES; ++s)
+        if (armed[s] > 0 && !mbar_wait(&full_bar[s], (armed[s] - 1) & 1)) drain_failed = 1;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = idesc_bf16_f32(GT_BM, 256);
+      if (!mbar_wait(&b_bar, 0)) failed = 1;
+      tc_fence_after();
+      int g = 0, i = 0;
+      for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++i) {
+        const int b = i & 1, u = i >> 1;
+        if (u > 0 && !mbar_wait(&tmem_empty[b], (u - 1) & 1)) {
+          failed = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * 256);
+        for (int it = 0; it < BS_KI; ++it, ++g) {
+          const int s = g % BS_STAGES, r = g / BS_STAGES;
+          if (!mbar_wait(&full_bar[s], r & 1)) {
+            failed = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = smem_desc_k128(ring + s * GT_A_BYTES);
+          const uint64_t bd = smem_desc_k128(bsm + it * BS_B_SLICE);
+#pragma unroll
+          for (int kk = 0; kk < GT_BK / 16; ++kk)
+            mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, idesc, it > 0 || kk > 0);
+          mma_commit(&empty_bar[s]);
+        }
+        mma_commit(&tmem_full[b]);
+      }
+      mma_commit(&drain_bar);
+      if (!mbar_wait(&drain_bar, 0)) drain_failed = 1;
+    }
+  } else {
+    // TMEM -> registers -> bias, mask -> bf16 -> smem -> TMA store; warp
+    // (quarter, half) drains lanes 32 quarter.. and columns 128 half.. in
+    // two 64-column blocks through its one staging block
+    const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
+    uint8_t* stage = stg + ew * GT_OUT_BYTES;
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int m0 = (t / n_tiles) * GT_BM;
+      const int b = i & 1, u = i >> 1;
+      const int row = m0 + quarter * 32 + lane;
+      const bool zero = row < M && e.zero_row != nullptr && e.zero_row[row] == 0;
+      if (!mbar_wait_warp(&tmem_full[b], u & 1)) {
+        failed = 1;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int cg = 0; cg < 2; ++cg) {
+        const int col0 = half * 128 + cg * 64;
+        if (lane == 0) tma_store_wait_read();      // the block's last store has left smem
+        __syncwarp();
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tmem_load32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 256 + col0 + c * 32),
+                      v);
+          if (e.bias) add_bias32(v, e.bias + n0 + col0 + c * 32);
+          if (zero) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          uint32_t packed[16];
+          pack_bf16x32(v, packed);
+          stage_row_chunks(stage, lane, c, packed);
+        }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) tma_store_2d(&tm_out, stage, n0 + col0, m0 + quarter * 32);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[b]);  // this warp is done with accumulator b
+    }
+    if (lane == 0) tma_store_wait_all();
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0 && !drain_failed) {
+    tc_fence_after();
+    tmem_dealloc(tmem, GT_ACC * 256);
+  }
+  if (threadIdx.x == 0 && (failed || drain_failed)) set_status(e.status, GRS_ERR_TIMEOUT);
+}
+
 // ---- host --------------------------------------------------------------------
 namespace {
 
@@ -717,6 +892,39 @@ GemmEpilogue store_epilogue(const float* bias, int gelu, void* out, int64_t ldo,
   return e;
 }
 
+// The B-stationary kernel for a K = 256 store GEMM (no residual, no GELU)
+// with enough row blocks that one CTA per SM, a multiple of N / 256 of them,
+// stays busy.  Returns -1 when the shape is not one it takes.
+int launch_bstat(const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K,
+                 void* out, int64_t ldo, const GemmEpilogue& e, cudaStream_t stream) {
+  if (K != BS_K || N % 256 || e.residual || e.gelu || M <= 0) return -1;
+  if (lda % 8 || ldb % 8 || lda < K || ldb < K || ldo % 8 || ldo < N) return -1;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(e.bias) || !aligned16(out)) return -1;
+  static bool attr[64] = {};
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int n_tiles = N / 256;
+  const int64_t row_blocks = (M + GT_BM - 1) / GT_BM;
+  const int sm_count = dev < 64 && sms[dev] ? sms[dev] : 148;
+  const int grid = (sm_count / n_tiles) * n_tiles;
+  if (grid == 0 || row_blocks * n_tiles < 4 * (int64_t)grid) return -1;
+  CUtensorMap tm_a, tm_b, tm_out;
+  if (!gemm_map(&tm_a, a, M, K, lda, GT_BM) || !gemm_map(&tm_b, b, N, K, ldb, 256) ||
+      !gemm_map(&tm_out, out, M, N, ldo, 32))
+    return GRS_ERR_SHAPE;
+  if (dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(gemm_bstat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             BS_SMEM) != cudaSuccess)
+      return GRS_ERR_CUDA;
+    attr[dev] = true;
+  }
+  gemm_bstat_kernel<<<grid, BS_THREADS, BS_SMEM, counted(stream)>>>(tm_a, tm_b, tm_out, M, N, e);
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
 }  // namespace
 }  // namespace grs
 
@@ -731,6 +939,8 @@ extern "C" int grs_gemm_bf16(const void* a, int64_t lda, const void* b, int64_t 
   // fill few SMs with 256-column tiles; 128-column tiles give twice the CTAs,
   // each with half the operand bytes and MMAs
   const int64_t tiles256 = (int64_t)((M + GT_BM - 1) / GT_BM) * (N / 256);
+  const int bstat = launch_bstat(a, lda, b, ldb, M, N, K, out, ldo, e, (cudaStream_t)stream);
+  if (bstat >= 0) return bstat;
   if (N % 256 == 0 && tiles256 >= 64)
     return launch_gemm<256, GT_EPI_STORE>(a, lda, b, ldb, M, N, K, out, ldo, e,
                                           (cudaStream_t)stream);

@@ -56,7 +56,11 @@ def test_gemm_epilogue_strided_rows_and_shape_refusal():
     (1, 256, 256, False, False, False, False), (1000, 768, 256, False, False, False, False),
     (1000, 1024, 256, True, True, False, False), (1000, 256, 1024, True, False, True, True),
     (4100, 128, 256, True, False, False, False), (777, 512, 768, True, True, False, False),
-    (30001, 256, 256, False, False, True, True)])
+    (30001, 256, 256, False, False, True, True),
+    # K = 256 with many row blocks and no residual or GELU: the weight-
+    # stationary kernel (N = 256, 512, 768; ragged last row block)
+    (80001, 256, 256, True, False, False, True), (80000, 512, 256, True, False, False, False),
+    (150017, 768, 256, False, False, False, True)])
 def test_gemm_general_epilogue_matches_torch(m, n, k, bias, gelu, residual, masked):
     """kernels.gemm at the model's projection shapes: bias, GELU, residual add
     and dead-row zeroing, N = 128 (tile width 128) and multiples of 256."""
