@@ -686,7 +686,8 @@ def run_rollout(args, world, rank, device):
         # traffic: the DRAM / algorithmic byte ratio ncu measured for the
         # store-epilogue GEMM on the update-projection shape (M = 300000),
         # applied to the probed launches' algorithmic bytes
-        "roofline": probe.roofline(measured_peaks(), "gemm_tc_kernel (store epilogue)",
+        "roofline": probe.roofline(measured_peaks(),
+                                   "tcgen05 store GEMMs (gemm_tc_kernel, gemm_bstat_kernel)",
                                    profiled_traffic("update_gemm_traffic_ratio")),
         "search": {"last_level": {k: getattr(last, k) for k in (
                        "step", "input_states", "output_states", "best_speculative_gate_count",
