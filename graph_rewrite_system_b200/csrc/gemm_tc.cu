@@ -609,16 +609,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__
 // into shared memory per output tile.  Here each CTA keeps its weight tile
 // (all four K slices, 128 KB) resident for every tile it computes - the grid
 // is a multiple of N / 256, so a CTA's tiles all share one column block -
-// and only A streams through a four-stage ring.  Eight epilogue warps (two
-// per TMEM lane quarter, 128 columns each) store 32 x 64 blocks with TMA.
+// and only A streams through a five-stage ring.  Eight epilogue warps (two
+// per TMEM lane quarter, 128 columns each) store 32 x 32 blocks with TMA
+// through one 2 KB staging block each (64-byte swizzle): shared memory goes
+// to A stages, which bound this kernel, rather than to deeper staging.
 // ---------------------------------------------------------------------------
-constexpr int BS_STAGES = 4;
+constexpr int BS_STAGES = 5;
 constexpr int BS_K = 256;
 constexpr int BS_KI = BS_K / GT_BK;                        // 4 K slices
 constexpr int BS_B_SLICE = 256 * GT_BK * 2;                // 32 KB: 256 weight rows x 64
 constexpr int BS_EPI_WARPS = 8, BS_THREADS = (2 + BS_EPI_WARPS) * 32;
+constexpr int BS_STAGING = GT_OUT_BYTES / 2;             // one 32 x 32 bf16 block per warp
 constexpr int BS_SMEM = BS_KI * BS_B_SLICE + BS_STAGES * GT_A_BYTES +
-                        BS_EPI_WARPS * GT_OUT_BYTES + 1024;   // + alignment slack
+                        BS_EPI_WARPS * BS_STAGING + 1024;   // + alignment slack
 
 __global__ void __launch_bounds__(BS_THREADS, 1)
 gemm_bstat_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -634,8 +637,8 @@ gemm_bstat_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(bs_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* bsm = smem;                                     // 4 x 32 KB weight slices
-  uint8_t* ring = bsm + BS_KI * BS_B_SLICE;                // 4 x 16 KB A stages
-  uint8_t* stg = ring + BS_STAGES * GT_A_BYTES;            // 8 x 4 KB output blocks
+  uint8_t* ring = bsm + BS_KI * BS_B_SLICE;                // 5 x 16 KB A stages
+  uint8_t* stg = ring + BS_STAGES * GT_A_BYTES;            // 8 x 2 KB output blocks
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = N / 256;
   const int tiles = ((M + GT_BM - 1) / GT_BM) * n_tiles;
@@ -722,10 +725,11 @@ gemm_bstat_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     }
   } else {
     // TMEM -> registers -> bias, mask -> bf16 -> smem -> TMA store; warp
-    // (quarter, half) drains lanes 32 quarter.. and columns 128 half.. in
-    // two 64-column blocks through its one staging block
+    // (quarter, half) drains lanes 32 quarter.. and columns 128 half.. as
+    // four 32 x 32 blocks through its 2 KB staging block (64-byte swizzle)
     const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
-    uint8_t* stage = stg + ew * GT_OUT_BYTES;
+    uint8_t* stage = stg + ew * BS_STAGING;
+    const int sw = (lane >> 1) & 3;                  // 64-byte swizzle of row `lane`
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int m0 = (t / n_tiles) * GT_BM;
@@ -738,27 +742,27 @@ gemm_bstat_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int cg = 0; cg < 2; ++cg) {
-        const int col0 = half * 128 + cg * 64;
-        if (lane == 0) tma_store_wait_read();      // the block's last store has left smem
+      for (int c = 0; c < 4; ++c) {
+        const int col0 = half * 128 + c * 32;
+        uint8_t* buf = stage;
+        if (lane == 0) tma_store_wait_read();        // the last block's store has left it
         __syncwarp();
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tmem_load32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 256 + col0 + c * 32),
-                      v);
-          if (e.bias) add_bias32(v, e.bias + n0 + col0 + c * 32);
-          if (zero) {
+        float v[32];
+        tmem_load32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 256 + col0), v);
+        if (e.bias) add_bias32(v, e.bias + n0 + col0);
+        if (zero) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
-          }
-          uint32_t packed[16];
-          pack_bf16x32(v, packed);
-          stage_row_chunks(stage, lane, c, packed);
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
+        uint32_t packed[16];
+        pack_bf16x32(v, packed);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ sw) << 4)) =
+              make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
         fence_async_shared();
         __syncwarp();
-        if (lane == 0) tma_store_2d(&tm_out, stage, n0 + col0, m0 + quarter * 32);
+        if (lane == 0) tma_store_2d(&tm_out, buf, n0 + col0, m0 + quarter * 32);
       }
       tc_fence_before();
       __syncwarp();
@@ -794,11 +798,11 @@ PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
 }
 
 // [rows, cols] bf16 row-major (row stride `ld` elements) in boxes of 64
-// columns x box_rows rows, 128-byte swizzle; a small cache keyed by every
-// encoded field.
+// columns x box_rows rows with the 128-byte swizzle, or of 32 columns with
+// the 64-byte swizzle; a small cache keyed by every encoded field.
 bool gemm_map(CUtensorMap* out, const void* base, int64_t rows, int64_t cols, int64_t ld,
-              int box_rows) {
-  struct Key { const void* base; int64_t rows, cols, ld; int box; };
+              int box_rows, int box_cols = 64) {
+  struct Key { const void* base; int64_t rows, cols, ld; int box, box_cols; };
   constexpr int kCache = 64;
   static Key keys[kCache];
   static CUtensorMap maps[kCache];
@@ -806,7 +810,8 @@ bool gemm_map(CUtensorMap* out, const void* base, int64_t rows, int64_t cols, in
   static std::mutex mu;
   Key k;
   std::memset(&k, 0, sizeof(k));
-  k.base = base; k.rows = rows; k.cols = cols; k.ld = ld; k.box = box_rows;
+  k.base = base; k.rows = rows; k.cols = cols; k.ld = ld; k.box = box_rows; k.box_cols = box_cols;
+  if (box_cols != 64 && box_cols != 32) return false;
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i)
     if (std::memcmp(&keys[i], &k, sizeof(Key)) == 0) {
@@ -817,10 +822,11 @@ bool gemm_map(CUtensorMap* out, const void* base, int64_t rows, int64_t cols, in
   if (!fn) return false;
   cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t gstr[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)box_rows}, estr[2] = {1, 1};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows}, estr[2] = {1, 1};
   CUtensorMap m;
   if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstr, box, estr,
-         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_INTERLEAVE_NONE,
+         box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return false;
   keys[next] = k;
@@ -912,7 +918,7 @@ int launch_bstat(const void* a, int64_t lda, const void* b, int64_t ldb, int M, 
   if (grid == 0 || row_blocks * n_tiles < 4 * (int64_t)grid) return -1;
   CUtensorMap tm_a, tm_b, tm_out;
   if (!gemm_map(&tm_a, a, M, K, lda, GT_BM) || !gemm_map(&tm_b, b, N, K, ldb, 256) ||
-      !gemm_map(&tm_out, out, M, N, ldo, 32))
+      !gemm_map(&tm_out, out, M, N, ldo, 32, 32))
     return GRS_ERR_SHAPE;
   if (dev < 64 && !attr[dev]) {
     if (cudaFuncSetAttribute(gemm_bstat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
