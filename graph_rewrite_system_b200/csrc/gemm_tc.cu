@@ -105,9 +105,11 @@ __device__ __forceinline__ float2 gelu_pair(float2 x) {
   q = __fmul2_rn(q, q);
   q = __fmul2_rn(q, q);
   q = __fmul2_rn(q, q);
-  const float ex = __fdividef(1.f, q.x), ey = __fdividef(1.f, q.y);
-  return make_float2(x.x >= 0.f ? x.x * fmaf(-0.5f, ex, 1.f) : 0.5f * x.x * ex,
-                     x.y >= 0.f ? x.y * fmaf(-0.5f, ey, 1.f) : 0.5f * x.y * ey);
+  // h = erfc(z) / 2 (exact halving); Phi(x) = 1 - h for x >= 0, h below:
+  // the same roundings as x (1 - erfc / 2) and (x / 2) erfc, on pairs
+  const float2 h = __fmul2_rn(make_float2(__fdividef(1.f, q.x), __fdividef(1.f, q.y)), c(0.5f));
+  const float2 om = __ffma2_rn(h, c(-1.f), c(1.f));
+  return __fmul2_rn(x, make_float2(x.x >= 0.f ? om.x : h.x, x.y >= 0.f ? om.y : h.y));
 }
 
 __device__ __forceinline__ void add_bias32(float v[32], const float* bias) {
