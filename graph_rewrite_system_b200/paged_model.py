@@ -609,17 +609,18 @@ class PagedActionBindingModel(nn.Module):
         token = torch.empty_like(raw)
         K.position_token(raw, w["action_position"], past_lengths, active, token)
         valid = active
-        new_keys = torch.empty(self.action_layers_count, b, h, hd, device=dev, dtype=dt)
-        new_values = torch.empty_like(new_keys)
+        # every layer's [q | k | v] rows in one buffer: the new keys and values
+        # of all layers leave it in two copies after the loop
+        qkv_all = torch.empty(self.action_layers_count, b, 3 * W, device=dev, dtype=dt)
         ln = torch.empty_like(token)
         token2 = torch.empty_like(token)
         for layer in range(self.action_layers_count):
             p = f"causal{layer}."
             K.add_layernorm(token, gamma=w[p + "in_w"], beta=w[p + "in_b"], ln_out=ln)
             if tc:
-                qkv = K.gemm(ln, w[p + "qkv_k"], status=status).view(b, 3, h, hd)
+                qkv = K.gemm(ln, w[p + "qkv_k"], out=qkv_all[layer], status=status).view(b, 3, h, hd)
             else:
-                qkv = K.linear(ln, w[p + "qkv_t"]).view(b, 3, h, hd)
+                qkv = K.linear(ln, w[p + "qkv_t"], out=qkv_all[layer]).view(b, 3, h, hd)
             q, k, v = qkv.unbind(1)
             ctx = paged_attention(q.unsqueeze(2), key_cache[layer], value_cache[layer],
                                   block_table, past_lengths, current_key=k, current_value=v,
@@ -639,8 +640,8 @@ class PagedActionBindingModel(nn.Module):
                 f0 = K.bias_gelu(K.linear(ln, w[p + "f0_t"]), w[p + "f0_b"])
                 f3 = K.linear(f0, w[p + "f3_t"], w[p + "f3_b"])
                 K.add_layernorm(token2, f3, sum_out=token, zero_beam=active, zero_before=True)
-            new_keys[layer].copy_(k)
-            new_values[layer].copy_(v)
+        kv = qkv_all.view(self.action_layers_count, b, 3, h, hd)
+        new_keys, new_values = kv[:, :, 1].contiguous(), kv[:, :, 2].contiguous()
         action = torch.empty_like(token)
         K.add_layernorm(token, gamma=w["out_norm_w"], beta=w["out_norm_b"], ln_out=action,
                         zero_beam=active)
