@@ -37,14 +37,14 @@ struct SelectArgs {
   float near_scale, near_bias, near_thr, far_scale, far_bias, far_thr;
   int64_t* out_batch; int64_t* out_source; int64_t* out_anchor; float* out_prob;
   float* out_score;              // optional calibrated score
+  int vec8;                      // rows are whole 8-item chunks, 16-byte aligned
 };
 
-__device__ __forceinline__ bool item_key(const SelectArgs& a, int64_t row, int idx,
-                                         uint32_t* key) {
+// the item's key from its already loaded eligibility and logit
+__device__ __forceinline__ bool item_key_loaded(const SelectArgs& a, int64_t row, int idx,
+                                                bool eligible, float logit, uint32_t* key) {
+  if (!eligible) return false;
   const int slot = idx / a.num_sources;
-  const int64_t off = row * (int64_t)a.slots * a.num_sources + idx;
-  if (!a.eligible[off]) return false;
-  const float logit = a.logits[off];
   const bool near = a.distance[row * a.slots + slot] <= 2;
   const float thr = near ? a.near_thr : a.far_thr;
   if (!(logit >= thr)) return false;
@@ -53,6 +53,13 @@ __device__ __forceinline__ bool item_key(const SelectArgs& a, int64_t row, int i
   if (!(calibrated > -INFINITY)) return false;  // -inf scores are not present
   *key = float_order(calibrated);
   return true;
+}
+
+__device__ __forceinline__ bool item_key(const SelectArgs& a, int64_t row, int idx,
+                                         uint32_t* key) {
+  const int64_t off = row * (int64_t)a.slots * a.num_sources + idx;
+  if (!a.eligible[off]) return false;
+  return item_key_loaded(a, row, idx, true, a.logits[off], key);
 }
 
 __global__ void __launch_bounds__(SEL_THREADS) select_candidates_kernel(SelectArgs a) {
@@ -71,7 +78,31 @@ __global__ void __launch_bounds__(SEL_THREADS) select_candidates_kernel(SelectAr
     const int shift = 24 - 8 * pass;
     for (int i = tid; i < 256; i += SEL_THREADS) hist[i] = 0;
     __syncthreads();
-    for (int idx = tid; idx < n; idx += SEL_THREADS) {
+    if (pass == 0 && a.vec8) {
+      // 8-item chunks: a thread's eligibility bytes and logits arrive in one
+      // 8-byte and two 16-byte loads
+      const int64_t base = row * (int64_t)n;
+      for (int ch = tid; ch < n / 8; ch += SEL_THREADS) {
+        const int idx0 = ch * 8;
+        const uint2 el = *reinterpret_cast<const uint2*>(a.eligible + base + idx0);
+        const float4 l0 = *reinterpret_cast<const float4*>(a.logits + base + idx0);
+        const float4 l1 = *reinterpret_cast<const float4*>(a.logits + base + idx0 + 4);
+        const float lg[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const bool e = ((j < 4 ? el.x : el.y) >> (8 * (j & 3))) & 0xffu;
+          uint32_t key;
+          if (item_key_loaded(a, row, idx0 + j, e, lg[j], &key)) {
+            atomicAdd(&hist[(key >> shift) & 255], 1);
+            const int slot = atomicAdd(&s_count, 1);
+            if (slot < SEL_MAX_K)
+              sel[slot] = ((unsigned long long)key << 32) |
+                          (unsigned long long)(0xffffffffu - (uint32_t)(idx0 + j));
+          }
+        }
+      }
+    }
+    for (int idx = tid; !(pass == 0 && a.vec8) && idx < n; idx += SEL_THREADS) {
       uint32_t key;
       if (item_key(a, row, idx, &key) && (key & mask) == prefix) {
         atomicAdd(&hist[(key >> shift) & 255], 1);
@@ -250,9 +281,12 @@ extern "C" int grs_select_candidates(const float* logits, const uint8_t* eligibl
                                      void* stream) {
   if (batch <= 0) return GRS_OK;
   if (k <= 0 || k > SEL_MAX_K || slots <= 0 || num_sources <= 0) return GRS_ERR_SHAPE;
+  const int64_t n = (int64_t)slots * num_sources;
+  const int vec8 = n % 8 == 0 && (reinterpret_cast<uintptr_t>(eligible) & 7) == 0 &&
+                   (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
   SelectArgs a{logits, eligible, distance, slots, num_sources, k, near_scale, near_bias,
                near_thr, far_scale, far_bias, far_thr, out_batch, out_source, out_anchor,
-               out_prob, out_score};
+               out_prob, out_score, vec8};
   select_candidates_kernel<<<batch, SEL_THREADS, 0, grs::counted((cudaStream_t)stream)>>>(a);
   GRS_CUDA_CHECK_LAUNCH();
   return GRS_OK;

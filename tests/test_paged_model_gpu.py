@@ -137,14 +137,16 @@ def test_structural_decode_and_candidates_match_reference(cuda_device):
                                rtol=1e-6, atol=1e-7)
 
 
-@pytest.mark.parametrize("k", [1, 7, 80, 500])
-def test_select_candidates_topk_with_ties(cuda_device, k):
-    """Random bf16-rounded logits (many exact ties) vs the oracle's stable order."""
+@pytest.mark.parametrize("k,s,ns", [(1, 97, 13), (7, 97, 13), (80, 97, 13), (500, 97, 13),
+                                    (7, 96, 31), (500, 96, 31), (2048, 96, 31)])
+def test_select_candidates_topk_with_ties(cuda_device, k, s, ns):
+    """Random bf16-rounded logits (many exact ties) vs the oracle's stable order;
+    96 x 31 items per row take the 8-item vector loads of the first pass."""
     from graph_rewrite_system_b200 import kernels as K
     from graph_rewrite_system_b200.synthetic import SELECT_ALL_THRESHOLDS
 
-    gen = torch.Generator().manual_seed(k)
-    b, s, ns = 6, 97, 13
+    gen = torch.Generator().manual_seed(k + s)
+    b = 6
     logits = torch.randn(b, s, ns, generator=gen).bfloat16().float()
     eligible = torch.rand(b, s, ns, generator=gen) > 0.4
     eligible[2] = False
