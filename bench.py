@@ -359,6 +359,36 @@ def run_decode_attention(args, world, rank, device):
     kernel_ms = start.elapsed_time(end) / args.steps
     kernel_ms = max_over_ranks(kernel_ms, world, device)
 
+    # the earlier 8-CTA cluster design on the same inputs, for comparison
+    from graph_rewrite_system_b200 import _lib
+
+    lib = _lib.lib()
+
+    def step_cluster(i):
+        x = sets[i % copies]
+        q, kc = x.query, x.key_cache
+        rc = lib.grs_decode_attention_shared_cluster(
+            q.data_ptr(), q.stride(0), q.stride(1), kc.data_ptr(), x.value_cache.data_ptr(),
+            kc.stride(0), kc.stride(1), kc.stride(2), x.block_table.data_ptr(),
+            x.block_table.stride(0), x.block_table.shape[1], x.lengths.data_ptr(), kc.shape[0],
+            None, None, 0, 0, None, x.shared_key.data_ptr(), x.shared_value.data_ptr(),
+            x.shared_key.shape[0], out.data_ptr(), out.stride(0), out.stride(1), q.shape[0],
+            q.shape[1], kc.shape[1], None, stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"cluster decode returned {rc}")
+
+    for i in range(copies):
+        step_cluster(i)
+    torch.cuda.synchronize(device)
+    device_sleep_us(queue_ahead_us(args.steps))
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    for i in range(args.steps):
+        step_cluster(i)
+    c1.record(stream)
+    torch.cuda.synchronize(device)
+    cluster_ms = c0.elapsed_time(c1) / args.steps
+
     # the same launch alone after an L2 flush (launch latency included)
     single = []
     device_sleep_us(queue_ahead_us(args.steps))
@@ -422,6 +452,7 @@ def run_decode_attention(args, world, rank, device):
                          f"({copies * w.unique_bytes / 1e6:.0f} MB) used in rotation",
                    "timing": "launches back to back, queued ahead of the device",
                    "single_launch_after_l2_flush_ms": single_ms,
+                   "cluster_kernel_ms": cluster_ms,
                    "parallelism": f"replicas x{world}"},
         "e2e": {"value": world * 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
@@ -433,7 +464,7 @@ def run_decode_attention(args, world, rank, device):
                      "logical_bytes": logical,
                      "logical_gbs": logical / (kernel_ms * 1e-3) / 1e9,
                      "peak_source": f"{peaks['source']} hbm_gbs",
-                     "kernel": "decode_cluster_kernel"},
+                     "kernel": "decode_group_kernel"},
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -537,6 +537,463 @@ decode_cluster_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tm_sk,
   }
 }
 
+// ---- grouped decode: one CTA per (32 beams, head), no clusters -------------
+//
+// The cluster kernel above reads the whole shared prefix once per 16 beams
+// and pays for a cross-CTA merge.  Here a CTA owns 32 consecutive beams (two
+// mma M tiles of 16) for ONE head and every key those beams see, so the
+// shared prefix is read once per 32 beams and per head slice (64 bytes of
+// each key row), the pages once per 16-beam tile that holds them, and the
+// softmax merge stays inside the CTA.  Beams of a search are stored in
+// lineage order, so neighbouring beams share their upper pages.
+//
+// Staging is plain 16-byte cp.async into shared memory with a 64-byte row
+// swizzle (16-byte chunk c of row r at c ^ ((r >> 1) & 3): conflict-free
+// ldmatrix over eight consecutive rows).  The shared prefix of the head goes
+// out at kernel entry, in chunks of `chunk_rows`; while it lands the CTA reads
+// the 32 beams' block tables, two warps deduplicate each M tile's pages per
+// column, and the distinct page units (16 rows each; the tile's current tokens
+// form one more unit) go out in rounds of `round_units`.  Each thread keeps
+// one fixed (K or V, row, 16-byte chunk) position of a unit and walks the
+// units, so a copy costs a few instructions.  Warps 0-7 take M tile 0 and
+// warps 8-15 M tile 1; the eight warps of a tile take every eighth unit, up
+// to four units per online-softmax step (all their scores, one max, one
+// rescale; ldmatrix-fed m16n8k16 bf16 mma, fp32 accumulation), and merge
+// their eight partials through shared memory at the end.  The kernel has no inter-CTA waits and no spin loops.
+constexpr int DG_BEAMS = 32;                  // beams per CTA (two M tiles)
+constexpr int DG_WARPS = 16;                  // eight per M tile
+constexpr int DG_THREADS = DG_WARPS * 32;
+constexpr int DG_MAX_COLS = 32;               // block-table columns
+constexpr int DG_TILE_BYTES = DC_UNIT * 64;   // 16 rows x one head of 32 bf16
+constexpr int DG_MAX_CHUNK_ROWS = 512;        // shared rows staged at once
+constexpr int DG_ROUND_UNITS = 48;            // page/current units staged at once
+constexpr int DG_TILE_WARPS = DG_WARPS / 2;
+constexpr int DG_STEP = 4;                    // units per online-softmax step
+constexpr int DG_MERGE_BYTES = 2 * DG_TILE_WARPS * DC_UNIT * (int)sizeof(Partial);
+
+struct GroupArgs {
+  const __nv_bfloat16* q; int64_t q_sb, q_sh;
+  const __nv_bfloat16* kc; const __nv_bfloat16* vc; int64_t kc_sp, kc_st, kc_sh;
+  const int32_t* bt; int64_t bt_s; int cols; const int32_t* lengths; int num_pages;
+  const __nv_bfloat16* ck; const __nv_bfloat16* cv; int64_t ck_sb, ck_sh;
+  const uint8_t* cvalid;
+  const __nv_bfloat16* sk; const __nv_bfloat16* sv; int num_shared;   // [N, H, 32] contiguous
+  __nv_bfloat16* out; int64_t o_sb, o_sh;
+  int B, H, page; float scale_log2;
+  int chunk_rows;     // shared rows staged at once (a multiple of 16)
+  int round_units;    // page/current units staged at once
+};
+
+// 16-byte copy into shared memory through L2; a miss brings the surrounding
+// 256 bytes into L2 (the other heads' slices of the same key row, which the
+// CTAs of those heads read at about the same time)
+__device__ __forceinline__ void cp_async16(unsigned dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;\n" ::"r"(dst), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void st_shared_zero16(unsigned dst) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(dst), "r"(0) : "memory");
+}
+// 16-byte chunk `chunk` (0-3) of row `row` in a tile of 64-byte rows
+__device__ __forceinline__ unsigned swz64(unsigned tile, int row, int chunk) {
+  return tile + row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4);
+}
+
+// one staged unit of 16 key rows as seen by one warp's M tile
+struct GroupView {
+  unsigned kt, vt;    // K and V tiles in shared memory
+  int kind;           // 0 shared, 1 page, 2 current tokens
+  int mask;           // beams of the tile that see the unit (page/current)
+  int pos0;           // position of the first row (page)
+  int rows;           // rows that are keys (shared)
+};
+
+__global__ void __launch_bounds__(DG_THREADS, 1) decode_group_kernel(GroupArgs a) {
+  __shared__ int s_len[DG_BEAMS], s_cur[DG_BEAMS];
+  // element offset of each staged unit's first K/V row for this head (page
+  // units), or -1 - m for the current unit of M tile m
+  __shared__ int64_t s_uoff[DG_ROUND_UNITS];
+  __shared__ int s_bt[DG_MAX_COLS][DG_BEAMS];
+  // distinct (column, page) entries per M tile: page id, column << 16 | beam mask
+  __shared__ int s_ent_page[2][DC_UNIT * DG_MAX_COLS];
+  __shared__ int s_ent_cm[2][DC_UNIT * DG_MAX_COLS];
+  __shared__ int s_nent[2], s_curmask[2];
+  extern __shared__ __align__(1024) unsigned char dyn[];
+
+  const int h = blockIdx.y;
+  const int beam0 = blockIdx.x * DG_BEAMS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int mt = warp / DG_TILE_WARPS, sub = warp % DG_TILE_WARPS;
+  const int ns = a.num_shared;
+  const unsigned shk = smem_addr(dyn);
+  const unsigned shv = shk + a.chunk_rows * 64;
+  const unsigned pg = shk + a.chunk_rows * 128;
+  Partial* part = reinterpret_cast<Partial*>(dyn + a.chunk_rows * 128 +
+                                             a.round_units * 2 * DG_TILE_BYTES);
+
+  // rows r0 .. r0 + chunk_rows - 1 of the shared prefix (head h); rows past
+  // the prefix are zero so that masked rows never carry non-finite values.
+  // Thread t copies chunk t % 4 of rows t / 4, t / 4 + 128, ... of K and V.
+  auto load_shared = [&](int r0) {
+    const int rows = min(a.chunk_rows, ns - r0);
+    const int rows16 = (rows + DC_UNIT - 1) & ~(DC_UNIT - 1);
+    const int c = tid & 3;
+    const int64_t row_stride = (int64_t)a.H * DC_D * (DG_THREADS / 4);
+    const int64_t off0 = (int64_t)(r0 + (tid >> 2)) * a.H * DC_D + h * DC_D + c * 8;
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const __nv_bfloat16* src = (kv ? a.sv : a.sk) + off0;
+      const unsigned tile = kv ? shv : shk;
+      for (int r = tid >> 2; r < rows16; r += DG_THREADS / 4, src += row_stride) {
+        if (r < rows) cp_async16(swz64(tile, r, c), src);
+        else st_shared_zero16(swz64(tile, r, c));
+      }
+    }
+  };
+
+  // 1. the shared prefix goes out first: it needs no block-table data
+  if (ns > 0) load_shared(0);
+  cp_async_commit();
+
+  // 2. lengths, current-token flags and block-table columns of the 32 beams
+  if (tid < DG_BEAMS) {
+    const int b = beam0 + tid;
+    s_len[tid] = b < a.B ? a.lengths[b] : 0;
+    s_cur[tid] = (b < a.B && a.ck) ? (a.cvalid[b] != 0) : 0;
+  }
+  for (int i = tid; i < a.cols * DG_BEAMS; i += DG_THREADS) {
+    const int c = i >> 5, j = i & 31, b = beam0 + j;
+    s_bt[c][j] = b < a.B ? a.bt[(int64_t)b * a.bt_s + c] : -1;
+  }
+  // query fragments (A operand, rows = beams) of this warp's M tile
+  uint32_t qa[2][4] = {};
+  {
+    const int r0 = beam0 + mt * DC_UNIT + g, r1 = r0 + 8;
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      const int c = ks * 16 + tig * 2;
+      const __nv_bfloat16* p0 = a.q + (int64_t)r0 * a.q_sb + (int64_t)h * a.q_sh + c;
+      const __nv_bfloat16* p1 = a.q + (int64_t)r1 * a.q_sb + (int64_t)h * a.q_sh + c;
+      if (r0 < a.B) {
+        qa[ks][0] = *reinterpret_cast<const uint32_t*>(p0);
+        qa[ks][2] = *reinterpret_cast<const uint32_t*>(p0 + 8);
+      }
+      if (r1 < a.B) {
+        qa[ks][1] = *reinterpret_cast<const uint32_t*>(p1);
+        qa[ks][3] = *reinterpret_cast<const uint32_t*>(p1 + 8);
+      }
+    }
+  }
+  __syncthreads();
+
+  // 3. distinct pages per column of each M tile (warp m for tile m): lanes
+  // 0-15 take column c, lanes 16-31 column c + 1
+  if (warp < 2) {
+    const int m = warp;
+    int count = 0;
+    for (int c0 = 0; c0 < a.cols; c0 += 2) {
+      const int c = c0 + (lane >> 4), j = m * DC_UNIT + (lane & 15);
+      int p = -1;
+      if (c < a.cols && c * a.page < s_len[j]) {
+        p = s_bt[c][j];
+        if (p < 0 || p >= a.num_pages) p = -1;
+      }
+      const unsigned long long key =
+          p >= 0 ? (((unsigned long long)(unsigned)p << 1) | (unsigned)(lane >> 4))
+                 : ((1ull << 63) | (unsigned)lane);
+      const unsigned peers = __match_any_sync(0xffffffffu, key);
+      const bool lead = p >= 0 && __ffs(peers) - 1 == lane;
+      const unsigned leads = __ballot_sync(0xffffffffu, lead);
+      if (lead) {
+        const int e = count + __popc(leads & ((1u << lane) - 1u));
+        s_ent_page[m][e] = p;
+        s_ent_cm[m][e] = (c << 16) | ((peers >> (lane & 16)) & 0xFFFF);
+      }
+      count += __popc(leads);
+    }
+    const unsigned cm = __ballot_sync(0xffffffffu, lane < DC_UNIT && s_cur[m * DC_UNIT + lane]);
+    if (lane == 0) {
+      s_nent[m] = count;
+      s_curmask[m] = (int)cm;
+    }
+  }
+  __syncthreads();
+
+  // units of tile 0 come first, then those of tile 1; per tile: page
+  // entry e, 16-row block sb of it, then the current unit (if any beam has one)
+  const int per_page = a.page / DC_UNIT;
+  const int n0 = s_nent[0] * per_page + (s_curmask[0] ? 1 : 0);
+  const int total = n0 + s_nent[1] * per_page + (s_curmask[1] ? 1 : 0);
+  // page id (-1: current unit), first row in the page, beam mask, position
+  auto unit_info = [&](int u, int& page, int& row0, int& mask, int& pos0, int& m) {
+    m = u < n0 ? 0 : 1;
+    const int local = u - (m ? n0 : 0);
+    if (local < s_nent[m] * per_page) {
+      const int e = per_page == 1 ? local : local / per_page, sb = local - e * per_page;
+      const int cm = s_ent_cm[m][e];
+      page = s_ent_page[m][e];
+      row0 = sb * DC_UNIT;
+      mask = cm & 0xFFFF;
+      pos0 = (cm >> 16) * a.page + row0;
+    } else {
+      page = -1;
+      row0 = 0;
+      mask = s_curmask[m];
+      pos0 = -1;
+    }
+  };
+  // units u0 .. u0 + nr - 1 into the page slots: first each unit's source
+  // offset, then thread t copies (K or V, row, chunk) = position t % 128 of
+  // units t / 128, t / 128 + 4, ...
+  auto load_round = [&](int u0, int nr) {
+    if (tid < nr) {
+      int page, row0, mask, pos0, m;
+      unit_info(u0 + tid, page, row0, mask, pos0, m);
+      s_uoff[tid] = page >= 0
+                        ? (int64_t)page * a.kc_sp + (int64_t)row0 * a.kc_st + (int64_t)h * a.kc_sh
+                        : (int64_t)(-1 - m);
+    }
+    __syncthreads();
+    const int rem = tid & 127;
+    const int kv = rem >> 6, r = (rem >> 2) & 15, c = rem & 3;
+    const __nv_bfloat16* cache = kv ? a.vc : a.kc;
+    const __nv_bfloat16* cur = kv ? a.cv : a.ck;
+    const int64_t page_off = (int64_t)r * a.kc_st + c * 8;
+    const unsigned dst0 = swz64(pg + kv * DG_TILE_BYTES, r, c);
+    for (int j = tid >> 7; j < nr; j += DG_THREADS / 128) {
+      const int64_t off = s_uoff[j];
+      const unsigned dst = dst0 + j * 2 * DG_TILE_BYTES;
+      if (off >= 0) {
+        cp_async16(dst, cache + off + page_off);
+      } else {
+        const int b = beam0 + (int)(-1 - off) * DC_UNIT + r;
+        if (b < a.B) cp_async16(dst, cur + (int64_t)b * a.ck_sb + (int64_t)h * a.ck_sh + c * 8);
+        else st_shared_zero16(dst);
+      }
+    }
+  };
+  // 4. the first round of page units
+  load_round(0, min(total, a.round_units));
+  cp_async_commit();
+
+  // ---- online softmax over this warp's units -------------------------------
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float o[4][4] = {};
+  const bool live = beam0 + mt * DC_UNIT < a.B;
+  const int len0 = s_len[mt * DC_UNIT + g], len1 = s_len[mt * DC_UNIT + g + 8];
+
+  auto step = [&](int n, const GroupView* v) {
+    float s[DG_STEP][2][4] = {};
+#pragma unroll
+    for (int k = 0; k < DG_STEP; ++k) {
+      if (k >= n) break;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        uint32_t kf[4];
+        ldmatrix_x4(kf, swz64(v[k].kt, nt * 8 + (lane & 7), lane >> 3));
+        mma16816(s[k][nt], qa[0], kf[0], kf[1]);
+        mma16816(s[k][nt], qa[1], kf[2], kf[3]);
+      }
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < DG_STEP; ++k) {
+      if (k >= n) break;
+      // rows of the unit that beams g (vm0) and g + 8 (vm1) see, as 16-bit
+      // masks, shifted so that bit nt * 8 + c is this lane's row nt * 8 + tig * 2 + c
+      const bool see0 = (v[k].mask >> g) & 1, see1 = (v[k].mask >> (g + 8)) & 1;
+      auto first_rows = [](int n) -> unsigned {
+        return n >= DC_UNIT ? 0xFFFFu : (n <= 0 ? 0u : (1u << n) - 1u);
+      };
+      unsigned vm0, vm1;
+      if (v[k].kind == 0) {
+        vm0 = vm1 = first_rows(v[k].rows);
+      } else if (v[k].kind == 1) {
+        vm0 = see0 ? first_rows(len0 - v[k].pos0) : 0u;
+        vm1 = see1 ? first_rows(len1 - v[k].pos0) : 0u;
+      } else {                                     // row r is beam r's current token
+        vm0 = see0 ? 1u << g : 0u;
+        vm1 = see1 ? 1u << (g + 8) : 0u;
+      }
+      vm0 >>= tig * 2;
+      vm1 >>= tig * 2;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const bool v0 = (vm0 >> (nt * 8 + c)) & 1, v1 = (vm1 >> (nt * 8 + c)) & 1;
+          s[k][nt][c] = v0 ? s[k][nt][c] * a.scale_log2 : -INFINITY;
+          s[k][nt][2 + c] = v1 ? s[k][nt][2 + c] * a.scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, s[k][nt][c]);
+          mx1 = fmaxf(mx1, s[k][nt][2 + c]);
+        }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    // a row that has seen no key yet keeps -inf and is exponentiated against
+    // 0 instead, so every term is 2^-inf = 0
+    const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+    const float e0 = nm0 == -INFINITY ? 0.f : nm0, e1 = nm1 == -INFINITY ? 0.f : nm1;
+    const float c0 = fast_exp2(m0 - e0), c1 = fast_exp2(m1 - e1);
+    float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < DG_STEP; ++k) {
+      if (k >= n) break;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          s[k][nt][c] = fast_exp2(s[k][nt][c] - e0);
+          s[k][nt][2 + c] = fast_exp2(s[k][nt][2 + c] - e1);
+          sum0 += s[k][nt][c];
+          sum1 += s[k][nt][2 + c];
+        }
+    }
+    l0 = l0 * c0 + sum0;
+    l1 = l1 * c1 + sum1;
+    m0 = nm0;
+    m1 = nm1;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      o[nt][0] *= c0; o[nt][1] *= c0; o[nt][2] *= c1; o[nt][3] *= c1;
+    }
+#pragma unroll
+    for (int k = 0; k < DG_STEP; ++k) {
+      if (k >= n) break;
+      uint32_t pa[4];
+      pa[0] = pack2(s[k][0][0], s[k][0][1]);
+      pa[1] = pack2(s[k][0][2], s[k][0][3]);
+      pa[2] = pack2(s[k][1][0], s[k][1][1]);
+      pa[3] = pack2(s[k][1][2], s[k][1][3]);
+#pragma unroll
+      for (int dp = 0; dp < 2; ++dp) {
+        // four 8x8 tiles: keys 0-7 / 8-15 x dims dp*16 + 0-7 / 8-15
+        uint32_t vf[4];
+        ldmatrix_x4_trans(vf, swz64(v[k].vt, (lane & 7) + ((lane >> 3) & 1) * 8,
+                                    dp * 2 + (lane >> 4)));
+        mma16816(o[2 * dp], pa, vf[0], vf[1]);
+        mma16816(o[2 * dp + 1], pa, vf[2], vf[3]);
+      }
+    }
+  };
+
+  // 5. the shared prefix, chunk by chunk (the first chunk is already in flight)
+  for (int r0 = 0; r0 < ns; r0 += a.chunk_rows) {
+    if (r0 > 0) {
+      __syncthreads();                 // every warp is done with the previous chunk
+      load_shared(r0);
+      cp_async_commit();
+      cp_async_wait<0>();
+    } else {
+      cp_async_wait<1>();              // the first chunk; the first page round may still land
+    }
+    __syncthreads();
+    const int rows = min(a.chunk_rows, ns - r0);
+    const int units = (rows + DC_UNIT - 1) / DC_UNIT;
+    if (live)
+      for (int u = sub; u < units; u += DG_STEP * DG_TILE_WARPS) {
+        GroupView v[DG_STEP];
+        int n = 0;
+#pragma unroll
+        for (int k = 0; k < DG_STEP; ++k) {
+          const int uu = u + DG_TILE_WARPS * k;
+          if (uu >= units) break;
+          v[k] = {shk + uu * DG_TILE_BYTES, shv + uu * DG_TILE_BYTES, 0, 0xFFFF, 0,
+                  rows - uu * DC_UNIT};
+          n = k + 1;
+        }
+        step(n, v);
+      }
+  }
+
+  // 6. the page/current units, round by round (the first round is in flight)
+  for (int u0 = 0; u0 < total; u0 += a.round_units) {
+    const int nr = min(a.round_units, total - u0);
+    if (u0 > 0) {
+      __syncthreads();                 // every warp is done with the previous round
+      load_round(u0, nr);
+      cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    // this warp's tile's units inside the round
+    const int lo = max(u0, mt == 0 ? 0 : n0), hi = min(u0 + nr, mt == 0 ? n0 : total);
+    if (live)
+      for (int u = lo + sub; u < hi; u += DG_STEP * DG_TILE_WARPS) {
+        GroupView v[DG_STEP];
+        int n = 0;
+#pragma unroll
+        for (int k = 0; k < DG_STEP; ++k) {
+          const int uu = u + DG_TILE_WARPS * k;
+          if (uu >= hi) break;
+          int page, row0, mask, pos0, m;
+          unit_info(uu, page, row0, mask, pos0, m);
+          const unsigned kt = pg + (uu - u0) * 2 * DG_TILE_BYTES;
+          v[k] = {kt, kt + DG_TILE_BYTES, page >= 0 ? 1 : 2, mask, pos0, DC_UNIT};
+          n = k + 1;
+        }
+        step(n, v);
+      }
+  }
+  cp_async_wait<0>();                  // nothing stays in flight past the kernel
+
+  // 7. merge the eight partials of each M tile and write the output
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  {
+    Partial* p0 = part + (mt * DG_TILE_WARPS + sub) * DC_UNIT + g;
+    Partial* p1 = p0 + 8;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int d = nt * 8 + tig * 2;
+      *reinterpret_cast<float2*>(&p0->acc[d]) = make_float2(o[nt][0], o[nt][1]);
+      *reinterpret_cast<float2*>(&p1->acc[d]) = make_float2(o[nt][2], o[nt][3]);
+    }
+    if (tig == 0) {
+      p0->m = m0; p0->l = l0;
+      p1->m = m1; p1->l = l1;
+    }
+  }
+  __syncthreads();
+  {
+    const int bb = tid >> 4, d0 = (tid & 15) * 2;   // beam of the CTA, 2 dims
+    const int m = bb >> 4, row = bb & 15;
+    const Partial* pp = part + m * DG_TILE_WARPS * DC_UNIT + row;
+    float M = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < DG_TILE_WARPS; ++s) M = fmaxf(M, pp[s * DC_UNIT].m);
+    const float Me = M == -INFINITY ? 0.f : M;
+    float L = 0.f, O0 = 0.f, O1 = 0.f;
+#pragma unroll
+    for (int s = 0; s < DG_TILE_WARPS; ++s) {
+      const Partial& p = pp[s * DC_UNIT];
+      const float w = fast_exp2(p.m - Me);
+      const float2 acc = *reinterpret_cast<const float2*>(&p.acc[d0]);
+      L += p.l * w;
+      O0 += acc.x * w;
+      O1 += acc.y * w;
+    }
+    const int b = beam0 + bb;
+    if (b < a.B) {
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      *reinterpret_cast<__nv_bfloat162*>(a.out + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + d0) =
+          __floats2bfloat162_rn(O0 * inv, O1 * inv);
+    }
+  }
+}
+
 // ---- host: tensor maps ----------------------------------------------------
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no
 // libcuda link), with a small cache keyed by every encoded field.
@@ -603,15 +1060,15 @@ static bool tile_map(CUtensorMap* out, const void* base, int rank, const uint64_
 
 using namespace grs;
 
-extern "C" int grs_decode_attention_shared(
-    const void* query, int64_t q_sb, int64_t q_sh, const void* key_cache,
-    const void* value_cache, int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
-    const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* lengths,
-    int num_pages, const void* current_key, const void* current_value, int64_t ck_sb,
-    int64_t ck_sh, const uint8_t* current_valid, const void* shared_key,
-    const void* shared_value, int num_shared, void* output, int64_t o_sb, int64_t o_sh,
-    int batch, int heads, int page_size, int32_t* status, void* stream) {
-  if (batch <= 0) return GRS_OK;
+// shape and alignment rules shared by both shared-prefix decode kernels
+static int check_shared_decode(const void* query, int64_t q_sb, int64_t q_sh,
+                               const void* key_cache, const void* value_cache, int64_t kc_sp,
+                               int64_t kc_st, int64_t kc_sh, int max_blocks, int num_pages,
+                               const void* current_key, const void* current_value,
+                               int64_t ck_sb, int64_t ck_sh, const uint8_t* current_valid,
+                               const void* shared_key, const void* shared_value, int num_shared,
+                               void* output, int64_t o_sb, int64_t o_sh, int heads,
+                               int page_size) {
   if (heads <= 0 || heads > DC_CONSUMERS || heads % 2 || page_size <= 0 || page_size % DC_UNIT ||
       num_shared < 0 || num_pages <= 0 || max_blocks <= 0 || max_blocks > DC_MAX_COLS)
     return GRS_ERR_SHAPE;
@@ -631,7 +1088,64 @@ extern "C" int grs_decode_attention_shared(
   if (current_key && (((uintptr_t)current_key | (uintptr_t)current_value) & 15 || ck_sb % 8))
     return GRS_ERR_SHAPE;
   if (((uintptr_t)output & 3) || (o_sb | o_sh) % 2) return GRS_ERR_SHAPE;
+  return GRS_OK;
+}
 
+extern "C" int grs_decode_attention_shared(
+    const void* query, int64_t q_sb, int64_t q_sh, const void* key_cache,
+    const void* value_cache, int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
+    const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* lengths,
+    int num_pages, const void* current_key, const void* current_value, int64_t ck_sb,
+    int64_t ck_sh, const uint8_t* current_valid, const void* shared_key,
+    const void* shared_value, int num_shared, void* output, int64_t o_sb, int64_t o_sh,
+    int batch, int heads, int page_size, int32_t* status, void* stream) {
+  if (batch <= 0) return GRS_OK;
+  if (int rc = check_shared_decode(query, q_sb, q_sh, key_cache, value_cache, kc_sp, kc_st,
+                                   kc_sh, max_blocks, num_pages, current_key, current_value,
+                                   ck_sb, ck_sh, current_valid, shared_key, shared_value,
+                                   num_shared, output, o_sb, o_sh, heads, page_size))
+    return rc;
+  GroupArgs a{(const __nv_bfloat16*)query, q_sb, q_sh, (const __nv_bfloat16*)key_cache,
+              (const __nv_bfloat16*)value_cache, kc_sp, kc_st, kc_sh, block_table, bt_stride,
+              max_blocks, lengths, num_pages, (const __nv_bfloat16*)current_key,
+              (const __nv_bfloat16*)current_value, ck_sb, ck_sh, current_valid,
+              (const __nv_bfloat16*)shared_key, (const __nv_bfloat16*)shared_value, num_shared,
+              (__nv_bfloat16*)output, o_sb, o_sh, batch, heads, page_size,
+              1.4426950408889634f / sqrtf(32.f), 0, DG_ROUND_UNITS};
+  a.chunk_rows = num_shared > 0
+                     ? min(DG_MAX_CHUNK_ROWS, (num_shared + DC_UNIT - 1) / DC_UNIT * DC_UNIT)
+                     : 0;
+  const size_t smem = (size_t)a.chunk_rows * 128 + (size_t)a.round_units * 2 * DG_TILE_BYTES +
+                      DG_MERGE_BYTES;
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(decode_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         DG_MAX_CHUNK_ROWS * 128 + DG_ROUND_UNITS * 2 * DG_TILE_BYTES +
+                             DG_MERGE_BYTES);
+    attr[dev] = true;
+  }
+  const dim3 grid((batch + DG_BEAMS - 1) / DG_BEAMS, heads);
+  decode_group_kernel<<<grid, DG_THREADS, smem, grs::counted((cudaStream_t)stream)>>>(a);
+  GRS_CUDA_CHECK_LAUNCH();
+  return GRS_OK;
+}
+
+extern "C" int grs_decode_attention_shared_cluster(
+    const void* query, int64_t q_sb, int64_t q_sh, const void* key_cache,
+    const void* value_cache, int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
+    const int32_t* block_table, int64_t bt_stride, int max_blocks, const int32_t* lengths,
+    int num_pages, const void* current_key, const void* current_value, int64_t ck_sb,
+    int64_t ck_sh, const uint8_t* current_valid, const void* shared_key,
+    const void* shared_value, int num_shared, void* output, int64_t o_sb, int64_t o_sh,
+    int batch, int heads, int page_size, int32_t* status, void* stream) {
+  if (batch <= 0) return GRS_OK;
+  if (int rc = check_shared_decode(query, q_sb, q_sh, key_cache, value_cache, kc_sp, kc_st,
+                                   kc_sh, max_blocks, num_pages, current_key, current_value,
+                                   ck_sb, ck_sh, current_valid, shared_key, shared_value,
+                                   num_shared, output, o_sb, o_sh, heads, page_size))
+    return rc;
   // a key row of H*32 elements as H/2 chunks of 64 (128 bytes)
   const uint64_t chunks = (uint64_t)heads / 2;
   CUtensorMap tm_kc, tm_vc, tm_sk, tm_sv, tm_ck, tm_cv;

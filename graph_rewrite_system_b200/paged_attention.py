@@ -13,8 +13,8 @@ int32) receives in-kernel errors of the decode kernels (default: a
 per-device word read by ``check_decode_status``).
 
 bf16 one-query decode runs on ``grs_decode_causal`` (page-staged, one CTA per
-beam) or, with a shared prefix, ``grs_decode_attention_shared`` (8-CTA
-clusters); other shapes and fp32 on ``grs_paged_attention``.
+beam) or, with a shared prefix, ``grs_decode_attention_shared`` (one CTA
+per 32 beams and head); other shapes and fp32 on ``grs_paged_attention``.
 """
 from __future__ import annotations
 
@@ -144,7 +144,7 @@ def paged_attention(
             status_word.data_ptr(), _lib.stream_of(query))
         if code == 0:
             return output
-        # only a layout the cluster kernel does not take (nothing launched)
+        # only a layout the grouped kernel does not take (nothing launched)
         # goes on to the general kernel; a failed launch raises
         if code != _lib.GRS_ERR_SHAPE:
             _lib.check(code, "shared-prefix decode attention")

@@ -94,16 +94,16 @@ GRS_API int grs_decode_causal(const void* query, int64_t q_sb, int64_t q_sh,
 
 /* Shared-prefix decode (bf16, head width 32, one query, heads <= 8): the
  * same semantics as grs_paged_attention with query_len 1 (token order:
- * shared prefix, pages, current token), in one launch of 8-CTA clusters of
- * 16 beams.  Each cluster reads every distinct page of its beams once;
- * shared and page keys are split across the cluster and the partials are
- * combined through distributed shared memory.  block_table rows hold
- * max_blocks (<= 32) entries.  Requires 16-byte aligned query, cache,
- * current and shared tensors, heads adjacent in the cache and current rows
- * (head stride 32) and strides that are multiples of 8 elements; returns
- * GRS_ERR_SHAPE otherwise (the caller then uses grs_paged_attention).
- * `status` (device int32, may be null) receives GRS_ERR_TIMEOUT if an
- * in-kernel wait gives up; it is left untouched otherwise. */
+ * shared prefix, pages, current token).  One CTA per 32 consecutive beams
+ * and head holds every key those beams see: the head's slice of the shared
+ * prefix (staged once per CTA), each distinct page of each 16-beam tile
+ * (deduplicated per block-table column) and the current tokens, so no
+ * partial leaves the CTA.  block_table rows hold max_blocks (<= 32)
+ * entries.  Requires 16-byte aligned query, cache, current and shared
+ * tensors, heads adjacent in the cache and current rows (head stride 32)
+ * and strides that are multiples of 8 elements; returns GRS_ERR_SHAPE
+ * otherwise (the caller then uses grs_paged_attention).  The kernel has no
+ * in-kernel waits and leaves `status` untouched. */
 GRS_API int grs_decode_attention_shared(const void* query, int64_t q_sb, int64_t q_sh,
                                         const void* key_cache, const void* value_cache,
                                         int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
@@ -115,6 +115,25 @@ GRS_API int grs_decode_attention_shared(const void* query, int64_t q_sb, int64_t
                                         const void* shared_value, int num_shared, void* output,
                                         int64_t o_sb, int64_t o_sh, int batch, int heads,
                                         int page_size, int32_t* status, void* stream);
+
+/* The same decode in one launch of 8-CTA clusters of 16 beams (the earlier
+ * design, kept for comparison): each cluster reads every distinct page of
+ * its beams once, shared and page keys are split across the cluster and the
+ * partials are combined through distributed shared memory.  Same arguments
+ * and shape rules as grs_decode_attention_shared.  `status` (device int32,
+ * may be null) receives GRS_ERR_TIMEOUT if an in-kernel wait gives up; it is
+ * left untouched otherwise. */
+GRS_API int grs_decode_attention_shared_cluster(const void* query, int64_t q_sb, int64_t q_sh,
+                                                const void* key_cache, const void* value_cache,
+                                                int64_t kc_sp, int64_t kc_st, int64_t kc_sh,
+                                                const int32_t* block_table, int64_t bt_stride,
+                                                int max_blocks, const int32_t* lengths, int num_pages,
+                                                const void* current_key, const void* current_value,
+                                                int64_t ck_sb, int64_t ck_sh,
+                                                const uint8_t* current_valid, const void* shared_key,
+                                                const void* shared_value, int num_shared, void* output,
+                                                int64_t o_sb, int64_t o_sh, int batch, int heads,
+                                                int page_size, int32_t* status, void* stream);
 
 /* ---- PagedKVCache device state: paged_cache.py:16-105 -------------------
  * refcounts int32 [capacity], free_list int32 [capacity] with its length in

@@ -127,9 +127,11 @@ def test_partial_current_triple_rejected(cuda_device):
 
 
 @pytest.mark.parametrize("batch,shared,current", [(37, 381, False), (16, 381, True),
-                                                  (5, 17, True), (48, 0, False)])
-def test_cluster_decode_shared_prefix(cuda_device, batch, shared, current):
-    """The 8-CTA cluster decode (shared prefix split across the cluster) vs the oracle."""
+                                                  (5, 17, True), (48, 0, False),
+                                                  (40, 700, True)])
+def test_shared_decode_shared_prefix(cuda_device, batch, shared, current):
+    """The shared-prefix decode vs the oracle (700 shared keys: two staged
+    chunks of the prefix per CTA)."""
     from graph_rewrite_system_b200.paged_attention import check_decode_status
 
     out, exp = _random_case(7 + batch, batch, 8, 32, 16, 200, 1, 64, torch.bfloat16, cuda_device,
@@ -141,10 +143,12 @@ def test_cluster_decode_shared_prefix(cuda_device, batch, shared, current):
 @pytest.mark.parametrize("batch,heads,cap,max_len,page", [(40, 6, 6, 64, 16), (33, 8, 3, 96, 32),
                                                           (24, 5, 9, 61, 16), (70, 8, 400, 64, 16),
                                                           (33, 8, 3, 50, 8), (16, 4, 12, 17, 4)])
-def test_cluster_decode_shared_pages(cuda_device, batch, heads, cap, max_len, page):
+def test_shared_decode_shared_pages(cuda_device, batch, heads, cap, max_len, page):
     """Heavily shared pages (small arenas) exercise the per-column page dedup
-    of the cluster decode; ragged lengths, odd head counts, pages of 32 rows
-    and partial clusters included (page sizes 8 and 4 take the rows kernel)."""
+    of the shared-prefix decode; ragged lengths, odd head counts (the general
+    kernel), pages of 32 rows, partial beam groups and near-private pages (a
+    400-page arena: several staging rounds per CTA) included (page sizes 8
+    and 4 take the rows kernel)."""
     from graph_rewrite_system_b200.paged_attention import check_decode_status
 
     out, exp = _random_case(100 + batch, batch, heads, 32, page, cap, 1, max_len, torch.bfloat16,
@@ -153,7 +157,7 @@ def test_cluster_decode_shared_pages(cuda_device, batch, heads, cap, max_len, pa
     check_decode_status(cuda_device)
 
 
-def test_cluster_decode_prefix_tree(cuda_device):
+def test_shared_decode_prefix_tree(cuda_device):
     """The decode microbenchmark's own prefix-tree tables at a small size."""
     from graph_rewrite_system_b200.paged_attention import paged_attention
     from graph_rewrite_system_b200.workloads import decode_attention_workload
@@ -168,30 +172,45 @@ def test_cluster_decode_prefix_tree(cuda_device):
     np.testing.assert_allclose(got.float().cpu().numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
 
 
-def test_cluster_decode_takes_the_cluster_kernel(cuda_device):
-    """The decode workload's layout is accepted by the cluster kernel itself
-    (a non-zero return would mean the rows-kernel fallback ran instead)."""
+@pytest.mark.parametrize("entry", ["grs_decode_attention_shared",
+                                   "grs_decode_attention_shared_cluster"])
+@pytest.mark.parametrize("beams,current", [(40, False), (512, True)])
+def test_shared_decode_entry_points(cuda_device, entry, beams, current):
+    """Both shared-prefix decode kernels, called through the C ABI on the
+    decode microbenchmark's prefix-tree layout, accept it (a non-zero return
+    would mean the rows-kernel fallback) and match the oracle."""
     from graph_rewrite_system_b200 import _lib
     from graph_rewrite_system_b200.paged_attention import check_decode_status
     from graph_rewrite_system_b200.workloads import decode_attention_workload
 
-    w = decode_attention_workload(cuda_device, beams=40, num_shared=381, seed=9)
+    w = decode_attention_workload(cuda_device, beams=beams, num_shared=381, seed=9 + beams)
     out = torch.empty_like(w.query)
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
     q, kc = w.query, w.key_cache
-    rc = _lib.lib().grs_decode_attention_shared(
+    g = torch.Generator().manual_seed(beams)
+    ck = cv = valid = None
+    if current:
+        ck = torch.randn(beams, q.shape[1], 32, generator=g).to(cuda_device, q.dtype)
+        cv = torch.randn(beams, q.shape[1], 32, generator=g).to(cuda_device, q.dtype)
+        valid = (torch.rand(beams, generator=g) > 0.3).to(cuda_device)
+    rc = getattr(_lib.lib(), entry)(
         q.data_ptr(), q.stride(0), q.stride(1), kc.data_ptr(), w.value_cache.data_ptr(),
         kc.stride(0), kc.stride(1), kc.stride(2), w.block_table.data_ptr(),
         w.block_table.stride(0), w.block_table.shape[1], w.lengths.data_ptr(), kc.shape[0],
-        None, None, 0, 0, None, w.shared_key.data_ptr(), w.shared_value.data_ptr(),
-        w.shared_key.shape[0], out.data_ptr(), out.stride(0), out.stride(1), q.shape[0],
-        q.shape[1], kc.shape[1], status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        _lib.ptr(ck), _lib.ptr(cv), ck.stride(0) if current else 0,
+        ck.stride(1) if current else 0, _lib.ptr(valid), w.shared_key.data_ptr(),
+        w.shared_value.data_ptr(), w.shared_key.shape[0], out.data_ptr(), out.stride(0),
+        out.stride(1), q.shape[0], q.shape[1], kc.shape[1], status.data_ptr(),
+        torch.cuda.current_stream().cuda_stream)
     assert rc == 0
     assert int(status.item()) == 0
     f = lambda t: t.float().cpu()
+    kw = {}
+    if current:
+        kw = dict(current_key=f(ck), current_value=f(cv), current_valid=valid.cpu())
     exp = oracle.paged_attention(f(w.query), f(w.key_cache), f(w.value_cache),
                                  w.block_table.cpu(), w.lengths.cpu(), shared_key=f(w.shared_key),
-                                 shared_value=f(w.shared_value))
+                                 shared_value=f(w.shared_value), **kw)
     np.testing.assert_allclose(out.float().cpu().numpy(), exp.numpy(), rtol=2e-2, atol=2e-2)
     check_decode_status(cuda_device)
 
